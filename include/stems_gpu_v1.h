@@ -1,0 +1,191 @@
+/* stems_gpu_v1.h -- C ABI of the B200 spectral front/back end of stems.cpp.
+ *
+ * This library replaces the host-side spectral path of stems.cpp's separators with CUDA
+ * kernels for sm_100a. It sits under the reference's unchanged outer contract
+ * (src/libstems_v1.h: stems_get_api(1)->separate) and behind the internal seam
+ * Separator::separate(const float* mix, int len, const SeparateOptions&)
+ * (src/separator.h:53), where each architecture's separate() runs
+ *
+ *     chunk scheduler -> STFT -> [network] -> mask / unpack -> iSTFT -> overlap-add
+ *
+ * The network is out of scope: a caller-supplied mask buffer stands in for its output, in
+ * exactly the layout the reference's network produces (see each plan's mask layout).
+ *
+ * Conventions (same as libstems_v1.h):
+ *   - every function returns a stg_status; the codes are stems_status_v1's (0 = OK);
+ *   - audio is planar float: samples[channel * n_samples + sample];
+ *   - results are planar [source][channel][sample];
+ *   - an engine is bound to one CUDA device and is not reentrant (one per host thread);
+ *   - "d_" pointers are device memory owned by the caller, "h_" pointers host memory;
+ *     `stream` is a cudaStream_t (NULL = the legacy default stream);
+ *   - size-tagged structs: zero them, set .size = sizeof(struct), fill the fields.
+ */
+#ifndef STEMS_GPU_V1_H
+#define STEMS_GPU_V1_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#  define STG_API __attribute__((visibility("default")))
+#else
+#  define STG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t stg_status;
+enum {
+    STG_OK               = 0,   /* STEMS_STATUS_OK_V1 */
+    STG_INVALID_ARGUMENT = 1,   /* STEMS_STATUS_INVALID_ARGUMENT_V1 */
+    STG_UNSUPPORTED      = 2,   /* a configuration the kernels do not implement */
+    STG_CANCELLED        = 3,   /* STEMS_STATUS_CANCELLED_V1 */
+    STG_MODEL_ERROR      = 4,   /* STEMS_STATUS_MODEL_ERROR_V1: inconsistent model configuration */
+    STG_IO_ERROR         = 5,
+    STG_OUT_OF_MEMORY    = 6,   /* STEMS_STATUS_OUT_OF_MEMORY_V1 */
+    STG_INTERNAL_ERROR   = 7    /* STEMS_STATUS_INTERNAL_ERROR_V1: CUDA errors and the rest */
+};
+
+typedef struct stg_engine stg_engine;
+typedef struct stg_plan stg_plan;
+
+/* ---- library and engine ------------------------------------------------------------------ */
+
+/* Version string, like libstems' runtime_version (src/libstems.cpp:16, 39). */
+STG_API const char* stg_version(void);
+
+/* Number of CUDA devices visible, or a negative value when the CUDA runtime fails. */
+STG_API int stg_device_count(void);
+
+/* One engine per device and host thread. Replaces the per-model backend handle that
+ * HTDemucs/RoFormer/TFCTDF::Impl hold (src/htdemucs.cpp:309, src/roformer.cpp:65,
+ * src/tfc_tdf.cpp:75) for the spectral path. */
+STG_API stg_status stg_engine_create(int device, stg_engine** out_engine);
+STG_API void stg_engine_destroy(stg_engine* engine);
+/* The message of the engine's last failure ("" after success). Borrowed. */
+STG_API const char* stg_engine_last_error(const stg_engine* engine);
+
+/* ---- model configurations (the GGUF metadata the reference reads) ------------------------ */
+
+/* HTDemucs (src/htdemucs.cpp:478-500; n_fft 4096 and hop 1024 are fixed, :35-36). */
+typedef struct {
+    uint32_t size;
+    int32_t n_channels;      /* stems.audio_channels (2) */
+    int32_t n_sources;       /* len(stems.sources) (4 or 6) */
+    int32_t segment;         /* segment_samples() = seg_num * sr / seg_den (343980) */
+    float overlap;           /* SeparateOptions.overlap; < 0 = 0.25 */
+} stg_htdemucs_config;
+
+/* Mel-Band / BS-RoFormer (src/roformer.cpp:360-412). */
+typedef struct {
+    uint32_t size;
+    int32_t n_channels;      /* 2 */
+    int32_t n_stems;         /* the model's own stems */
+    int32_t n_fft;           /* roformer.stft_n_fft (2048) */
+    int32_t hop;             /* roformer.stft_hop_length (441) */
+    int32_t normalized;      /* roformer.stft_normalized */
+    int32_t zero_dc;         /* roformer.zero_dc */
+    int32_t chunk;           /* roformer.chunk_size (352800) */
+    int32_t num_overlap;     /* roformer.num_overlap */
+    float overlap;           /* SeparateOptions.overlap; < 0 = chunk / num_overlap */
+    int32_t n_bands;
+    const int32_t* band_sizes;   /* roformer.band_sizes [n_bands] */
+    const int32_t* band_freqs;   /* roformer.band_freqs [sum band_sizes] */
+    int32_t complement;      /* stems.complement present: append mix - first stem */
+} stg_roformer_config;
+
+/* TFC-TDF / MDX (src/tfc_tdf.cpp:498-553). */
+typedef struct {
+    uint32_t size;
+    int32_t n_stems;
+    int32_t n_fft;           /* tfc_tdf.n_fft (7680 for Kim_Vocal_2) */
+    int32_t hop;             /* tfc_tdf.hop */
+    int32_t dim_f;           /* tfc_tdf.dim_f */
+    int32_t dim_t;           /* tfc_tdf.dim_t */
+    int32_t zero_bins;       /* tfc_tdf.zero_bins (uvr_mdx) */
+    int32_t chunking;        /* 0 = "uvr_mdx", 1 = "msst" (tfc_tdf.chunking) */
+    int32_t num_overlap;     /* tfc_tdf.num_overlap (msst) */
+    float overlap;           /* SeparateOptions.overlap; < 0 = the model default */
+    float compensate;        /* tfc_tdf.compensate */
+    int32_t complement;      /* stems.complement present: append mix - sum of stems */
+} stg_tfc_config;
+
+/* ---- plans: one model configuration and one track length ---------------------------------- */
+
+/* Build the chunk schedule and every table of one separation. Replaces the set-up half of
+ * HTDemucs::separate (src/htdemucs.cpp:534-583), RoFormer::Impl::demix (src/roformer.cpp:
+ * 286-316) and TFCTDF::Impl::demix_uvr / demix_msst (src/tfc_tdf.cpp:398-410, 434-460).
+ * Fails with STG_INVALID_ARGUMENT for the inputs the reference rejects (empty input,
+ * overlap >= 1, reflect pads longer than the signal) and STG_UNSUPPORTED for an n_fft the
+ * kernels do not implement (2048 and 4096; 7680 for TFC-TDF). */
+STG_API stg_status stg_plan_htdemucs(stg_engine* engine, const stg_htdemucs_config* config,
+                                     int64_t n_samples, stg_plan** out_plan);
+STG_API stg_status stg_plan_roformer(stg_engine* engine, const stg_roformer_config* config,
+                                     int64_t n_samples, stg_plan** out_plan);
+STG_API stg_status stg_plan_tfc(stg_engine* engine, const stg_tfc_config* config,
+                                int64_t n_samples, stg_plan** out_plan);
+STG_API void stg_plan_destroy(stg_plan* plan);
+
+typedef struct {
+    uint32_t size;
+    int32_t arch;                  /* 0 RoFormer, 1 HTDemucs, 2 TFC-TDF */
+    int64_t n_samples;             /* per channel, in and out */
+    int32_t n_channels;
+    int32_t n_out_sources;         /* stems in the result, complement included */
+    int64_t n_chunks;              /* segments (HTDemucs) or chunks: the reference's passes */
+    int64_t n_frames;              /* STFT frames per chunk */
+    int64_t mask_floats_per_chunk; /* the stand-in network output of one chunk */
+    int64_t out_floats;            /* n_out_sources * n_channels * n_samples */
+    int64_t scratch_bytes;         /* device scratch the plan holds */
+} stg_plan_info;
+STG_API stg_status stg_plan_get_info(const stg_plan* plan, stg_plan_info* info);
+
+/* Layout of one chunk's mask (the network output the plan consumes):
+ *   HTDemucs  [S][2C][F = 2048][T] float: plane 2c = real, 2c+1 = imaginary part of a
+ *             complex multiplier of the CaC spectrogram (the network's `ox`,
+ *             src/htdemucs.cpp:450-452 and 463-469, with ox = Z * M);
+ *   RoFormer  [S][sum_b din_b * T] float, band-major: band b is a [T][din_b] block,
+ *             din_b = size_b * C * 2, entry (j*C + c)*2 + {re, im}: the network's per-band
+ *             masks (src/roformer.cpp:251-269);
+ *   TFC-TDF   [4S][dim_f][T] float: a real multiplier of the CaC input (the network's
+ *             output y = in * mask, src/tfc_tdf.cpp:377-387).
+ * Chunks follow each other. */
+
+/* Run the whole separation on device buffers: d_mix [C][n], d_mask [n_chunks][mask per
+ * chunk], d_out [n_out_sources][C][n]. Asynchronous on `stream`. Replaces the scheduler
+ * loops and the spectral glue of HTDemucs::separate (src/htdemucs.cpp:589-606, with
+ * Impl::run :419-475), RoFormer::Impl::demix (src/roformer.cpp:317-350, with Impl::run
+ * :217-283) and TFCTDF demix_uvr / demix_msst (src/tfc_tdf.cpp:411-428, 461-494, with
+ * run_chunk :362-391), plus the complement and compensation epilogues
+ * (src/roformer.cpp:481-485, src/tfc_tdf.cpp:586-596). d_mask must be 16-byte aligned. */
+STG_API stg_status stg_separate(stg_plan* plan, const float* d_mix, const float* d_mask,
+                                float* d_out, void* stream);
+
+/* The same on host buffers: copies the mix and the masks in, runs, copies the result out,
+ * and returns when the result is in h_out. This is the end-to-end call a host such as
+ * libstems' separate (src/libstems.cpp:135-219) makes. */
+STG_API stg_status stg_separate_host(stg_plan* plan, const float* h_mix, const float* h_mask,
+                                     float* h_out, void* stream);
+
+/* Progress and cancellation between chunk batches, like SeparateOptions.progress /
+ * should_cancel (src/separator.h:28-31): on_progress(user, done, total) after each batch,
+ * should_cancel(user) before each batch (non-zero abandons the job with STG_CANCELLED). */
+typedef void (*stg_progress_fn)(void* user, int32_t done, int32_t total);
+typedef int32_t (*stg_cancel_fn)(void* user);
+typedef struct {
+    uint32_t size;
+    int32_t chunks_per_batch;      /* <= 0: everything in one batch */
+    stg_progress_fn on_progress;
+    stg_cancel_fn should_cancel;
+    void* user;
+} stg_run_options;
+STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
+                                   float* d_out, void* stream, const stg_run_options* options);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STEMS_GPU_V1_H */

@@ -1,0 +1,924 @@
+/* oracle.c -- CPU restatement of stems.cpp's spectral path. TEST INFRASTRUCTURE ONLY.
+ * See oracle.h for what this is and who may call it. All citations are paths inside the
+ * reference project (betweentwomidnights/stems.cpp). */
+#define _GNU_SOURCE
+#include "oracle.h"
+
+#include <complex.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef double complex cplx;
+
+#define ERR_ARG (-1)
+#define ERR_MEM (-2)
+#define ERR_PAD (-3)
+
+/* ===================================================================================== */
+/* radix-2 FFT: src/stft.h:19-55                                                           */
+/* ===================================================================================== */
+typedef struct { int n; int* rev; cplx* tw; } fft_plan;
+static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
+static fft_plan* g_fft[31];
+
+static const fft_plan* fft_plan_for(int n) {
+    if (n < 2 || (n & (n - 1))) return NULL;               /* stft.h:22 */
+    int bits = 0;
+    while ((1 << bits) < n) bits++;
+    pthread_mutex_lock(&g_mu);
+    if (!g_fft[bits]) {
+        fft_plan* p = (fft_plan*)calloc(1, sizeof(fft_plan));
+        p->n = n;
+        p->rev = (int*)malloc(sizeof(int) * n);
+        p->tw = (cplx*)malloc(sizeof(cplx) * (n / 2));
+        for (int i = 0; i < n; i++) {                       /* stft.h:25-29 */
+            int r = 0;
+            for (int b = 0; b < bits; b++) r |= ((i >> b) & 1) << (bits - 1 - b);
+            p->rev[i] = r;
+        }
+        for (int i = 0; i < n / 2; i++) {                   /* stft.h:30, std::polar(1, th) */
+            const double th = -2.0 * M_PI * i / n;
+            p->tw[i] = cos(th) + I * sin(th);
+        }
+        g_fft[bits] = p;
+    }
+    pthread_mutex_unlock(&g_mu);
+    return g_fft[bits];
+}
+
+/* In place, unnormalised; inverse uses conjugate twiddles (stft.h:35-49). */
+static void fft_run(const fft_plan* p, cplx* a, int inverse) {
+    const int n = p->n;
+    for (int i = 0; i < n; i++)
+        if (i < p->rev[i]) { cplx t = a[i]; a[i] = a[p->rev[i]]; a[p->rev[i]] = t; }
+    for (int len = 2; len <= n; len <<= 1) {
+        const int step = n / len, h = len / 2;
+        for (int i = 0; i < n; i += len)
+            for (int j = 0; j < h; j++) {
+                cplx w = p->tw[j * step];
+                if (inverse) w = conj(w);
+                const cplx u = a[i + j], v = a[i + j + h] * w;
+                a[i + j] = u + v;
+                a[i + j + h] = u - v;
+            }
+    }
+}
+
+int or_fft(int n, double* a, int inverse) {
+    const fft_plan* p = fft_plan_for(n);
+    if (!p || !a) return ERR_ARG;
+    fft_run(p, (cplx*)a, inverse);
+    return 0;
+}
+
+/* ===================================================================================== */
+/* Bluestein FFT for any n: src/vr_dsp.h:11-37                                             */
+/* ===================================================================================== */
+typedef struct { int n, m; const fft_plan* fft; cplx* chirp; cplx* kernel; } blue_plan;
+static blue_plan* g_blue[16];
+
+static const blue_plan* blue_plan_for(int n) {
+    if (n < 1) return NULL;
+    pthread_mutex_lock(&g_mu);
+    blue_plan* found = NULL;
+    int slot = -1;
+    for (int i = 0; i < 16; i++) {
+        if (g_blue[i] && g_blue[i]->n == n) { found = g_blue[i]; break; }
+        if (!g_blue[i] && slot < 0) slot = i;
+    }
+    pthread_mutex_unlock(&g_mu);
+    if (found) return found;
+    if (slot < 0) return NULL;
+    int m = 1;
+    while (m < 2 * n - 1) m *= 2;                           /* vr_dsp.h:16 */
+    const fft_plan* f = fft_plan_for(m);
+    blue_plan* p = (blue_plan*)calloc(1, sizeof(blue_plan));
+    p->n = n; p->m = m; p->fft = f;
+    p->chirp = (cplx*)calloc((size_t)n, sizeof(cplx));
+    p->kernel = (cplx*)calloc((size_t)m, sizeof(cplx));
+    for (int i = 0; i < n; i++) {                           /* vr_dsp.h:18-22 */
+        const double th = -M_PI * (double)i * i / n;
+        p->chirp[i] = cos(th) + I * sin(th);
+        p->kernel[i] = conj(p->chirp[i]);
+        if (i) p->kernel[m - i] = p->kernel[i];
+    }
+    fft_run(f, p->kernel, 0);                               /* vr_dsp.h:23 */
+    pthread_mutex_lock(&g_mu);
+    for (int i = 0; i < 16; i++)
+        if (g_blue[i] && g_blue[i]->n == n) { found = g_blue[i]; break; }
+    if (!found) { g_blue[slot] = p; found = p; }
+    pthread_mutex_unlock(&g_mu);
+    return found;
+}
+
+static void blue_run(const blue_plan* p, cplx* x, int inverse) {   /* vr_dsp.h:26-36 */
+    const int n = p->n, m = p->m;
+    cplx* a = (cplx*)calloc((size_t)m, sizeof(cplx));
+    for (int i = 0; i < n; i++) a[i] = (inverse ? conj(x[i]) : x[i]) * p->chirp[i];
+    fft_run(p->fft, a, 0);
+    for (int i = 0; i < m; i++) a[i] *= p->kernel[i];
+    fft_run(p->fft, a, 1);
+    for (int i = 0; i < n; i++) {
+        const cplx v = a[i] * p->chirp[i] / (double)m;
+        x[i] = inverse ? conj(v) : v;
+    }
+    free(a);
+}
+
+int or_vrfft(int n, double* a, int inverse) {
+    const blue_plan* p = blue_plan_for(n);
+    if (!p || !a) return ERR_ARG;
+    blue_run(p, (cplx*)a, inverse);
+    return 0;
+}
+
+/* The transform torch_stft/istft is given: st::FFT for powers of two, st::VRFFT otherwise
+ * (src/tfc_tdf.cpp:551-552). */
+static int dft(int n, cplx* a, int inverse) {
+    if (n >= 2 && !(n & (n - 1))) { fft_run(fft_plan_for(n), a, inverse); return 0; }
+    const blue_plan* p = blue_plan_for(n);
+    if (!p) return ERR_ARG;
+    blue_run(p, a, inverse);
+    return 0;
+}
+
+/* ===================================================================================== */
+/* reflect pad, Hann, STFT / iSTFT: src/stft.h:57-197                                      */
+/* ===================================================================================== */
+static double* reflect_pad(const float* x, int n, int left, int right) {  /* stft.h:58-68 */
+    if (n <= left || n <= right) return NULL;
+    const size_t sz = (size_t)n + left + right;
+    double* y = (double*)malloc(sizeof(double) * sz);
+    for (int i = 0; i < (int)sz; i++) {
+        int j = i - left;
+        if (j < 0) j = -j;
+        if (j >= n) j = 2 * (n - 1) - j;
+        y[i] = x[j];
+    }
+    return y;
+}
+
+static double* hann_periodic(int n) {                                    /* stft.h:70-74 */
+    double* w = (double*)malloc(sizeof(double) * n);
+    for (int i = 0; i < n; i++) w[i] = 0.5 - 0.5 * cos(2.0 * M_PI * i / n);
+    return w;
+}
+
+int or_torch_stft(int nfft, const float* x, int len, int hop, int normalized, double* outd,
+                  int* n_frames) {                                       /* stft.h:146-164 */
+    if (nfft < 2 || hop < 1 || !x || !outd || len < 1) return ERR_ARG;
+    const int F = nfft / 2 + 1;
+    double* xp = reflect_pad(x, len, nfft / 2, nfft / 2);
+    if (!xp) return ERR_PAD;
+    double* win = hann_periodic(nfft);
+    const double norm = normalized ? 1.0 / sqrt((double)nfft) : 1.0;
+    const int T = len / hop + 1;
+    if (n_frames) *n_frames = T;
+    cplx* out = (cplx*)outd;
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    int rc = 0;
+    for (int t = 0; t < T && !rc; t++) {
+        const size_t start = (size_t)t * hop;
+        for (int i = 0; i < nfft; i++) buf[i] = xp[start + i] * win[i];
+        rc = dft(nfft, buf, 0);
+        for (int f = 0; f < F; f++) out[(size_t)f * T + t] = buf[f] * norm;
+    }
+    free(buf); free(win); free(xp);
+    return rc;
+}
+
+int or_torch_istft(int nfft, const double* specd, int n_frames, int hop, int normalized,
+                   float* out) {                                         /* stft.h:167-197 */
+    if (nfft < 2 || hop < 1 || n_frames < 1 || !specd || !out) return ERR_ARG;
+    const cplx* spec = (const cplx*)specd;
+    const int F = nfft / 2 + 1;
+    double* win = hann_periodic(nfft);
+    const size_t full = (size_t)nfft + (size_t)hop * (n_frames - 1);
+    double* y = (double*)calloc(full, sizeof(double));
+    double* env = (double*)calloc(full, sizeof(double));
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    const double norm = (normalized ? sqrt((double)nfft) : 1.0) / nfft;
+    int rc = 0;
+    for (int t = 0; t < n_frames && !rc; t++) {
+        buf[0] = creal(spec[t]);                     /* c2r ignores the DC and Nyquist imag */
+        for (int f = 1; f < F - 1; f++) {
+            buf[f] = spec[(size_t)f * n_frames + t];
+            buf[nfft - f] = conj(buf[f]);
+        }
+        buf[F - 1] = creal(spec[(size_t)(F - 1) * n_frames + t]);
+        rc = dft(nfft, buf, 1);
+        const size_t off = (size_t)t * hop;
+        for (int i = 0; i < nfft; i++) {
+            y[off + i] += creal(buf[i]) * norm * win[i];
+            env[off + i] += win[i] * win[i];
+        }
+    }
+    const int length = hop * (n_frames - 1);
+    for (int i = 0; i < length; i++) {
+        const size_t j = (size_t)nfft / 2 + i;
+        out[i] = env[j] > 1e-11 ? (float)(y[j] / env[j]) : 0.0f;
+    }
+    free(buf); free(env); free(y); free(win);
+    return rc;
+}
+
+int or_htdemucs_spec(int nfft, const float* x, int len, double* outd, int* n_frames) {
+    /* stft.h:79-103 */
+    if (nfft < 8 || (nfft & (nfft - 1)) || !x || !outd || len < 1) return ERR_ARG;
+    const int hl = nfft / 4;
+    const int le = (len + hl - 1) / hl;
+    const int pad = hl / 2 * 3;
+    double* p = reflect_pad(x, len, pad, pad + le * hl - len);
+    if (!p) return ERR_PAD;
+    const int nxf = len + pad + pad + le * hl - len;
+    float* xf = (float*)malloc(sizeof(float) * nxf);
+    for (int i = 0; i < nxf; i++) xf[i] = (float)p[i];
+    free(p);
+    double* xp = reflect_pad(xf, nxf, nfft / 2, nfft / 2);
+    free(xf);
+    if (!xp) return ERR_PAD;
+    double* win = hann_periodic(nfft);
+    const double norm = 1.0 / sqrt((double)nfft);
+    const int F = nfft / 2;
+    if (n_frames) *n_frames = le;
+    cplx* out = (cplx*)outd;
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    for (int t = 0; t < le; t++) {
+        const size_t start = (size_t)(t + 2) * hl;          /* skip the first two frames */
+        for (int i = 0; i < nfft; i++) buf[i] = xp[start + i] * win[i];
+        fft_run(fft_plan_for(nfft), buf, 0);
+        for (int f = 0; f < F; f++) out[(size_t)f * le + t] = buf[f] * norm;
+    }
+    free(buf); free(win); free(xp);
+    return 0;
+}
+
+int or_htdemucs_ispec(int nfft, const double* specd, int n_frames, int length, float* out) {
+    /* stft.h:106-140 */
+    if (nfft < 8 || (nfft & (nfft - 1)) || !specd || !out || n_frames < 1 || length < 0)
+        return ERR_ARG;
+    const cplx* spec = (const cplx*)specd;
+    const int hl = nfft / 4, F = nfft / 2;
+    const int pad = hl / 2 * 3;
+    const int le_out = hl * ((length + hl - 1) / hl) + 2 * pad;
+    const int frames = n_frames + 4;
+    double* win = hann_periodic(nfft);
+    const size_t full = (size_t)nfft + (size_t)hl * (frames - 1);
+    double* y = (double*)calloc(full, sizeof(double));
+    double* env = (double*)calloc(full, sizeof(double));
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    const double norm = sqrt((double)nfft) / nfft;
+    for (int t = 0; t < frames; t++) {
+        const int st = t - 2;
+        const size_t off = (size_t)t * hl;
+        if (st >= 0 && st < n_frames) {
+            buf[0] = creal(spec[st]);
+            for (int f = 1; f < F; f++) {
+                buf[f] = spec[(size_t)f * n_frames + st];
+                buf[nfft - f] = conj(buf[f]);
+            }
+            buf[F] = 0.0;
+            fft_run(fft_plan_for(nfft), buf, 1);
+            for (int i = 0; i < nfft; i++) y[off + i] += creal(buf[i]) * norm * win[i];
+        }
+        for (int i = 0; i < nfft; i++) env[off + i] += win[i] * win[i];
+    }
+    for (int i = 0; i < length; i++) {
+        const size_t j = (size_t)nfft / 2 + pad + i;
+        if ((int)(j - nfft / 2) >= le_out || j >= full) { out[i] = 0.0f; continue; }
+        out[i] = env[j] > 1e-11 ? (float)(y[j] / env[j]) : 0.0f;
+    }
+    free(buf); free(env); free(y); free(win);
+    return 0;
+}
+
+/* ===================================================================================== */
+/* primitive table: the restatement above, or the reference's own compiled code            */
+/* ===================================================================================== */
+typedef int (*stft_fn)(int, const float*, int, int, int, double*, int*);
+typedef int (*istft_fn)(int, const double*, int, int, int, float*);
+typedef int (*hspec_fn)(int, const float*, int, double*, int*);
+typedef int (*hispec_fn)(int, const double*, int, int, float*);
+static struct { stft_fn stft; istft_fn istft; hspec_fn hspec; hispec_fn hispec; void* so; } g_dsp = {
+    or_torch_stft, or_torch_istft, or_htdemucs_spec, or_htdemucs_ispec, NULL};
+
+int or_use_reference(const char* path) {
+    if (!path) {
+        g_dsp.stft = or_torch_stft; g_dsp.istft = or_torch_istft;
+        g_dsp.hspec = or_htdemucs_spec; g_dsp.hispec = or_htdemucs_ispec;
+        return 0;
+    }
+    void* so = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    if (!so) return ERR_ARG;
+    stft_fn a = (stft_fn)dlsym(so, "ref_torch_stft");
+    istft_fn b = (istft_fn)dlsym(so, "ref_torch_istft");
+    hspec_fn c = (hspec_fn)dlsym(so, "ref_htdemucs_spec");
+    hispec_fn d = (hispec_fn)dlsym(so, "ref_htdemucs_ispec");
+    if (!a || !b || !c || !d) { dlclose(so); return ERR_ARG; }
+    g_dsp.stft = a; g_dsp.istft = b; g_dsp.hspec = c; g_dsp.hispec = d; g_dsp.so = so;
+    return 0;
+}
+
+int or_using_reference(void) { return g_dsp.stft != or_torch_stft; }
+
+/* ===================================================================================== */
+/* a tiny parallel-for over chunk indices (the per-chunk work is independent; the          */
+/* accumulation afterwards runs in chunk order, exactly as the reference's serial loop)    */
+/* ===================================================================================== */
+typedef struct {
+    int (*fn)(void* ctx, int i);
+    void* ctx;
+    int first, end;
+    int next;
+    int rc;
+    pthread_mutex_t mu;
+} pfor_t;
+
+static void* pfor_worker(void* arg) {
+    pfor_t* pf = (pfor_t*)arg;
+    for (;;) {
+        pthread_mutex_lock(&pf->mu);
+        const int i = pf->next++;
+        const int stop = pf->rc != 0;
+        pthread_mutex_unlock(&pf->mu);
+        if (i >= pf->end || stop) break;
+        const int rc = pf->fn(pf->ctx, i);
+        if (rc) { pthread_mutex_lock(&pf->mu); if (!pf->rc) pf->rc = rc; pthread_mutex_unlock(&pf->mu); }
+    }
+    return NULL;
+}
+
+static int parallel_for(int first, int end, int threads, int (*fn)(void*, int), void* ctx) {
+    if (threads <= 1 || end - first <= 1) {
+        for (int i = first; i < end; i++) { const int rc = fn(ctx, i); if (rc) return rc; }
+        return 0;
+    }
+    pfor_t pf = {fn, ctx, first, end, first, 0, PTHREAD_MUTEX_INITIALIZER};
+    if (threads > end - first) threads = end - first;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * threads);
+    for (int k = 0; k < threads; k++) pthread_create(&th[k], NULL, pfor_worker, &pf);
+    for (int k = 0; k < threads; k++) pthread_join(th[k], NULL);
+    free(th);
+    return pf.rc;
+}
+
+static void sample_window(int n, int first, int count, int* lo, int* hi) {
+    *lo = 0; *hi = n;
+    if (count > 0) {
+        *lo = first < 0 ? 0 : (first > n ? n : first);
+        *hi = *lo + count > n ? n : *lo + count;
+    }
+}
+
+/* ===================================================================================== */
+/* HTDemucs: Impl::run spectral part (htdemucs.cpp:419-475) + separate (534-644)           */
+/* ===================================================================================== */
+enum { HT_NFFT = 4096, HT_HOP = 1024 };   /* htdemucs.cpp:35-36 */
+
+int or_ht_n_frames(const or_ht_params* p) { return (p->segment + HT_HOP - 1) / HT_HOP; }  /* :320 */
+
+static int ht_stride(const or_ht_params* p) {                            /* htdemucs.cpp:563-564 */
+    const double overlap = p->overlap < 0.0f ? 0.25 : (double)p->overlap;
+    return (int)((1.0 - overlap) * p->segment);
+}
+
+int or_ht_n_segments(const or_ht_params* p, int len) {
+    const int stride = ht_stride(p);
+    if (stride <= 0 || len <= 0) return 0;
+    return (len + stride - 1) / stride;                                   /* :576 */
+}
+
+static double mean_of(const float* x, size_t n) {                        /* htdemucs.cpp:293-297 */
+    double s = 0;
+    for (size_t i = 0; i < n; i++) s += x[i];
+    return s / n;
+}
+static double std_of(const float* x, size_t n, double mean) {            /* :298-302 */
+    double s = 0;
+    for (size_t i = 0; i < n; i++) { const double d = x[i] - mean; s += d * d; }
+    return sqrt(s / (n - 1));
+}
+
+typedef struct {
+    const or_ht_params* p;
+    const float* mix;      /* normalised mix [C][len] */
+    int len, stride, seg, T;
+    const float* mask;
+    float* seg_out;        /* [G][S][C][seg] */
+} ht_job;
+
+/* One segment: padded view (htdemucs.cpp:552-561, 594-595) -> run (419-475) with the
+ * network replaced by ox = Z * M (complex, per stem and channel). */
+static int ht_segment(void* vctx, int g) {
+    ht_job* J = (ht_job*)vctx;
+    const or_ht_params* p = J->p;
+    const int C = p->n_channels, S = p->n_sources, L = J->seg, T = J->T, F = HT_NFFT / 2;
+    const int off = g * J->stride;
+    const int length = J->len - off < L ? J->len - off : L;
+    const int start = off - (L - length) / 2;
+    float* seg_in = (float*)calloc((size_t)C * L, sizeof(float));
+    for (int c = 0; c < C; c++)
+        for (int i = 0; i < L; i++) {
+            const int j = start + i;
+            if (j >= 0 && j < J->len) seg_in[(size_t)c * L + i] = J->mix[(size_t)c * J->len + j];
+        }
+    const size_t FT = (size_t)F * T;
+    float* mag = (float*)malloc(sizeof(float) * 2 * C * FT);
+    cplx* z = (cplx*)malloc(sizeof(cplx) * FT);
+    int rc = 0;
+    for (int c = 0; c < C && !rc; c++) {
+        int frames = 0;
+        rc = g_dsp.hspec(HT_NFFT, seg_in + (size_t)c * L, L, (double*)z, &frames);
+        if (!rc && frames != T) rc = ERR_ARG;
+        for (size_t i = 0; i < FT && !rc; i++) {
+            mag[(size_t)(2 * c) * FT + i] = (float)creal(z[i]);
+            mag[(size_t)(2 * c + 1) * FT + i] = (float)cimag(z[i]);
+        }
+    }
+    double mean = 0.0, sd = 1.0;
+    if (!rc && p->cac_norm) {                                             /* :434-436 */
+        mean = mean_of(mag, 2 * C * FT);
+        sd = std_of(mag, 2 * C * FT, mean);
+        for (size_t i = 0; i < 2 * C * FT; i++) mag[i] = (float)((mag[i] - mean) / (1e-5 + sd));
+    }
+    cplx* spec = z;
+    float* y = (float*)malloc(sizeof(float) * L);
+    const float* M = J->mask + (size_t)g * S * 2 * C * FT;
+    for (int s = 0; s < S && !rc; s++)
+        for (int c = 0; c < C && !rc; c++) {
+            const float* zr = mag + (size_t)(2 * c) * FT;
+            const float* zi = mag + (size_t)(2 * c + 1) * FT;
+            const float* mr = M + (size_t)(s * 2 * C + 2 * c) * FT;
+            const float* mi = M + (size_t)(s * 2 * C + 2 * c + 1) * FT;
+            for (size_t i = 0; i < FT; i++) {
+                /* stand-in network output, a float tensor like ox (htdemucs.cpp:450-452) */
+                const float re = (float)((double)zr[i] * mr[i] - (double)zi[i] * mi[i]);
+                const float im = (float)((double)zr[i] * mi[i] + (double)zi[i] * mr[i]);
+                spec[i] = p->cac_norm ? (re * sd + mean) + I * (im * sd + mean)   /* :469 */
+                                      : (double)re + I * (double)im;
+            }
+            rc = g_dsp.hispec(HT_NFFT, (const double*)spec, T, L, y);     /* :470 */
+            float* o = J->seg_out + (((size_t)g * S + s) * C + c) * L;
+            memcpy(o, y, sizeof(float) * L);                              /* time branch dropped */
+        }
+    free(y); free(z); free(mag); free(seg_in);
+    return rc;
+}
+
+int or_ht_separate(const or_ht_params* p, const float* mix_in, int len, const float* mask,
+                   float* est) {
+    if (!p || !mix_in || !mask || !est || len <= 0 || p->n_channels < 1 || p->n_sources < 1 ||
+        p->segment < 4 * HT_HOP)
+        return ERR_ARG;
+    const int S = p->n_sources, C = p->n_channels, seg = p->segment;
+    const int stride = ht_stride(p);
+    if (stride <= 0) return ERR_ARG;
+    /* mono-mix normalisation (htdemucs.cpp:539-549), optional here */
+    float* mix = (float*)malloc(sizeof(float) * C * len);
+    double ref_mean = 0.0, ref_std = 1.0;
+    if (p->mono_norm) {
+        float* mono = (float*)malloc(sizeof(float) * len);
+        for (int i = 0; i < len; i++) {
+            double s = 0;
+            for (int c = 0; c < C; c++) s += mix_in[(size_t)c * len + i];
+            mono[i] = (float)(s / C);
+        }
+        ref_mean = mean_of(mono, len);
+        ref_std = std_of(mono, len, ref_mean);
+        if (ref_std < 1e-8) ref_std = 1e-8;
+        for (size_t i = 0; i < (size_t)C * len; i++) mix[i] = (float)((mix_in[i] - ref_mean) / ref_std);
+        free(mono);
+    } else {
+        memcpy(mix, mix_in, sizeof(float) * C * len);
+    }
+    /* triangular weight (htdemucs.cpp:566-573) */
+    float* weight = (float*)malloc(sizeof(float) * seg);
+    {
+        const int half = seg / 2;
+        for (int i = 0; i < half; i++) weight[i] = (float)(i + 1);
+        for (int i = half; i < seg; i++) weight[i] = (float)(seg - i);
+        float mx = weight[0];
+        for (int i = 1; i < seg; i++) if (weight[i] > mx) mx = weight[i];
+        for (int i = 0; i < seg; i++) weight[i] /= mx;
+    }
+    const int G = or_ht_n_segments(p, len);
+    int lo, hi;
+    sample_window(G, p->sample_first, p->sample_count, &lo, &hi);
+    ht_job J = {p, mix, len, stride, seg, or_ht_n_frames(p), mask, NULL};
+    J.seg_out = (float*)malloc(sizeof(float) * (size_t)G * S * C * seg);
+    if (!J.seg_out) { free(weight); free(mix); return ERR_MEM; }
+    int rc = parallel_for(lo, hi, p->threads, ht_segment, &J);
+    /* split(): weighted overlap-add, centre trim, divide by the summed weight (:589-606) */
+    float* sum_w = (float*)calloc((size_t)len, sizeof(float));
+    memset(est, 0, sizeof(float) * (size_t)S * C * len);
+    for (int g = lo; g < hi && !rc; g++) {
+        const int off = g * stride;
+        const int length = len - off < seg ? len - off : seg;
+        const int trim = (seg - length) / 2;
+        for (int sc = 0; sc < S * C; sc++) {
+            const float* so = J.seg_out + ((size_t)g * S * C + sc) * seg;
+            for (int i = 0; i < length; i++)
+                est[(size_t)sc * len + off + i] += weight[i] * so[trim + i];
+        }
+        for (int i = 0; i < length; i++) sum_w[off + i] += weight[i];
+    }
+    for (int sc = 0; sc < S * C && !rc; sc++)
+        for (int i = 0; i < len; i++) est[(size_t)sc * len + i] /= sum_w[i];
+    /* one model, weight 1: v / 1 * ref_std + ref_mean (:629-642) */
+    if (p->mono_norm && !rc)
+        for (size_t i = 0; i < (size_t)S * C * len; i++) est[i] = (float)(est[i] * ref_std + ref_mean);
+    free(sum_w); free(J.seg_out); free(weight); free(mix);
+    return rc;
+}
+
+/* ===================================================================================== */
+/* RoFormer: Impl::run (roformer.cpp:217-283), demix (286-351), separate (436-486)         */
+/* ===================================================================================== */
+static int rf_check(const or_rf_params* p) {
+    if (!p || p->n_channels < 1 || p->n_stems < 1 || p->n_fft < 2 || p->hop < 1 ||
+        p->chunk < 1 || p->step < 1 || p->chunk % p->hop || p->n_bands < 1 || !p->band_sizes ||
+        !p->band_freqs)
+        return ERR_ARG;
+    const int F = p->n_fft / 2 + 1;
+    size_t nf = 0;
+    for (int b = 0; b < p->n_bands; b++) nf += p->band_sizes[b];
+    for (size_t k = 0; k < nf; k++)
+        if (p->band_freqs[k] < 0 || p->band_freqs[k] >= F) return ERR_ARG;  /* :408-411 */
+    return 0;
+}
+
+int or_rf_n_chunks(const or_rf_params* p, int len) {                    /* roformer.cpp:353-357 */
+    const int border = p->chunk - p->step;
+    const int Lp = (len > 2 * border && border > 0) ? len + 2 * border : len;
+    return (Lp + p->step - 1) / p->step;
+}
+
+int or_rf_band_gather(const or_rf_params* p, const double* zd, int T, float* feat) {
+    /* roformer.cpp:226-241: 'b (f s) t c' by the band lists, then 'b f t c -> b t (f c)' */
+    if (rf_check(p) || !zd || !feat) return ERR_ARG;
+    const cplx* z = (const cplx*)zd;
+    const int C = p->n_channels, F = p->n_fft / 2 + 1;
+    size_t foff = 0, off = 0;
+    for (int b = 0; b < p->n_bands; b++) {
+        const int din = p->band_sizes[b] * C * 2;
+        float* blk = feat + off * T;
+        for (int j = 0; j < p->band_sizes[b]; j++) {
+            const int f = p->band_freqs[foff + j];
+            for (int c = 0; c < C; c++)
+                for (int t = 0; t < T; t++) {
+                    const cplx v = z[((size_t)c * F + f) * T + t];
+                    float* q = &blk[(size_t)t * din + (j * C + c) * 2];
+                    q[0] = (float)creal(v);
+                    q[1] = (float)cimag(v);
+                }
+        }
+        foff += p->band_sizes[b];
+        off += din;
+    }
+    return 0;
+}
+
+typedef struct {
+    const or_rf_params* p;
+    const float* x;       /* padded mix [C][Lp] */
+    int Lp;
+    const float* mask;
+    size_t mask_per_chunk;
+    float* y;             /* [G][S][C][chunk] */
+    const int* bpf;       /* bands_per_freq [F] */
+} rf_job;
+
+static int rf_chunk(void* vctx, int g) {
+    rf_job* J = (rf_job*)vctx;
+    const or_rf_params* p = J->p;
+    const int C = p->n_channels, S = p->n_stems, Cc = p->chunk, F = p->n_fft / 2 + 1;
+    const int T = Cc / p->hop + 1;                                        /* :83 */
+    const int i0 = g * p->step;
+    const int length = J->Lp - i0 < Cc ? J->Lp - i0 : Cc;
+    /* chunk copy with the short-tail rule (roformer.cpp:318-331) */
+    float* part = (float*)calloc((size_t)C * Cc, sizeof(float));
+    int rc = 0;
+    for (int c = 0; c < C && !rc; c++) {
+        const float* src = &J->x[(size_t)c * J->Lp + i0];
+        float* dst = &part[(size_t)c * Cc];
+        memcpy(dst, src, sizeof(float) * length);
+        if (length < Cc) {
+            if (length > Cc / 2 + 1) {
+                double* q = reflect_pad(src, length, 0, Cc - length);
+                if (!q) { rc = ERR_PAD; break; }
+                for (int k = 0; k < Cc; k++) dst[k] = (float)q[k];
+                free(q);
+            }
+        }
+    }
+    const size_t FT = (size_t)F * T;
+    cplx* z = (cplx*)malloc(sizeof(cplx) * C * FT);
+    for (int c = 0; c < C && !rc; c++) {                                  /* :220-224 */
+        int frames = 0;
+        rc = g_dsp.stft(p->n_fft, part + (size_t)c * Cc, Cc, p->hop, p->normalized,
+                        (double*)(z + (size_t)c * FT), &frames);
+        if (!rc && frames != T) rc = ERR_ARG;
+    }
+    /* masks averaged where bands overlap, applied, inverted (:251-282) */
+    cplx* acc = (cplx*)malloc(sizeof(cplx) * C * FT);
+    cplx* spec = (cplx*)malloc(sizeof(cplx) * FT);
+    float* yt = (float*)malloc(sizeof(float) * ((size_t)p->hop * (T - 1)));
+    for (int s = 0; s < S && !rc; s++) {
+        memset(acc, 0, sizeof(cplx) * C * FT);
+        const float* m = J->mask + (size_t)g * J->mask_per_chunk + (size_t)s * (J->mask_per_chunk / S);
+        size_t foff = 0, off = 0;
+        for (int b = 0; b < p->n_bands; b++) {
+            const int din = p->band_sizes[b] * C * 2;
+            const float* mb = m + off * T;
+            for (int j = 0; j < p->band_sizes[b]; j++) {
+                const int f = p->band_freqs[foff + j];
+                for (int c = 0; c < C; c++)
+                    for (int t = 0; t < T; t++) {
+                        const float* q = &mb[(size_t)t * din + (j * C + c) * 2];
+                        acc[((size_t)c * F + f) * T + t] += q[0] + I * (double)q[1];
+                    }
+            }
+            foff += p->band_sizes[b];
+            off += din;
+        }
+        for (int c = 0; c < C && !rc; c++) {
+            for (int f = 0; f < F; f++) {
+                const double denom = J->bpf[f] > 1 ? J->bpf[f] : 1;
+                for (int t = 0; t < T; t++) {
+                    const size_t i = (size_t)f * T + t;
+                    spec[i] = z[(size_t)c * FT + i] * (acc[(size_t)c * FT + i] / denom);
+                }
+            }
+            if (p->zero_dc) for (int t = 0; t < T; t++) spec[t] = 0.0;        /* :278 */
+            rc = g_dsp.istft(p->n_fft, (const double*)spec, T, p->hop, p->normalized, yt);
+            memcpy(J->y + (((size_t)g * S + s) * C + c) * Cc, yt, sizeof(float) * Cc);  /* :280 */
+        }
+    }
+    free(yt); free(spec); free(acc); free(z); free(part);
+    return rc;
+}
+
+int or_rf_separate(const or_rf_params* p, const float* mix, int len, const float* mask, float* out) {
+    if (rf_check(p) || !mix || !mask || !out || len <= 0) return ERR_ARG;
+    const int C = p->n_channels, S = p->n_stems, Cc = p->chunk, step = p->step, F = p->n_fft / 2 + 1;
+    const int T = Cc / p->hop + 1;
+    const int fade = Cc / 10, border = Cc - step;                         /* :288-291 */
+    const int pad = len > 2 * border && border > 0;
+    const int Lp = pad ? len + 2 * border : len;
+    float* x = (float*)malloc(sizeof(float) * C * Lp);
+    for (int c = 0; c < C; c++) {
+        const float* src = &mix[(size_t)c * len];
+        if (pad) {
+            double* q = reflect_pad(src, len, border, border);
+            if (!q) { free(x); return ERR_PAD; }
+            for (int k = 0; k < Lp; k++) x[(size_t)c * Lp + k] = (float)q[k];
+            free(q);
+        } else {
+            memcpy(&x[(size_t)c * Lp], src, sizeof(float) * len);
+        }
+    }
+    /* torch.linspace(0, 1, fade) from both ends; fade-in and fade-out window (:303-313) */
+    float* fade_in = (float*)calloc((size_t)(fade > 0 ? fade : 1), sizeof(float));
+    float* window = (float*)malloc(sizeof(float) * Cc);
+    for (int i = 0; i < Cc; i++) window[i] = 1.0f;
+    if (fade > 1) {
+        const float stp = 1.0f / (float)(fade - 1);
+        for (int i = 0; i < fade; i++)
+            fade_in[i] = i < fade / 2 ? (float)i * stp : 1.0f - (float)(fade - 1 - i) * stp;
+    }
+    for (int i = 0; i < fade; i++) { window[i] *= fade_in[i]; window[Cc - 1 - i] *= fade_in[i]; }
+    /* bands per frequency (:399-411) and the per-chunk mask size */
+    int* bpf = (int*)calloc((size_t)F, sizeof(int));
+    size_t nf = 0, din_total = 0;
+    for (int b = 0; b < p->n_bands; b++) { nf += p->band_sizes[b]; din_total += (size_t)p->band_sizes[b] * C * 2; }
+    for (size_t k = 0; k < nf; k++) bpf[p->band_freqs[k]]++;
+    const int G = (Lp + step - 1) / step;
+    int lo, hi;
+    sample_window(G, p->sample_first, p->sample_count, &lo, &hi);
+    rf_job J = {p, x, Lp, mask, (size_t)S * din_total * T, NULL, bpf};
+    J.y = (float*)malloc(sizeof(float) * (size_t)G * S * C * Cc);
+    int rc = J.y ? parallel_for(lo, hi, p->threads, rf_chunk, &J) : ERR_MEM;
+    double* result = (double*)calloc((size_t)S * C * Lp, sizeof(double));
+    double* counter = (double*)calloc((size_t)Lp, sizeof(double));
+    float* w = (float*)malloc(sizeof(float) * Cc);
+    for (int g = lo; g < hi && !rc; g++) {                                /* :317-341 */
+        const int i0 = g * step;
+        const int length = Lp - i0 < Cc ? Lp - i0 : Cc;
+        memcpy(w, window, sizeof(float) * Cc);
+        if (i0 == 0) for (int k = 0; k < fade; k++) w[k] = 1.0f;
+        else if (i0 + Cc >= Lp) for (int k = Cc - fade; k < Cc; k++) w[k] = 1.0f;
+        for (int k = 0; k < S * C; k++)
+            for (int t = 0; t < length; t++)
+                result[(size_t)k * Lp + i0 + t] += (double)J.y[((size_t)g * S * C + k) * Cc + t] * w[t];
+        for (int t = 0; t < length; t++) counter[i0 + t] += w[t];
+    }
+    const int off = pad ? border : 0;                                     /* :343-349 */
+    for (int k = 0; k < S * C && !rc; k++)
+        for (int t = 0; t < len; t++) {
+            const double v = result[(size_t)k * Lp + off + t] / counter[off + t];
+            out[(size_t)k * len + t] = isfinite(v) ? (float)v : 0.0f;
+        }
+    if (p->complement && !rc)                                             /* :481-485 */
+        for (size_t i = 0; i < (size_t)C * len; i++) out[(size_t)S * C * len + i] = mix[i] - out[i];
+    free(w); free(counter); free(result); free(J.y); free(bpf); free(window); free(fade_in); free(x);
+    return rc;
+}
+
+/* ===================================================================================== */
+/* TFC-TDF: run_chunk (tfc_tdf.cpp:362-391), demix_uvr (398-429), demix_msst (434-495),    */
+/* separate (570-598)                                                                      */
+/* ===================================================================================== */
+static int tfc_chunk_len(const or_tfc_params* p) { return p->hop * (p->dim_t - 1); }   /* :94 */
+
+static int64_t tfc_step(const or_tfc_params* p) {
+    const int C = tfc_chunk_len(p);
+    if (p->chunking == 0)                                                 /* :403 */
+        return p->overlap < 0 ? C - p->n_fft : (int64_t)((1.0 - (double)p->overlap) * C);
+    if (p->overlap < 0) return C / p->num_overlap;                        /* :437 */
+    const long s = lround(C * (1.0 - p->overlap));
+    return s > 1 ? s : 1;
+}
+
+static int tfc_check(const or_tfc_params* p) {
+    if (!p || p->n_stems < 1 || p->n_fft < 16 || p->hop < 1 || p->dim_f < 1 ||
+        p->dim_f > p->n_fft / 2 + 1 || p->dim_t < 2 || p->zero_bins < 0 || p->zero_bins > p->dim_f ||
+        (p->chunking != 0 && p->chunking != 1) || (p->chunking == 1 && p->num_overlap < 1))
+        return ERR_ARG;
+    if (tfc_chunk_len(p) <= p->n_fft / 2) return ERR_ARG;
+    if (p->chunking == 0 && tfc_chunk_len(p) - p->n_fft <= 0) return ERR_ARG;
+    if (tfc_step(p) <= 0) return ERR_ARG;
+    return 0;
+}
+
+/* Length of the padded signal the chunks walk over, and where the track starts in it. */
+static int64_t tfc_padded(const or_tfc_params* p, int len, int* start) {
+    const int C = tfc_chunk_len(p);
+    if (p->chunking == 0) {
+        const int trim = p->n_fft / 2, gen = C - 2 * trim;                /* :400-402 */
+        *start = trim;
+        return (int64_t)trim + len + gen + trim - len % gen;
+    }
+    const int border = C - (int)tfc_step(p);                              /* :438-440 */
+    const int pad = len > 2 * border && border > 0;
+    *start = pad ? border : 0;
+    return pad ? (int64_t)len + 2 * border : len;
+}
+
+int or_tfc_n_chunks(const or_tfc_params* p, int len) {
+    if (tfc_check(p) || len <= 0) return 0;
+    int start;
+    const int64_t M = tfc_padded(p, len, &start);
+    const int64_t step = tfc_step(p);
+    return (int)((M + step - 1) / step);
+}
+
+typedef struct {
+    const or_tfc_params* p;
+    const float* x;     /* padded [2][M] */
+    int64_t M, step;
+    const float* mask;
+    float* y;           /* [G][S][2][chunk] */
+} tfc_job;
+
+static int tfc_chunk(void* vctx, int g) {
+    tfc_job* J = (tfc_job*)vctx;
+    const or_tfc_params* p = J->p;
+    const int C = tfc_chunk_len(p), S = p->n_stems, Fn = p->n_fft / 2 + 1, dim_f = p->dim_f,
+              dim_t = p->dim_t;
+    const int64_t i0 = (int64_t)g * J->step;
+    const int n = (int)(J->M - i0 < C ? J->M - i0 : C);
+    float* part = (float*)calloc((size_t)2 * C, sizeof(float));
+    int rc = 0;
+    for (int c = 0; c < 2; c++) {
+        const float* src = &J->x[(size_t)c * J->M + i0];
+        float* dst = &part[(size_t)c * C];
+        memcpy(dst, src, sizeof(float) * n);                              /* uvr: zero tail (:413-416) */
+        if (p->chunking == 1 && n < C && n > C / 2) {                     /* msst (:467-474) */
+            double* q = reflect_pad(src, n, 0, C - n);
+            if (!q) { rc = ERR_PAD; break; }
+            for (int k = 0; k < C; k++) dst[k] = (float)q[k];
+            free(q);
+        }
+    }
+    const size_t plane = (size_t)dim_f * dim_t;
+    float* in = (float*)calloc(4 * plane, sizeof(float));
+    cplx* s = (cplx*)malloc(sizeof(cplx) * (size_t)Fn * dim_t);
+    for (int c = 0; c < 2 && !rc; c++) {                                  /* :366-376 */
+        int T = 0;
+        rc = g_dsp.stft(p->n_fft, part + (size_t)c * C, C, p->hop, 0, (double*)s, &T);
+        if (!rc && T != dim_t) rc = ERR_ARG;
+        for (int f = p->zero_bins; f < dim_f && !rc; f++)
+            for (int t = 0; t < T; t++) {
+                const cplx v = s[(size_t)f * T + t];
+                in[(2 * c) * plane + (size_t)f * T + t] = (float)creal(v);
+                in[(2 * c + 1) * plane + (size_t)f * T + t] = (float)cimag(v);
+            }
+    }
+    float* w = (float*)malloc(sizeof(float) * C);
+    const float* m = J->mask + (size_t)g * 4 * S * plane;
+    for (int k = 0; k < S && !rc; k++)                                    /* :381-390 */
+        for (int c = 0; c < 2 && !rc; c++) {
+            const float* mr = m + (size_t)(4 * k + 2 * c) * plane;
+            const float* mi = mr + plane;
+            const float* re = in + (size_t)(2 * c) * plane;
+            const float* im = re + plane;
+            for (size_t i = 0; i < (size_t)Fn * dim_t; i++) s[i] = 0.0;
+            for (size_t i = 0; i < plane; i++) s[i] = (double)(re[i] * mr[i]) + I * (double)(im[i] * mi[i]);
+            rc = g_dsp.istft(p->n_fft, (const double*)s, dim_t, p->hop, 0, w);
+            memcpy(J->y + (((size_t)g * S + k) * 2 + c) * C, w, sizeof(float) * C);
+        }
+    free(w); free(s); free(in); free(part);
+    return rc;
+}
+
+static void np_hanning(int n, double* w) {                                /* tfc_tdf.cpp:65-70 */
+    for (int i = 0; i < n; i++) w[i] = 1.0;
+    if (n > 1) for (int i = 0; i < n; i++) w[i] = 0.5 - 0.5 * cos(2.0 * M_PI * i / (n - 1));
+}
+
+static void torch_linspace(float a, float b, int n, float* v) {           /* tfc_tdf.cpp:55-62 */
+    if (n == 1) v[0] = a;
+    if (n < 2) return;
+    const float step = (b - a) / (float)(n - 1);
+    for (int i = 0; i < n; i++) v[i] = i < n / 2 ? a + step * (float)i : b - step * (float)(n - 1 - i);
+}
+
+int or_tfc_separate(const or_tfc_params* p, const float* mix, int len, const float* mask, float* out) {
+    if (tfc_check(p) || !mix || !mask || !out || len <= 0) return ERR_ARG;
+    for (size_t k = 0; k < (size_t)2 * len; k++) if (!isfinite(mix[k])) return ERR_ARG;   /* :573-574 */
+    const int C = tfc_chunk_len(p), S = p->n_stems;
+    int start = 0;
+    const int64_t M = tfc_padded(p, len, &start);
+    const int64_t step = tfc_step(p);
+    float* x = (float*)calloc((size_t)2 * M, sizeof(float));
+    for (int c = 0; c < 2; c++) {
+        const float* src = mix + (size_t)c * len;
+        if (p->chunking == 0 || start == 0) {
+            memcpy(&x[(size_t)c * M + start], src, sizeof(float) * len);  /* :405-406 */
+        } else {
+            double* q = reflect_pad(src, len, start, start);              /* :442-450 */
+            if (!q) { free(x); return ERR_PAD; }
+            for (int64_t k = 0; k < M; k++) x[(size_t)c * M + k] = (float)q[k];
+            free(q);
+        }
+    }
+    const int G = (int)((M + step - 1) / step);
+    int lo, hi;
+    sample_window(G, p->sample_first, p->sample_count, &lo, &hi);
+    tfc_job J = {p, x, M, step, mask, NULL};
+    J.y = (float*)malloc(sizeof(float) * (size_t)G * S * 2 * C);
+    int rc = J.y ? parallel_for(lo, hi, p->threads, tfc_chunk, &J) : ERR_MEM;
+    double* result = (double*)calloc((size_t)S * 2 * M, sizeof(double));
+    double* divider = (double*)calloc((size_t)M, sizeof(double));
+    double* w = (double*)malloc(sizeof(double) * C);
+    const int fade = C / 10;
+    float* window = (float*)malloc(sizeof(float) * C);
+    if (p->chunking == 1) {                                               /* :451-456 */
+        for (int i = 0; i < C; i++) window[i] = 1.0f;
+        if (fade > 0) {
+            float* a = (float*)malloc(sizeof(float) * fade);
+            torch_linspace(1, 0, fade, a);
+            memcpy(window + C - fade, a, sizeof(float) * fade);
+            torch_linspace(0, 1, fade, a);
+            memcpy(window, a, sizeof(float) * fade);
+            free(a);
+        }
+    }
+    for (int g = lo; g < hi && !rc; g++) {
+        const int64_t i0 = (int64_t)g * step;
+        const int n = (int)(M - i0 < C ? M - i0 : C);
+        if (p->chunking == 0) {                                           /* :419-422 */
+            if (p->overlap == 0) for (int t = 0; t < n; t++) w[t] = 1.0;
+            else np_hanning(n, w);
+        } else {                                                          /* :479-484 */
+            for (int t = 0; t < C; t++) w[t] = window[t];
+            if (i0 == 0) for (int t = 0; t < fade; t++) w[t] = 1.0f;
+            else if (i0 + step >= M) for (int t = C - fade; t < C; t++) w[t] = 1.0f;
+        }
+        for (int k = 0; k < S * 2; k++)
+            for (int t = 0; t < n; t++)
+                result[(size_t)k * M + i0 + t] += (double)J.y[((size_t)g * S * 2 + k) * C + t] * w[t];
+        for (int t = 0; t < n; t++) divider[i0 + t] += w[t];
+    }
+    for (int k = 0; k < S * 2 && !rc; k++)
+        for (int t = 0; t < len; t++) {
+            const double v = result[(size_t)k * M + start + t] / divider[start + t];
+            out[(size_t)k * len + t] = p->chunking == 0 ? (float)v : (isfinite(v) ? (float)v : 0.0f);
+        }
+    if (!rc && p->compensate != 1.0f)                                     /* :586-587 */
+        for (size_t i = 0; i < (size_t)S * 2 * len; i++) out[i] *= p->compensate;
+    if (!rc && p->complement) {                                           /* :588-596 */
+        const size_t n = (size_t)2 * len;
+        float* rest = out + (size_t)S * n;
+        for (size_t i = 0; i < n; i++) {
+            float v = mix[i];
+            for (int k = 0; k < S; k++) v -= out[(size_t)k * n + i];
+            rest[i] = v;
+        }
+    }
+    free(window); free(w); free(divider); free(result); free(J.y); free(x);
+    return rc;
+}

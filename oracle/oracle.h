@@ -1,0 +1,99 @@
+/* oracle.h -- CPU checker for the spectral front/back end of stems.cpp.
+ *
+ * TEST INFRASTRUCTURE ONLY. Nothing in the product links, loads or calls this library:
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference leg
+ * use it, and only as the checker or as the timed CPU baseline.
+ *
+ * It restates, in plain C and double precision, the reference's host path:
+ *   - the DSP primitives of src/stft.h and src/vr_dsp.h (radix-2 FFT, Bluestein FFT,
+ *     reflect pad, periodic Hann, HTDemucs _spec/_ispec, torch.stft/istft);
+ *   - the per-architecture glue and chunk schedulers of src/htdemucs.cpp,
+ *     src/roformer.cpp and src/tfc_tdf.cpp, with the network replaced by a synthetic
+ *     stand-in that multiplies the spectrogram by a caller-supplied mask.
+ * Each function names the reference lines it follows. The primitives can be swapped for
+ * the reference's own compiled stft.h/vr_dsp.h (oracle/_ref/libstems_ref.so, built from the
+ * reference sources by oracle/build_ref.sh) with or_use_reference(), which is how the
+ * restatement is pinned and how the "reference" CPU baseline is timed.
+ *
+ * Complex arrays are interleaved doubles (re, im), i.e. numpy complex128.
+ * Every function returns 0 on success and a negative code on bad arguments.
+ */
+#ifndef STEMS_ORACLE_H
+#define STEMS_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- DSP primitives (src/stft.h, src/vr_dsp.h) ---------------------------------------- */
+int or_fft(int n, double* a, int inverse);                 /* stft.h:19-55, n a power of two */
+int or_vrfft(int n, double* a, int inverse);               /* vr_dsp.h:11-37 (Bluestein) */
+int or_torch_stft(int n_fft, const float* x, int len, int hop, int normalized,
+                  double* out, int* n_frames);             /* stft.h:146-164 */
+int or_torch_istft(int n_fft, const double* spec, int n_frames, int hop, int normalized,
+                   float* out);                            /* stft.h:167-197 */
+int or_htdemucs_spec(int n_fft, const float* x, int len, double* out, int* n_frames);  /* stft.h:79-103 */
+int or_htdemucs_ispec(int n_fft, const double* spec, int n_frames, int length, float* out); /* stft.h:106-140 */
+
+/* Swap the primitives above (as used by the glue below) for the reference's own compiled
+ * code. path = NULL restores the restatement. Returns 0 on success. */
+int or_use_reference(const char* path);
+int or_using_reference(void);
+
+/* ---- glue: HTDemucs (src/htdemucs.cpp:419-475, 534-644) ------------------------------ */
+typedef struct {
+    int n_channels;      /* C */
+    int n_sources;       /* S */
+    int segment;         /* samples per segment (343980 for the published models) */
+    float overlap;       /* < 0: 0.25 */
+    int cac_norm;        /* 1: mean/std normalise the CaC spectrogram around the stand-in */
+    int mono_norm;       /* 1: demucs' mono-mix normalisation around the whole separation */
+    int sample_first;    /* timing only: process segments [first, first+count) */
+    int sample_count;    /* <= 0: all segments */
+    int threads;         /* worker threads for the per-segment work (<= 1: serial) */
+} or_ht_params;
+/* mask: per segment [S][2C][F = n_fft/2][T] float (re plane 2c, im plane 2c+1), segments
+ * back to back. out: [S][C][len]. */
+int or_ht_n_segments(const or_ht_params* p, int len);
+int or_ht_n_frames(const or_ht_params* p);
+int or_ht_separate(const or_ht_params* p, const float* mix, int len, const float* mask, float* out);
+
+/* ---- glue: RoFormer (src/roformer.cpp:217-357, 436-486) ------------------------------ */
+typedef struct {
+    int n_channels, n_stems;
+    int n_fft, hop, normalized, zero_dc;
+    int chunk, step;
+    int n_bands;
+    const int* band_sizes;  /* [n_bands] */
+    const int* band_freqs;  /* [sum band_sizes] */
+    int complement;         /* append mix - est as one more stem */
+    int sample_first, sample_count, threads;
+} or_rf_params;
+/* mask: per chunk [S][sum_b din_b * T] band-major, block b = [T][din_b], din_b = size_b*C*2,
+ * entries (j*C + c)*2 + {re, im}. out: [S(+1)][C][len]. */
+int or_rf_n_chunks(const or_rf_params* p, int len);
+int or_rf_separate(const or_rf_params* p, const float* mix, int len, const float* mask, float* out);
+/* The band gather of one chunk (roformer.cpp:226-241): z [C][F][T] complex -> feat. */
+int or_rf_band_gather(const or_rf_params* p, const double* z, int n_frames, float* feat);
+
+/* ---- glue: TFC-TDF / MDX (src/tfc_tdf.cpp:55-70, 354-495, 570-598) ------------------- */
+typedef struct {
+    int n_stems;
+    int n_fft, hop, dim_f, dim_t, zero_bins;
+    int chunking;           /* 0 = uvr_mdx, 1 = msst */
+    float overlap;          /* < 0: the model default */
+    int num_overlap;        /* msst default step = chunk / num_overlap */
+    float compensate;
+    int complement;
+    int sample_first, sample_count, threads;
+} or_tfc_params;
+/* mask: per chunk real [4S][dim_f][dim_t]; the stand-in network is y = in * mask. */
+int or_tfc_n_chunks(const or_tfc_params* p, int len);
+int or_tfc_separate(const or_tfc_params* p, const float* mix, int len, const float* mask, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

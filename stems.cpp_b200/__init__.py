@@ -1,0 +1,273 @@
+"""stems.cpp_b200 -- the B200 spectral front/back end of stems.cpp, from Python.
+
+A thin ctypes layer over the C ABI in include/stems_gpu_v1.h (libstems_gpu.so, built
+in-tree for sm_100a by build.py). It mirrors the reference's separator interface
+(src/separator.h:19-54): a plan is made for one model configuration and one track length,
+and ``separate`` runs chunking -> STFT -> mask -> iSTFT -> overlap-add on the GPU. The
+network is out of scope; a mask buffer stands in for its output.
+
+There is no CPU fallback: when the library is missing or no B200 is visible, every call
+raises. Device buffers may be torch CUDA tensors (their data_ptr and the current stream are
+used) or raw device pointers.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import bands  # noqa: F401  (band tables for RoFormer configurations)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libstems_gpu.so")
+
+STATUS = {0: "OK", 1: "INVALID_ARGUMENT", 2: "UNSUPPORTED", 3: "CANCELLED", 4: "MODEL_ERROR",
+          5: "IO_ERROR", 6: "OUT_OF_MEMORY", 7: "INTERNAL_ERROR"}
+ARCH_ROFORMER, ARCH_HTDEMUCS, ARCH_TFC = 0, 1, 2
+
+_I32P = C.POINTER(C.c_int32)
+
+
+class StemsError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__(f"{STATUS.get(code, code)}: {message}")
+        self.code = code
+
+
+class Cancelled(StemsError):
+    pass
+
+
+class HTDemucsConfig(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("n_channels", C.c_int32), ("n_sources", C.c_int32),
+                ("segment", C.c_int32), ("overlap", C.c_float)]
+
+
+class RoFormerConfig(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("n_channels", C.c_int32), ("n_stems", C.c_int32),
+                ("n_fft", C.c_int32), ("hop", C.c_int32), ("normalized", C.c_int32),
+                ("zero_dc", C.c_int32), ("chunk", C.c_int32), ("num_overlap", C.c_int32),
+                ("overlap", C.c_float), ("n_bands", C.c_int32), ("band_sizes", _I32P),
+                ("band_freqs", _I32P), ("complement", C.c_int32)]
+
+
+class TFCConfig(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("n_stems", C.c_int32), ("n_fft", C.c_int32),
+                ("hop", C.c_int32), ("dim_f", C.c_int32), ("dim_t", C.c_int32),
+                ("zero_bins", C.c_int32), ("chunking", C.c_int32), ("num_overlap", C.c_int32),
+                ("overlap", C.c_float), ("compensate", C.c_float), ("complement", C.c_int32)]
+
+
+class PlanInfo(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("arch", C.c_int32), ("n_samples", C.c_int64),
+                ("n_channels", C.c_int32), ("n_out_sources", C.c_int32), ("n_chunks", C.c_int64),
+                ("n_frames", C.c_int64), ("mask_floats_per_chunk", C.c_int64),
+                ("out_floats", C.c_int64), ("scratch_bytes", C.c_int64)]
+
+
+PROGRESS_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int32, C.c_int32)
+CANCEL_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p)
+
+
+class RunOptions(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("chunks_per_batch", C.c_int32),
+                ("on_progress", PROGRESS_FN), ("should_cancel", CANCEL_FN), ("user", C.c_void_p)]
+
+
+# Every symbol include/stems_gpu_v1.h declares, with its ctypes signature.
+_SIGNATURES = {
+    "stg_version": (C.c_char_p, []),
+    "stg_device_count": (C.c_int, []),
+    "stg_engine_create": (C.c_int32, [C.c_int, C.POINTER(C.c_void_p)]),
+    "stg_engine_destroy": (None, [C.c_void_p]),
+    "stg_engine_last_error": (C.c_char_p, [C.c_void_p]),
+    "stg_plan_htdemucs": (C.c_int32, [C.c_void_p, C.POINTER(HTDemucsConfig), C.c_int64, C.POINTER(C.c_void_p)]),
+    "stg_plan_roformer": (C.c_int32, [C.c_void_p, C.POINTER(RoFormerConfig), C.c_int64, C.POINTER(C.c_void_p)]),
+    "stg_plan_tfc": (C.c_int32, [C.c_void_p, C.POINTER(TFCConfig), C.c_int64, C.POINTER(C.c_void_p)]),
+    "stg_plan_destroy": (None, [C.c_void_p]),
+    "stg_plan_get_info": (C.c_int32, [C.c_void_p, C.POINTER(PlanInfo)]),
+    "stg_separate": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.POINTER(RunOptions)]),
+}
+
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def lib():
+    """The loaded C library. Raises when it has not been built (no silent fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise StemsError(7, f"{LIB_PATH} is missing: run __graft_entry__.build() first")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def version() -> str:
+    return lib().stg_version().decode()
+
+
+def device_count() -> int:
+    return lib().stg_device_count()
+
+
+def _ptr(x):
+    """Device pointer of a torch tensor (checked contiguous, float32, CUDA) or an int."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        if not x.is_cuda:
+            raise StemsError(1, "expected a CUDA tensor")
+        if not x.is_contiguous():
+            raise StemsError(1, "expected a contiguous tensor")
+        return x.data_ptr()
+    raise TypeError(f"cannot take a device pointer of {type(x)}")
+
+
+def _stream_of(stream, *tensors):
+    if stream is not None:
+        return stream if isinstance(stream, int) else stream.cuda_stream
+    for t in tensors:
+        if hasattr(t, "device") and getattr(t, "is_cuda", False):
+            import torch
+            return torch.cuda.current_stream(t.device).cuda_stream
+    return None
+
+
+class Engine:
+    """One CUDA device (include/stems_gpu_v1.h: stg_engine_create)."""
+
+    def __init__(self, device: int = 0):
+        self._h = C.c_void_p()
+        rc = lib().stg_engine_create(device, C.byref(self._h))
+        if rc != 0:
+            raise StemsError(rc, f"cannot create an engine on device {device}")
+        self.device = device
+
+    def close(self):
+        if self._h:
+            lib().stg_engine_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return lib().stg_engine_last_error(self._h).decode()
+
+    def _check(self, rc, what):
+        if rc != 0:
+            msg = self.last_error()
+            if rc == 3:
+                raise Cancelled(rc, msg or what)
+            raise StemsError(rc, f"{what}: {msg}")
+
+    # -- plans ---------------------------------------------------------------------------
+    def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0):
+        cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap)
+        h = C.c_void_p()
+        self._check(lib().stg_plan_htdemucs(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_htdemucs")
+        return Plan(self, h)
+
+    def plan_roformer(self, n_samples, band_sizes, band_freqs, n_channels=2, n_stems=1, n_fft=2048,
+                      hop=441, normalized=False, zero_dc=False, chunk=352800, num_overlap=2,
+                      overlap=-1.0, complement=False):
+        sizes = np.ascontiguousarray(band_sizes, dtype=np.int32)
+        freqs = np.ascontiguousarray(band_freqs, dtype=np.int32)
+        cfg = RoFormerConfig(C.sizeof(RoFormerConfig), n_channels, n_stems, n_fft, hop, int(normalized),
+                             int(zero_dc), chunk, num_overlap, overlap, sizes.size,
+                             sizes.ctypes.data_as(_I32P), freqs.ctypes.data_as(_I32P), int(complement))
+        h = C.c_void_p()
+        self._check(lib().stg_plan_roformer(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_roformer")
+        return Plan(self, h)
+
+    def plan_tfc(self, n_samples, n_stems=1, n_fft=7680, hop=1024, dim_f=3072, dim_t=256, zero_bins=3,
+                 chunking="uvr_mdx", num_overlap=4, overlap=-1.0, compensate=1.0, complement=False):
+        ch = {"uvr_mdx": 0, "msst": 1}[chunking] if isinstance(chunking, str) else int(chunking)
+        cfg = TFCConfig(C.sizeof(TFCConfig), n_stems, n_fft, hop, dim_f, dim_t, zero_bins, ch, num_overlap,
+                        overlap, compensate, int(complement))
+        h = C.c_void_p()
+        self._check(lib().stg_plan_tfc(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_tfc")
+        return Plan(self, h)
+
+
+class Plan:
+    """A model configuration bound to one track length (stg_plan_*)."""
+
+    def __init__(self, engine: Engine, handle):
+        self.engine = engine
+        self._h = handle
+        info = PlanInfo()
+        info.size = C.sizeof(PlanInfo)
+        engine._check(lib().stg_plan_get_info(self._h, C.byref(info)), "plan_get_info")
+        self.arch = info.arch
+        self.n_samples = info.n_samples
+        self.n_channels = info.n_channels
+        self.n_out_sources = info.n_out_sources
+        self.n_chunks = info.n_chunks
+        self.n_frames = info.n_frames
+        self.mask_floats_per_chunk = info.mask_floats_per_chunk
+        self.mask_floats = info.mask_floats_per_chunk * info.n_chunks
+        self.out_floats = info.out_floats
+        self.scratch_bytes = info.scratch_bytes
+
+    @property
+    def out_shape(self):
+        return (self.n_out_sources, self.n_channels, self.n_samples)
+
+    def close(self):
+        if self._h:
+            lib().stg_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def separate(self, mix, mask, out, stream=None, chunks_per_batch=0, progress=None, should_cancel=None):
+        """Device buffers (torch CUDA tensors or pointers): mix [C][n], mask, out [S][C][n]."""
+        st = _stream_of(stream, mix, mask, out)
+        if progress is None and should_cancel is None and chunks_per_batch <= 0:
+            rc = lib().stg_separate(self._h, _ptr(mix), _ptr(mask), _ptr(out), st)
+        else:
+            opts = RunOptions()
+            opts.size = C.sizeof(RunOptions)
+            opts.chunks_per_batch = chunks_per_batch
+            opts.on_progress = PROGRESS_FN(lambda u, d, t: progress(d, t)) if progress else PROGRESS_FN()
+            opts.should_cancel = (CANCEL_FN(lambda u: int(bool(should_cancel()))) if should_cancel
+                                  else CANCEL_FN())
+            rc = lib().stg_separate_ex(self._h, _ptr(mix), _ptr(mask), _ptr(out), st, C.byref(opts))
+        self.engine._check(rc, "separate")
+        return out
+
+    def separate_host(self, mix, mask, out=None, stream=None):
+        """Host buffers (numpy float32); returns the [S][C][n] result."""
+        mix = np.ascontiguousarray(mix, dtype=np.float32)
+        mask = np.ascontiguousarray(mask, dtype=np.float32)
+        if mix.size != self.n_channels * self.n_samples or mask.size != self.mask_floats:
+            raise StemsError(1, "buffer sizes do not match the plan")
+        if out is None:
+            out = np.empty(self.out_shape, np.float32)
+        st = stream if (stream is None or isinstance(stream, int)) else stream.cuda_stream
+        rc = lib().stg_separate_host(self._h, mix.ctypes.data, mask.ctypes.data, out.ctypes.data, st)
+        self.engine._check(rc, "separate_host")
+        return out

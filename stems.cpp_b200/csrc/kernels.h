@@ -1,0 +1,109 @@
+// kernels.h -- device data structures and kernel launchers of the spectral path.
+//
+// Everything here is plain data: the host scheduler (engine.cu) builds these structs from a
+// model configuration and a track length, and the launchers in kernels.cu run them.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace stg {
+
+enum Arch : int { ARCH_ROFORMER = 0, ARCH_HTDEMUCS = 1, ARCH_TFC = 2 };
+
+// One chunk (RoFormer/TFC-TDF) or segment (HTDemucs) of a track.
+//
+// Input side: chunk-local sample p in [0, Lc) reads the track at src0 + p when p < valid;
+// past valid it reads the mirror 2*(valid-1) - p (tail_reflect) or zero. Track coordinates
+// outside [0, len) are reflected (FusedParams::reflect_global) or read as zero.
+// Output side: the chunk contributes out_len samples starting at global output coordinate
+// out0; sample u of them is the chunk's own output at y_off + u, weighted by W[w_off + u].
+struct ChunkDesc {
+    int64_t src0;
+    int64_t out0;
+    int32_t valid;
+    int32_t tail_reflect;
+    int32_t out_len;
+    int32_t y_off;
+    int32_t w_off;
+    int32_t _pad;
+};
+
+// STFT geometry of one chunk. Frame t covers padded positions [first_pos + t*hop, +n_fft).
+// A padded position q maps to chunk-local sample reflect(q - n_fft/2, Lc) (torch.stft's
+// centre pad), or, for HTDemucs' _spec, reflect(reflect(q - n_fft/2, ht_lxf) - ht_pad, Lc).
+// The chunk's output sample j (iSTFT with window-sum normalisation) sits at q = j + out_offset.
+struct FrameGeom {
+    int n_fft, hop;
+    int Lc;
+    int T;
+    int first_pos;
+    int ht_pad;
+    int ht_lxf;
+    int out_offset;
+    int Lout;
+};
+
+struct FusedParams {
+    const float* mix;          // planar [C][len]
+    int64_t len;
+    int n_channels;            // 1 or 2
+    int reflect_global;
+    const ChunkDesc* chunks;
+    int n_chunks;
+    FrameGeom g;
+    int K;                     // frames per tile
+    int n_tiles;
+    int S;                     // stems
+    const float* win;          // periodic Hann [n_fft]
+    const float2* tw;          // W_N^m, m in [0, n_fft)
+    const float* inv_env;      // [Lout]: 1 / sum of squared windows, 0 where it vanishes
+    float fwd_scale, inv_scale;
+    // mask (the stand-in for the network's output), one block per chunk
+    const float* mask;
+    int64_t mask_chunk_stride;
+    // RoFormer: bin -> (band entry) inverse table, CSR over bins
+    const int* bin_ebeg;       // [F + 1]
+    const int2* bin_ent;       // (offset of the entry in a stem's mask block without t, din_b)
+    const float* bin_inv;      // [F] 1 / max(bands_per_freq, 1)
+    int zero_dc;
+    int64_t stem_stride;       // floats per stem within a chunk's mask block
+    // TFC-TDF
+    int dim_f, zero_bins;
+    // outputs
+    float* Y;                  // [chunk][S*C][Lout]
+    int64_t y_chunk_stride;
+    float* Tr;                 // [chunk][tile][S*C][n_fft - hop]
+    int64_t tr_chunk_stride;
+};
+
+struct CombineParams {
+    const float* Y;
+    int64_t y_chunk_stride;
+    const float* Tr;
+    int64_t tr_chunk_stride;
+    const ChunkDesc* chunks;
+    int n_chunks;
+    int64_t step_out;          // regular chunk step in output coordinates
+    int64_t max_out_len;       // longest out_len of any chunk
+    FrameGeom g;
+    int K, n_tiles;
+    const float* W;            // weight tables
+    int S, C;
+    int64_t len;               // output samples per row
+    int64_t out_shift;         // global output coordinate of output sample 0
+    int mode;                  // ARCH_*
+    int nan_to_zero;
+    float compensate;          // multiplies the stems (1 = off)
+    int complement;            // 1: first stem; 2: all stems (TFC-TDF) subtracted from the mix
+    const float* mix;          // for the complement
+    float* out;                // [S(+1)][C][len]
+};
+
+// Launchers. Return a cudaError_t from the launch (kernel errors surface on sync).
+cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st);
+cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
+size_t fused_smem_bytes(int n_fft);
+int fused_threads(int n_fft);
+bool fused_supported(int n_fft);
+
+} // namespace stg
