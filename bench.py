@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""bench.py -- throughput of the B200 spectral path (chunking -> STFT -> mask -> iSTFT -> OLA).
+
+Metric: audio-seconds per second of the whole separation, whole job over
+all GPUs; plus the fused kernel's achieved HBM bandwidth against the measured peak.
+
+Workload (default ``cfg1``): Mel-Band RoFormer (Kim) front/back
+end on 60 s of seeded stereo 44.1 kHz audio: chunks of 352800 samples, num_overlap 4
+(36 chunks), STFT n_fft 2048 / hop 441 (801 frames, 1025 bins), 60 mel bands (1979
+band-bin entries, duplicates averaged), complex mask N(0, 0.5) in the network's band-major
+layout, iSTFT, windowed overlap-add across chunks. One step = one such track. The mask
+(913 MB) and the mix are resident in HBM before the timed region; they exceed the 126 MB
+L2, so no flush is needed between steps. Other workloads: cfg0, cfg2, cfg3 (see WORKLOADS).
+
+Multi-GPU (torchrun, one process per GPU): every rank separates its own track; there is no
+data-path collective (weak scaling). NCCL is used only for the barrier and the max-over-
+ranks of the device-timed duration.
+
+``--impl reference`` times the reference's CPU implementation of the same path on this
+box's host cores (rank 0 only): the reference's own stft.h compiled from its sources
+(oracle/_ref) under the restated host loops of src/roformer.cpp, with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SR = 44100
+
+WORKLOADS = {
+    "cfg1": dict(arch="roformer", bands="mel", seconds=60, chunk=352800, num_overlap=4, n_fft=2048,
+                 hop=441, zero_dc=False, sigma=0.5, seed=1,
+                 desc="Mel-Band RoFormer (Kim) front/back end, 60 s stereo, chunk 352800, overlap 4"),
+    "cfg2": dict(arch="roformer", bands="bs", seconds=180, chunk=352800, num_overlap=2, n_fft=2048,
+                 hop=441, zero_dc=True, sigma=0.5, seed=2,
+                 desc="BS-RoFormer (viperx 317) front/back end, 180 s stereo, chunk 352800, overlap 2"),
+    "cfg0": dict(arch="htdemucs", seconds=20, segment=343980, sources=4, sigma=1.0, seed=0,
+                 desc="HTDemucs spectral path, 20 s stereo, 4 stems, segments of 7.8 s, 25% overlap"),
+    "cfg3": dict(arch="tfc", seconds=180, n_fft=7680, hop=1024, dim_f=3072, dim_t=256, zero_bins=3,
+                 overlap=0.5, sigma=1.0, seed=3,
+                 desc="MDX TFC-TDF (Kim_Vocal_2) framing, 180 s stereo, n_fft 7680, UVR 50% overlap"),
+}
+
+
+def load_pkg():
+    import __graft_entry__
+    return __graft_entry__.load_package()
+
+
+def synth_audio(seed, length, channels=2):
+    """BASELINE.json's mix: 8 seeded sines (50-8000 Hz, amp 0.05-0.2) + N(0, 0.01) noise, clipped."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(length, dtype=np.float64) / SR
+    out = np.empty((channels, length), np.float32)
+    for c in range(channels):
+        f, a, ph = rng.uniform(50, 8000, 8), rng.uniform(0.05, 0.2, 8), rng.uniform(0, 2 * np.pi, 8)
+        x = np.zeros(length)
+        for k in range(8):
+            x += a[k] * np.sin(2 * np.pi * f[k] * t + ph[k])
+        x += 0.01 * rng.standard_normal(length)
+        out[c] = np.clip(x, -1, 1)
+    return out
+
+
+def make_plan(pkg, eng, w, length):
+    if w["arch"] == "roformer":
+        sizes, freqs = pkg.bands.mel_bands() if w["bands"] == "mel" else pkg.bands.bs_bands()
+        return eng.plan_roformer(length, sizes, freqs, chunk=w["chunk"], num_overlap=w["num_overlap"],
+                                 n_fft=w["n_fft"], hop=w["hop"], zero_dc=w["zero_dc"])
+    if w["arch"] == "htdemucs":
+        return eng.plan_htdemucs(length, n_sources=w["sources"], segment=w["segment"])
+    return eng.plan_tfc(length, n_fft=w["n_fft"], hop=w["hop"], dim_f=w["dim_f"], dim_t=w["dim_t"],
+                        zero_bins=w["zero_bins"], overlap=w["overlap"])
+
+
+def fused_algorithmic_bytes(plan, w):
+    """Bytes the fused kernel must move once: each chunk's audio window in, the masks in, and
+    each chunk's separated output out (4-byte floats)."""
+    if w["arch"] == "roformer":
+        lc = w["chunk"]
+    elif w["arch"] == "htdemucs":
+        lc = w["segment"]
+    else:
+        lc = w["hop"] * (w["dim_t"] - 1)
+    n_src = plan.n_out_sources
+    return 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats
+                + plan.n_chunks * n_src * plan.n_channels * lc)
+
+
+def path_algorithmic_bytes(plan, w):
+    """The survey's per-track figure: audio in per chunk window + masks in + stems out once."""
+    lc = {"roformer": w.get("chunk"), "htdemucs": w.get("segment")}.get(w["arch"]) or w["hop"] * (w["dim_t"] - 1)
+    return 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats + plan.out_floats)
+
+
+# ---- clocks during the timed region (NVML, the source nvidia-smi reads) -----------------------
+class ClockSampler:
+    BAD = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown")
+
+    def __init__(self, device_index, period_s=0.005):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period, self._stop, self._t, self.ok = period_s, threading.Event(), None, False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, b in bits.items():
+                    if r & b:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+    def rejected(self):
+        return any(r in self.reasons for r in self.BAD)
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(workload):
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"fused_kernel_{workload}.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---- CPU baselines -------------------------------------------------------------------------
+def cpu_run(w, length, mix, mask_host, n_sample, threads):
+    """Time the CPU path on a bounded sample of chunks; returns (seconds, chunks timed, kind)."""
+    import oracle
+    kind = "reference" if oracle.use_reference(True) else "port"
+    if w["arch"] == "roformer":
+        pkg = load_pkg()
+        sizes, freqs = pkg.bands.mel_bands() if w["bands"] == "mel" else pkg.bands.bs_bands()
+        p = oracle.rf_params(sizes, freqs, chunk=w["chunk"], num_overlap=w["num_overlap"],
+                             n_fft=w["n_fft"], hop=w["hop"], zero_dc=int(w["zero_dc"]),
+                             sample_first=0, sample_count=n_sample, threads=threads)
+        fn = oracle.rf_separate
+    elif w["arch"] == "htdemucs":
+        p = oracle.ht_params(n_sources=w["sources"], segment=w["segment"], sample_first=0,
+                             sample_count=n_sample, threads=threads)
+        fn = oracle.ht_separate
+    else:
+        p = oracle.tfc_params(n_fft=w["n_fft"], hop=w["hop"], dim_f=w["dim_f"], dim_t=w["dim_t"],
+                              zero_bins=w["zero_bins"], overlap=w["overlap"], sample_first=0,
+                              sample_count=n_sample, threads=threads)
+        fn = oracle.tfc_separate
+    t0 = time.perf_counter()
+    fn(p, mix, mask_host)
+    return time.perf_counter() - t0, kind
+
+
+def run_reference(args, w, rank):
+    if rank != 0:
+        return 0
+    length = w["seconds"] * SR
+    threads = os.cpu_count() or 1
+    mix = synth_audio(w["seed"], length)
+    n_chunks = _n_chunks(w, length)
+    n_sample = max(1, min(n_chunks, threads))
+    mask = _host_mask(w, length, n_chunks)
+    times, kind = [], "port"
+    for k in range(args.warmup + args.steps):
+        dt, kind = cpu_run(w, length, mix, mask, n_sample, threads)
+        if k >= args.warmup:
+            times.append(dt)
+    per_chunk_audio = w["seconds"] / n_chunks
+    value = n_sample * per_chunk_audio / statistics.mean(times)
+    line = {"metric": "audio_seconds_per_second", "value": value, "unit": "audio-s/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.mean(times), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w["desc"], "sample_chunks": n_sample,
+                       "chunks_per_track": n_chunks},
+            "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": threads, "kind": kind,
+                             "sample": f"{n_sample} of {n_chunks} chunks of one {w['seconds']} s track per step"},
+            "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def _n_chunks(w, length):
+    import oracle
+    if w["arch"] == "roformer":
+        pkg = load_pkg()
+        sizes, freqs = pkg.bands.mel_bands() if w["bands"] == "mel" else pkg.bands.bs_bands()
+        return oracle.rf_n_chunks(oracle.rf_params(sizes, freqs, chunk=w["chunk"], num_overlap=w["num_overlap"]), length)
+    if w["arch"] == "htdemucs":
+        return oracle.ht_n_segments(oracle.ht_params(n_sources=w["sources"], segment=w["segment"]), length)
+    return oracle.tfc_n_chunks(oracle.tfc_params(n_fft=w["n_fft"], hop=w["hop"], dim_f=w["dim_f"],
+                                                 dim_t=w["dim_t"], overlap=w["overlap"]), length)
+
+
+def _mask_floats_per_chunk(w):
+    if w["arch"] == "roformer":
+        pkg = load_pkg()
+        sizes, _ = pkg.bands.mel_bands() if w["bands"] == "mel" else pkg.bands.bs_bands()
+        return int(sizes.sum()) * 2 * 2 * (w["chunk"] // w["hop"] + 1)
+    if w["arch"] == "htdemucs":
+        return w["sources"] * 4 * 2048 * ((w["segment"] + 1023) // 1024)
+    return 4 * w["dim_f"] * w["dim_t"]
+
+
+def _host_mask(w, length, n_chunks):
+    rng = np.random.default_rng(w["seed"] + 1000)
+    n = n_chunks * _mask_floats_per_chunk(w)
+    return (w["sigma"] * rng.standard_normal(n, dtype=np.float32)).astype(np.float32)
+
+
+# ---- our arm -----------------------------------------------------------------------------
+def run_ours(args, w, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    pkg = load_pkg()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    eng = pkg.Engine(local_rank)
+    length = w["seconds"] * SR
+    plan = make_plan(pkg, eng, w, length)
+    mix_h = synth_audio(w["seed"] + 7 * rank, length)
+    d_mix = torch.from_numpy(mix_h).to(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    d_mask = torch.randn(plan.mask_floats, generator=gen, device=dev, dtype=torch.float32).mul_(w["sigma"])
+    d_out = torch.empty(plan.out_shape, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed_region():
+        for _ in range(args.warmup):
+            plan.separate(d_mix, d_mask, d_out, stream=stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                plan.separate(d_mix, d_mask, d_out, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps, clk
+
+    ms, clk = timed_region()
+    remeasured = False
+    if clk.rejected():
+        ms, clk = timed_region()
+        remeasured = True
+    ms = max_over_ranks(ms)
+
+    # Kernel-level timing on the launching stream (events recorded inside the engine).
+    eng.set_profiling(True)
+    fused, comb = [], []
+    for _ in range(max(3, min(args.steps, 20))):
+        plan.separate(d_mix, d_mask, d_out, stream=stream)
+        a, b, n_launch = plan.last_timing()
+        fused.append(a)
+        comb.append(b)
+    eng.set_profiling(False)
+    fused_ms = statistics.mean(fused)
+    combine_ms = statistics.mean(comb)
+
+    # End to end through the public host-buffer entry point (pinned host memory).
+    h_mix = torch.from_numpy(mix_h).pin_memory()
+    h_mask = d_mask.cpu().pin_memory()
+    h_out = torch.empty(plan.out_shape, dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+    plan.separate_host_ptr(h_mix.data_ptr(), h_mask.data_ptr(), h_out.data_ptr(), stream=stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        plan.separate_host_ptr(h_mix.data_ptr(), h_mask.data_ptr(), h_out.data_ptr(), stream=stream.cuda_stream)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = max_over_ranks(e2e_s)
+    barrier()
+
+    audio_s = w["seconds"] * world
+    value = audio_s / (ms / 1e3)
+    peak, peak_kind = measured_peak()
+    fbytes = fused_algorithmic_bytes(plan, w)
+    achieved = fbytes / (fused_ms / 1e3) / 1e9
+    traffic = profiled_traffic(args.workload)
+    line = None
+    if rank == 0:
+        line = {
+            "metric": "audio_seconds_per_second", "value": value, "unit": "audio-s/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded sines + noise; N(0, sigma) masks standing in for the network)",
+            "config": {"workload": args.workload, "desc": w["desc"], "tracks_per_step_per_gpu": 1,
+                       "chunks_per_track": plan.n_chunks, "frames_per_chunk": plan.n_frames,
+                       "mask_bytes_per_track": 4 * plan.mask_floats,
+                       "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "fused_kernel", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": fbytes,
+                         "fused_ms": fused_ms, "combine_ms": combine_ms},
+            "path": {"algorithmic_bytes_per_step": path_algorithmic_bytes(plan, w),
+                     "gbs": path_algorithmic_bytes(plan, w) / (ms / 1e3) / 1e9},
+            "clocks": dict(clk.summary(), remeasured=remeasured),
+            "e2e": {"value": audio_s / e2e_s, "unit": "audio-s/s",
+                    "h2d_bytes_per_step": 4 * (plan.n_channels * plan.n_samples + plan.mask_floats),
+                    "d2h_bytes_per_step": 4 * plan.out_floats},
+            "gpu_launches": n_launch * args.steps,
+        }
+    plan.close()
+    eng.close()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, w, rank)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, w, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+            dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            length = w["seconds"] * SR
+            threads = os.cpu_count() or 1
+            n_chunks = _n_chunks(w, length)
+            n_sample = max(1, min(n_chunks, 2 * threads))
+            mix = synth_audio(w["seed"], length)
+            dt, kind = cpu_run(w, length, mix, _host_mask(w, length, n_chunks), n_sample, threads)
+            line["cpu_baseline"] = {"value": n_sample * (w["seconds"] / n_chunks) / dt, "unit": "audio-s/s",
+                                    "cores": threads, "kind": kind,
+                                    "sample": f"{n_sample} of {n_chunks} chunks of one {w['seconds']} s track"}
+        print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -67,6 +67,14 @@ STG_API void stg_engine_destroy(stg_engine* engine);
 /* The message of the engine's last failure ("" after success). Borrowed. */
 STG_API const char* stg_engine_last_error(const stg_engine* engine);
 
+/* Kernel timing, the counterpart of the reference's wall-clock timers
+ * (tools/stems-split.cpp:94-97): when enabled, every run records CUDA events around its
+ * kernels on the run's stream; stg_plan_last_timing waits for the last run and returns the
+ * milliseconds of the fused spectral kernels and of the combine kernel. */
+STG_API stg_status stg_engine_set_profiling(stg_engine* engine, int32_t enabled);
+STG_API stg_status stg_plan_last_timing(stg_plan* plan, float* fused_ms, float* combine_ms,
+                                        int32_t* kernel_launches);
+
 /* ---- model configurations (the GGUF metadata the reference reads) ------------------------ */
 
 /* HTDemucs (src/htdemucs.cpp:478-500; n_fft 4096 and hop 1024 are fixed, :35-36). */

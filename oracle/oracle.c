@@ -806,11 +806,13 @@ static int tfc_chunk(void* vctx, int g) {
     const size_t plane = (size_t)dim_f * dim_t;
     float* in = (float*)calloc(4 * plane, sizeof(float));
     cplx* s = (cplx*)malloc(sizeof(cplx) * (size_t)Fn * dim_t);
+    /* zero_bins is read only for uvr_mdx models; msst ones keep every bin (:532) */
+    const int zero_bins = p->chunking == 0 ? p->zero_bins : 0;
     for (int c = 0; c < 2 && !rc; c++) {                                  /* :366-376 */
         int T = 0;
         rc = g_dsp.stft(p->n_fft, part + (size_t)c * C, C, p->hop, 0, (double*)s, &T);
         if (!rc && T != dim_t) rc = ERR_ARG;
-        for (int f = p->zero_bins; f < dim_f && !rc; f++)
+        for (int f = zero_bins; f < dim_f && !rc; f++)
             for (int t = 0; t < T; t++) {
                 const cplx v = s[(size_t)f * T + t];
                 in[(2 * c) * plane + (size_t)f * T + t] = (float)creal(v);

@@ -82,6 +82,9 @@ _SIGNATURES = {
     "stg_engine_create": (C.c_int32, [C.c_int, C.POINTER(C.c_void_p)]),
     "stg_engine_destroy": (None, [C.c_void_p]),
     "stg_engine_last_error": (C.c_char_p, [C.c_void_p]),
+    "stg_engine_set_profiling": (C.c_int32, [C.c_void_p, C.c_int32]),
+    "stg_plan_last_timing": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                         C.POINTER(C.c_int32)]),
     "stg_plan_htdemucs": (C.c_int32, [C.c_void_p, C.POINTER(HTDemucsConfig), C.c_int64, C.POINTER(C.c_void_p)]),
     "stg_plan_roformer": (C.c_int32, [C.c_void_p, C.POINTER(RoFormerConfig), C.c_int64, C.POINTER(C.c_void_p)]),
     "stg_plan_tfc": (C.c_int32, [C.c_void_p, C.POINTER(TFCConfig), C.c_int64, C.POINTER(C.c_void_p)]),
@@ -172,6 +175,10 @@ class Engine:
     def last_error(self) -> str:
         return lib().stg_engine_last_error(self._h).decode()
 
+    def set_profiling(self, enabled: bool = True):
+        """Record CUDA events around every run's kernels (see Plan.last_timing)."""
+        self._check(lib().stg_engine_set_profiling(self._h, int(enabled)), "set_profiling")
+
     def _check(self, rc, what):
         if rc != 0:
             msg = self.last_error()
@@ -258,6 +265,18 @@ class Plan:
             rc = lib().stg_separate_ex(self._h, _ptr(mix), _ptr(mask), _ptr(out), st, C.byref(opts))
         self.engine._check(rc, "separate")
         return out
+
+    def last_timing(self):
+        """(fused kernel ms, combine kernel ms, kernel launches) of the last run."""
+        a, b, n = C.c_float(), C.c_float(), C.c_int32()
+        self.engine._check(lib().stg_plan_last_timing(self._h, C.byref(a), C.byref(b), C.byref(n)),
+                           "last_timing")
+        return a.value, b.value, n.value
+
+    def separate_host_ptr(self, h_mix: int, h_mask: int, h_out: int, stream=None):
+        """Host pointers (e.g. pinned torch tensors' data_ptr()); blocks until h_out is filled."""
+        st = stream if (stream is None or isinstance(stream, int)) else stream.cuda_stream
+        self.engine._check(lib().stg_separate_host(self._h, h_mix, h_mask, h_out, st), "separate_host")
 
     def separate_host(self, mix, mask, out=None, stream=None):
         """Host buffers (numpy float32); returns the [S][C][n] result."""

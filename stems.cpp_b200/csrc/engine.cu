@@ -114,6 +114,7 @@ struct FftTables {
 // ---- engine -------------------------------------------------------------------------------
 struct stg_engine {
     int device = 0;
+    bool profiling = false;
     std::string last_error;
     std::map<int, std::unique_ptr<FftTables>> tables;
 
@@ -156,6 +157,14 @@ struct stg_plan {
     DevBuf d_y, d_tr;
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
     int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // fused start, fused end, combine end
+    bool timed = false;
+    int launches = 0;
+
+    ~stg_plan() {
+        for (cudaEvent_t& e : ev)
+            if (e) cudaEventDestroy(e);
+    }
 
     int64_t n_chunks() const { return (int64_t)chunks.size(); }
     int64_t out_floats() const { return (int64_t)S_out * C * len; }
@@ -434,6 +443,13 @@ void run_plan(stg_plan& P, const float* d_mix, const float* d_mask, float* d_out
     f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
     const int G = (int)P.chunks.size();
     const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : G;
+    P.timed = P.engine->profiling;
+    P.launches = 0;
+    if (P.timed) {
+        for (cudaEvent_t& e : P.ev)
+            if (!e) cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+        cuda_check(cudaEventRecord(P.ev[0], st), "cudaEventRecord");
+    }
     for (int b0 = 0; b0 < G; b0 += per) {
         if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
         const int nb = std::min(per, G - b0);
@@ -443,6 +459,7 @@ void run_plan(stg_plan& P, const float* d_mix, const float* d_mask, float* d_out
         f.Y = P.d_y.as<float>() + (int64_t)b0 * P.y_chunk_stride;
         f.Tr = P.d_tr.as<float>() + (int64_t)b0 * P.tr_chunk_stride;
         cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+        P.launches++;
         if (opt && opt->on_progress) {
             cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
             opt->on_progress(opt->user, b0 + nb, G);
@@ -458,7 +475,10 @@ void run_plan(stg_plan& P, const float* d_mix, const float* d_mask, float* d_out
     c.S = P.S; c.C = P.C; c.len = P.len; c.out_shift = P.out_shift;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    if (P.timed) cuda_check(cudaEventRecord(P.ev[1], st), "cudaEventRecord");
     cuda_check(launch_combine(c, st), "combine kernel launch");
+    P.launches++;
+    if (P.timed) cuda_check(cudaEventRecord(P.ev[2], st), "cudaEventRecord");
 }
 
 stg_status guard(stg_engine* e, const std::function<void()>& fn) {
@@ -534,6 +554,26 @@ STG_API void stg_engine_destroy(stg_engine* e) {
 }
 
 STG_API const char* stg_engine_last_error(const stg_engine* e) { return e ? e->last_error.c_str() : ""; }
+
+STG_API stg_status stg_engine_set_profiling(stg_engine* e, int32_t enabled) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    e->profiling = enabled != 0;
+    return STG_OK;
+}
+
+STG_API stg_status stg_plan_last_timing(stg_plan* p, float* fused_ms, float* combine_ms, int32_t* launches) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        if (!p->timed) fail(STG_INVALID_ARGUMENT, "the last run was not timed (stg_engine_set_profiling)");
+        cuda_check(cudaEventSynchronize(p->ev[2]), "cudaEventSynchronize");
+        float a = 0.0f, b = 0.0f;
+        cuda_check(cudaEventElapsedTime(&a, p->ev[0], p->ev[1]), "cudaEventElapsedTime");
+        cuda_check(cudaEventElapsedTime(&b, p->ev[1], p->ev[2]), "cudaEventElapsedTime");
+        if (fused_ms) *fused_ms = a;
+        if (combine_ms) *combine_ms = b;
+        if (launches) *launches = p->launches;
+    });
+}
 
 STG_API stg_status stg_plan_htdemucs(stg_engine* e, const stg_htdemucs_config* c, int64_t n, stg_plan** out) {
     return make_plan(e, c, n, out, plan_htdemucs);

@@ -1,0 +1,172 @@
+"""The CPU oracle, pinned three ways (no GPU needed):
+
+1. the reference's own known-answer tests, restated against the oracle's primitives
+   (tests/dsp_test.cpp:53-96 and tests/vr_dsp_test.cpp:8-33 of the reference), and, where
+   the reference was compiled here (oracle/_ref), the reference's own test binaries;
+2. the golden vectors of tests/golden/golden.npz, produced by the reference's compiled
+   st::FFT / st::VRFFT / st::torch_stft / st::htdemucs_spec (make_golden.py);
+3. the live reference, when oracle/_ref is present: primitives bit for bit, and whole
+   separations with the reference's primitives under the restated host loops.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from common import synth_audio
+from golden_cases import CASES, inputs_for
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+# ---- 1. the reference's known-answer tests -----------------------------------------------
+@pytest.mark.parametrize("binary", ["dsp_test", "vr_dsp_test"])
+def test_reference_kat_binaries_pass(binary):
+    path = os.path.join(ROOT, "oracle", "_ref", binary)
+    if not os.path.exists(path):
+        pytest.skip("reference not compiled on this machine")
+    res = subprocess.run([path], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and "PASS" in res.stdout, res.stdout + res.stderr
+
+
+def test_fft_inverse_is_identity(oracle_mod):                   # dsp_test.cpp:53-64
+    rng = np.random.default_rng(1234)
+    a = rng.uniform(-1, 1, 4096) + 1j * rng.uniform(-1, 1, 4096)
+    back = oracle_mod.fft(oracle_mod.fft(a), inverse=True) / 4096
+    assert np.abs(back - a).max() < 1e-12
+
+
+@pytest.mark.parametrize("normalized", [False, True])
+def test_stft_round_trip(oracle_mod, normalized):               # dsp_test.cpp:66-78
+    rng = np.random.default_rng(99)
+    x = rng.uniform(-1, 1, 441 * 200).astype(np.float32)
+    y = oracle_mod.torch_istft(oracle_mod.torch_stft(x, 2048, 441, normalized), 2048, 441, normalized)
+    assert y.size == x.size and np.abs(y - x).max() < 1e-5
+
+
+def test_htdemucs_round_trip_away_from_edges(oracle_mod):       # dsp_test.cpp:80-96
+    rng = np.random.default_rng(7)
+    f, p, a = rng.uniform(40, 0.4 * 44100, 24), rng.uniform(0, 2 * np.pi, 24), rng.uniform(0.02, 0.2, 24)
+    n = 1024 * 60
+    t = np.arange(n)
+    x = (a[:, None] * np.sin(2 * np.pi * f[:, None] * t / 44100 + p[:, None])).sum(0).astype(np.float32)
+    spec = oracle_mod.htdemucs_spec(x)
+    y = oracle_mod.htdemucs_ispec(spec, n)
+    assert spec.shape[1] == n // 1024
+    assert np.abs(y[4096:-4096] - x[4096:-4096]).max() < 1e-6
+
+
+@pytest.mark.parametrize("n", [320, 512, 640, 960, 2048, 7680])
+def test_vrfft_impulse_and_inverse(oracle_mod, n):               # vr_dsp_test.cpp:8-15
+    x = np.zeros(n, np.complex128)
+    x[7] = 1
+    X = _vr(oracle_mod, x)                                      # Bluestein at every size, as there
+    k = np.arange(n)
+    assert np.abs(X - np.exp(-2j * np.pi * 7 * k / n)).max() < 1e-10
+    back = _vr(oracle_mod, X, inverse=True)
+    assert np.abs(back / n - x).max() < 1e-10
+
+
+def _vr(oracle_mod, x, inverse=False):
+    a = np.ascontiguousarray(x, np.complex128).copy()
+    assert oracle_mod.lib().or_vrfft(a.size, a.view(np.float64), int(inverse)) == 0
+    return a
+
+
+def test_identity_mask_gives_back_the_mix(oracle_mod, pkg):
+    """RoFormer with every band mask 1+0i: the whole chunked path is the identity."""
+    sizes, freqs = pkg.bands.mel_bands()
+    chunk = 441 * 20
+    for length in (441 * 70 + 3, 441 * 15):
+        p = oracle_mod.rf_params(sizes, freqs, chunk=chunk, num_overlap=4)
+        T = chunk // 441 + 1
+        m = np.zeros((oracle_mod.rf_n_chunks(p, length), int(sizes.sum()) * 4 * T), np.float32)
+        m[:, 0::2] = 1.0
+        x = synth_audio(3, length)
+        y = oracle_mod.rf_separate(p, x, m)
+        assert np.abs(y[0] - x).max() < 1e-6
+
+
+# ---- 2. golden vectors from the reference ----------------------------------------------------
+def test_primitives_match_golden(oracle_mod, golden):
+    g = golden
+    assert np.array_equal(oracle_mod.fft(g["prim_fft4096_in"]), g["prim_fft4096"])
+    assert np.abs(_vr(oracle_mod, g["prim_vrfft7680_in"]) - g["prim_vrfft7680"]).max() < 1e-12
+    s = oracle_mod.torch_stft(g["prim_stft_in"], 2048, 441)
+    assert np.array_equal(s, g["prim_stft_2048_441"])
+    assert np.array_equal(oracle_mod.torch_istft(s, 2048, 441), g["prim_istft_2048_441"])
+    h = oracle_mod.htdemucs_spec(g["prim_hspec_in"])
+    assert np.array_equal(h, g["prim_hspec_4096"])
+    assert np.array_equal(oracle_mod.htdemucs_ispec(h, g["prim_hspec_in"].size), g["prim_hispec_4096"])
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_separation_matches_golden(oracle_mod, golden, name):
+    case = CASES[name]
+    params, mix, mask = inputs_for(case)
+    assert np.sum(mix, dtype=np.float64) == golden[f"{name}_mix_sum"], "input generator drifted"
+    assert np.sum(mask, dtype=np.float64) == golden[f"{name}_mask_sum"], "input generator drifted"
+    got = case["run"](params, mix, mask)
+    want = golden[f"{name}_out"]
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= 1e-6 * max(1.0, np.abs(want).max())
+
+
+# ---- 3. the live reference --------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def ref(oracle_mod):
+    R = oracle_mod.ref_lib()
+    if R is None:
+        pytest.skip("reference not compiled on this machine")
+    return R
+
+
+def test_primitives_bit_exact_vs_reference(oracle_mod, ref):
+    rng = np.random.default_rng(5)
+    for n in (2048, 4096, 16384):
+        x = rng.standard_normal(n) + 1j * rng.standard_normal(n)
+        assert np.array_equal(oracle_mod.fft(x), oracle_mod.fft(x, impl=ref))
+    for n in (320, 7680):
+        x = rng.standard_normal(n) + 1j * rng.standard_normal(n)
+        assert np.array_equal(_vr(oracle_mod, x), oracle_mod.fft(x, impl=ref))
+    x = rng.uniform(-1, 1, 441 * 30 + 11).astype(np.float32)
+    for nfft, hop in ((2048, 441), (7680, 1024)):
+        s = oracle_mod.torch_stft(x, nfft, hop)
+        assert np.array_equal(s, oracle_mod.torch_stft(x, nfft, hop, impl=ref))
+        assert np.array_equal(oracle_mod.torch_istft(s, nfft, hop), oracle_mod.torch_istft(s, nfft, hop, impl=ref))
+    h = oracle_mod.htdemucs_spec(x)
+    assert np.array_equal(h, oracle_mod.htdemucs_spec(x, impl=ref))
+    assert np.array_equal(oracle_mod.htdemucs_ispec(h, x.size), oracle_mod.htdemucs_ispec(h, x.size, impl=ref))
+
+
+@pytest.mark.parametrize("name", ["rf_bs", "tfc_uvr"])
+def test_separation_with_reference_primitives(oracle_mod, ref, name):
+    case = CASES[name]
+    params, mix, mask = inputs_for(case, seed=77)
+    mine = case["run"](params, mix, mask)
+    assert oracle_mod.use_reference(True)
+    try:
+        theirs = case["run"](params, mix, mask)
+    finally:
+        oracle_mod.use_reference(False)
+    assert np.array_equal(mine, theirs)
+
+
+# ---- band tables (tools/convert_roformer.py:107-124) ---------------------------------------
+def test_band_tables(pkg):
+    sizes, freqs = pkg.bands.mel_bands()
+    bpf = pkg.bands.bands_per_freq(sizes, freqs, 1025)
+    assert sizes.size == 60 and sizes.sum() == 1979 and sizes.min() == 6 and sizes.max() == 130
+    assert bpf.min() == 1 and bpf.max() == 2
+    bs, bf = pkg.bands.bs_bands()
+    assert bs.size == 62 and bs.sum() == 1025 and list(bs[-2:]) == [128, 129]
+    assert np.array_equal(bf, np.arange(1025))
