@@ -124,11 +124,19 @@ struct stg_engine {
             auto nt = std::make_unique<FftTables>();
             const std::vector<double> w = hann_periodic(n);
             std::vector<float> wf(w.begin(), w.end());
-            std::vector<float2> tw(n);
-            for (int m = 0; m < n; m++) {
-                const double th = -2.0 * M_PI * (double)m / n;
-                tw[m] = make_float2((float)std::cos(th), (float)std::sin(th));
+            // per-pass tables of the kernel's radix plan: the pass at stride NS (radix R)
+            // holds W_{NS*R}^{k*r} at (NS - 1) + (r - 1)*NS + k
+            std::vector<float2> tw(n, make_float2(1.0f, 0.0f));
+            int ns = 1;
+            for (int R : fused_radices(n)) {
+                for (int r = 1; r < R; r++)
+                    for (int k = 0; k < ns; k++) {
+                        const double th = -2.0 * M_PI * (double)k * r / ((double)ns * R);
+                        tw[(ns - 1) + (r - 1) * ns + k] = make_float2((float)std::cos(th), (float)std::sin(th));
+                    }
+                ns *= R;
             }
+            if (ns != n) fail(STG_INTERNAL_ERROR, "radix plan does not multiply to n_fft");
             upload(nt->win, wf, "window table");
             upload(nt->tw, tw, "twiddle table");
             t = std::move(nt);
@@ -151,9 +159,9 @@ struct stg_plan {
     int64_t step_out = 1, out_shift = 0, max_out_len = 0;
     int nan_to_zero = 0, complement = 0;
     float compensate = 1.0f;
-    int zero_dc = 0, dim_f = 0, zero_bins = 0;
+    int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
     int64_t stem_stride = 0;
-    DevBuf d_chunks, d_w, d_env, d_ebeg, d_ent, d_binv;
+    DevBuf d_chunks, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
     int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
@@ -177,6 +185,8 @@ namespace {
 void finish_plan(stg_plan& P, const std::vector<float>& W, int env_frames) {
     const int N = P.g.n_fft, hop = P.g.hop;
     if (!fused_supported(N)) fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
+    if (hop > fused_max_hop(N) || hop > N)
+        fail(STG_UNSUPPORTED, "hop " + std::to_string(hop) + " is too large for n_fft " + std::to_string(N));
     if (P.K * hop < N - hop) P.K = (N - hop + hop - 1) / hop;   // one tile boundary per sample at most
     P.n_tiles = (P.g.T + P.K - 1) / P.K;
     P.y_chunk_stride = (int64_t)P.S * P.C * P.g.Lout;
@@ -268,6 +278,7 @@ void plan_roformer(stg_plan& P, const stg_roformer_config& c, int64_t len) {
         const int sz = c.band_sizes[b];
         if (sz < 1) fail(STG_MODEL_ERROR, "roformer: empty band");
         const int din = sz * P.C * 2;                                 // :85
+        if (din > 0xffff) fail(STG_UNSUPPORTED, "roformer: band too wide");
         for (int j = 0; j < sz; j++) {
             const int f = c.band_freqs[foff + j];
             if (f < 0 || f >= F) fail(STG_MODEL_ERROR, "roformer: band frequency out of range");
@@ -283,12 +294,28 @@ void plan_roformer(stg_plan& P, const stg_roformer_config& c, int64_t len) {
     std::vector<int> ebeg(F + 1, 0);
     std::vector<int2> ent;
     std::vector<float> binv(F);
+    // bin_tab[f]: the first two bands holding f, each as (entry offset without the frame term)
+    // / (2C) in bits 0-21 | band size in bits 22-31; 0 when absent. A bin no band holds gets
+    // weight 0: its mask average is 0 / 1 (src/roformer.cpp:272).
+    std::vector<int2> btab(F, make_int2(0, 0));
+    int multi = 0;
     for (int f = 0; f < F; f++) {
         ebeg[f] = (int)ent.size();
         ent.insert(ent.end(), per_bin[f].begin(), per_bin[f].end());
-        binv[f] = (float)(1.0 / std::max(bpf[f], 1));
+        binv[f] = per_bin[f].empty() ? 0.0f : (float)(1.0 / bpf[f]);
+        const size_t n = per_bin[f].size();
+        int v[2] = {0, 0};
+        for (size_t k = 0; k < n && k < 2; k++) {
+            const int units = per_bin[f][k].x / (P.C * 2), size = per_bin[f][k].y / (P.C * 2);
+            if (units >= (1 << 22) || size >= (1 << 10)) fail(STG_UNSUPPORTED, "roformer: band table too large");
+            v[k] = (int)((unsigned)units | ((unsigned)size << 22));
+        }
+        btab[f] = make_int2(v[0], v[1]);
+        if (n > 2) multi = 1;
     }
+    P.bin_multi = multi;
     ebeg[F] = (int)ent.size();
+    upload(P.d_btab, btab, "band table");
     upload(P.d_ebeg, ebeg, "band table");
     upload(P.d_ent, ent, "band table");
     upload(P.d_binv, binv, "band table");
@@ -437,6 +464,8 @@ void run_plan(stg_plan& P, const float* d_mix, const float* d_mask, float* d_out
     f.win = tabs.win.as<float>(); f.tw = tabs.tw.as<float2>(); f.inv_env = P.d_env.as<float>();
     f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
     f.mask_chunk_stride = P.mask_per_chunk;
+    f.bin_tab = P.d_btab.as<int2>();
+    f.bin_multi = P.bin_multi;
     f.bin_ebeg = P.d_ebeg.as<int>(); f.bin_ent = P.d_ent.as<int2>(); f.bin_inv = P.d_binv.as<float>();
     f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
     f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;

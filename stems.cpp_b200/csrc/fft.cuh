@@ -12,8 +12,8 @@
 //
 // Twiddles: the codelets' internal twiddles W_R^m are compile-time constants derived from
 // the DFT definition (constexpr Taylor series in double, rounded once to float); the
-// inter-pass twiddles W_N^m come from a table computed on the host in double precision.
-// No device trigonometry is used anywhere.
+// inter-pass twiddles come from per-pass tables computed on the host in double precision
+// (twiddle_index). No device trigonometry is used anywhere.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -200,9 +200,29 @@ template <bool INV> struct Dft<10, INV> : DftCT<2, 5, INV> {};
 template <bool INV> struct Dft<32, INV> : DftCT<2, 16, INV> {};
 
 // ---- one Stockham pass and a whole transform ---------------------------------------------
-// buf: padded shared-memory frame. tw: W_N^m for m in [0, N) (forward sign).
-template <int N, int R, int NS, int T, bool INV>
-__device__ __forceinline__ void stockham_pass(float2* buf, const float2* __restrict__ tw, int tid) {
+// Twiddle table of a radix plan: the pass at stride NS (radix R) multiplies point r of its
+// butterfly k (k = j mod NS) by W_{NS*R}^{k*r}. Its (R-1)*NS values sit at
+// (NS - 1) + (r - 1)*NS + k, so the passes' tables tile [0, N - 1) (the sizes (R-1)*NS
+// telescope) and the lanes of a warp, which hold consecutive k, read consecutive entries.
+template <int NS> __host__ __device__ constexpr int twiddle_index(int r, int k) { return (NS - 1) + (r - 1) * NS + k; }
+
+// Twiddle sources: the table in global memory (read through L1) or a copy in shared memory.
+struct TwGlobal {
+    const float2* __restrict__ p;
+    __device__ __forceinline__ float2 operator()(int i) const { return __ldg(p + i); }
+};
+struct TwShared {
+    const float2* p;
+    __device__ __forceinline__ float2 operator()(int i) const { return p[i]; }
+};
+
+// One pass with caller-supplied input and output. Butterfly j reads the points
+// j + r*NB (NB = N/R) through ld(j, r) and writes the points base + r*NS through
+// st(base, r, v); r is a compile-time constant after unrolling, so callers fold it into
+// immediate offsets. MID_SYNC puts a barrier between the loads and the stores, which an
+// in-place pass needs; a pass that reads one buffer and writes another does not.
+template <int N, int R, int NS, int T, bool INV, bool MID_SYNC, class Tw, class Ld, class St>
+__device__ __forceinline__ void pass_io(const Tw& tw, int tid, Ld&& ld, St&& st) {
     constexpr int NB = N / R;
     constexpr int ROUNDS = (NB + T - 1) / T;
     constexpr bool EXACT = (NB % T) == 0;
@@ -212,20 +232,19 @@ __device__ __forceinline__ void stockham_pass(float2* buf, const float2* __restr
         const int j = tid + rd * T;
         if (EXACT || j < NB) {
 #pragma unroll
-            for (int r = 0; r < R; r++) v[rd][r] = buf[pad_idx(j + r * NB)];
+            for (int r = 0; r < R; r++) v[rd][r] = ld(j, r);
         }
     }
-    __syncthreads();
+    if constexpr (MID_SYNC) __syncthreads();
 #pragma unroll
     for (int rd = 0; rd < ROUNDS; rd++) {
         const int j = tid + rd * T;
         if (EXACT || j < NB) {
             const int k = j % NS;
             if constexpr (NS > 1) {
-                constexpr int STEP = N / (NS * R);
 #pragma unroll
                 for (int r = 1; r < R; r++) {
-                    float2 w = __ldg(&tw[k * r * STEP]);
+                    float2 w = tw(twiddle_index<NS>(r, k));
                     if (INV) w.y = -w.y;
                     v[rd][r] = cmul(v[rd][r], w);
                 }
@@ -233,26 +252,69 @@ __device__ __forceinline__ void stockham_pass(float2* buf, const float2* __restr
             Dft<R, INV>::template run<1>(v[rd]);
             const int base = (j / NS) * NS * R + k;
 #pragma unroll
-            for (int r = 0; r < R; r++) buf[pad_idx(base + r * NS)] = v[rd][r];
+            for (int r = 0; r < R; r++) st(base, r, v[rd][r]);
         }
     }
+}
+
+// Padded addresses of a pass's points. pad_idx(x + c) = pad_idx(x) + c + c/16 whenever c is
+// a multiple of 16, and pad_idx(x + r) = pad_idx(x) + r whenever x mod 16 + r < 16.
+template <int N, int R> __device__ __forceinline__ int pad_load(int j, int r) {
+    constexpr int NB = N / R;
+    if constexpr (NB % 16 == 0) return pad_idx(j) + r * (NB + NB / 16);
+    else return pad_idx(j + r * NB);
+}
+template <int R, int NS> __device__ __forceinline__ int pad_store(int base, int r) {
+    if constexpr (NS % 16 == 0) return pad_idx(base) + r * (NS + NS / 16);
+    else if constexpr (NS == 1 && 16 % R == 0) return pad_idx(base) + r;   // base = j*R
+    else return pad_idx(base + r * NS);
+}
+
+// In-place pass on the padded shared-memory frame buf, ending with a barrier.
+template <int N, int R, int NS, int T, bool INV, class Tw>
+__device__ __forceinline__ void stockham_pass(float2* buf, const Tw& tw, int tid) {
+    pass_io<N, R, NS, T, INV, true>(
+        tw, tid, [&](int j, int r) { return buf[pad_load<N, R>(j, r)]; },
+        [&](int base, int r, float2 v) { buf[pad_store<R, NS>(base, r)] = v; });
     __syncthreads();
 }
 
 template <int... Rs> struct RadixList {};
 
-template <int N, int T, bool INV, int NS, int R, int... Rest>
-__device__ __forceinline__ void fft_passes(float2* buf, const float2* __restrict__ tw, int tid) {
+// Split a radix list: Init<L>::type drops the last radix, ::last is it, ::prod multiplies the rest.
+template <class A, class B> struct Concat;
+template <int... A, int... B> struct Concat<RadixList<A...>, RadixList<B...>> { using type = RadixList<A..., B...>; };
+template <class L> struct Init;
+template <int R> struct Init<RadixList<R>> {
+    using type = RadixList<>;
+    static constexpr int last = R, prod = 1;
+};
+template <int R, int R2, int... Rest> struct Init<RadixList<R, R2, Rest...>> {
+    using sub = Init<RadixList<R2, Rest...>>;
+    using type = typename Concat<RadixList<R>, typename sub::type>::type;
+    static constexpr int last = sub::last, prod = R * sub::prod;
+};
+template <class L> struct Head;
+template <int R, int... Rest> struct Head<RadixList<R, Rest...>> {
+    static constexpr int first = R;
+    using tail = RadixList<Rest...>;
+};
+
+// In-place passes for the radices of a list, the first of them at stride NS.
+template <int N, int T, bool INV, int NS, class Tw>
+__device__ __forceinline__ void passes(float2*, const Tw&, int, RadixList<>) {}
+template <int N, int T, bool INV, int NS, class Tw, int R, int... Rest>
+__device__ __forceinline__ void passes(float2* buf, const Tw& tw, int tid, RadixList<R, Rest...>) {
     stockham_pass<N, R, NS, T, INV>(buf, tw, tid);
-    if constexpr (sizeof...(Rest) > 0) fft_passes<N, T, INV, NS * R, Rest...>(buf, tw, tid);
+    passes<N, T, INV, NS * R>(buf, tw, tid, RadixList<Rest...>{});
 }
 
 // Transform the frame in buf (padded layout) in place: X[k] = sum_n x[n] W_N^{nk}, W = e^{-2 pi i/N}
 // (forward) or e^{+2 pi i/N} (inverse, unnormalised). Callers synchronise before the first
 // pass reads what they wrote; the last pass ends with a barrier.
-template <int N, int T, bool INV, int... Rs>
-__device__ __forceinline__ void fft(float2* buf, const float2* __restrict__ tw, int tid, RadixList<Rs...>) {
-    fft_passes<N, T, INV, 1, Rs...>(buf, tw, tid);
+template <int N, int T, bool INV, class Tw, int... Rs>
+__device__ __forceinline__ void fft(float2* buf, const Tw& tw, int tid, RadixList<Rs...>) {
+    passes<N, T, INV, 1>(buf, tw, tid, RadixList<Rs...>{});
 }
 
 } // namespace stg

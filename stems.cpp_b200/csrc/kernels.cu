@@ -17,20 +17,59 @@
 // with their crossfade weights (reading Y and the tile-boundary partials Tr), divides by the
 // summed weight, and applies the architecture's epilogue (nan_to_num, compensation,
 // complement).
+#include <algorithm>
+#include <type_traits>
+#include <vector>
+
 #include "fft.cuh"
 #include "kernels.h"
 
 namespace stg {
 
+// Threads per CTA, radix plan, the CTAs per SM the register budget aims at, and the largest
+// hop the input prefetch registers cover.
 template <int N> struct FftCfg;
-template <> struct FftCfg<2048> { static constexpr int T = 128; using Plan = RadixList<8, 16, 16>; };
-template <> struct FftCfg<4096> { static constexpr int T = 256; using Plan = RadixList<16, 16, 16>; };
-template <> struct FftCfg<7680> { static constexpr int T = 512; using Plan = RadixList<15, 8, 8, 8>; };
+template <> struct FftCfg<2048> {
+    static constexpr int T = 128, MINB = 3, HOPMAX = 512;
+    static constexpr bool AHEAD = false;    // mask loads issued one frame ahead
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;   // table copies in shared memory
+    using Plan = RadixList<8, 16, 16>;
+};
+template <> struct FftCfg<4096> {
+    static constexpr int T = 256, MINB = 2, HOPMAX = 1024;
+    static constexpr bool AHEAD = false;
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    using Plan = RadixList<16, 16, 16>;
+};
+template <> struct FftCfg<7680> {
+    static constexpr int T = 512, MINB = 1, HOPMAX = 1024;
+    static constexpr bool AHEAD = false;
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    using Plan = RadixList<15, 8, 8, 8>;
+};
 
 __device__ __forceinline__ int64_t reflect1(int64_t j, int64_t n) {
     if (j < 0) j = -j;
     if (j >= n) j = 2 * (n - 1) - j;
     return j;
+}
+
+// Loads for data read once per kernel (the masks): bypass L1 so the tables stay resident.
+__device__ __forceinline__ float ld_stream(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float2 ld_stream2(const float* p) {
+    float2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+    return v;
 }
 
 __device__ __forceinline__ float chunk_sample(const FusedParams& p, const ChunkDesc& cd,
@@ -42,215 +81,366 @@ __device__ __forceinline__ float chunk_sample(const FusedParams& p, const ChunkD
     int64_t x = cd.src0 + pl;
     if (p.reflect_global) x = reflect1(x, p.len);
     else if (x < 0 || x >= p.len) return 0.0f;
-    return __ldg(chan + x);
+    return ld_stream(chan + x);
 }
 
-// The stand-in network: turn the two channels' spectra at bin f of frame t into the
-// spectra the iSTFT consumes for stem s.
-template <int ARCH, int N>
-__device__ __forceinline__ void spectral_op(const FusedParams& p, int ci, int s, int t, int f,
-                                            float2 zl, float2 zr, float2& yl, float2& yr) {
-    const float* __restrict__ m = p.mask + (int64_t)ci * p.mask_chunk_stride;
-    if constexpr (ARCH == ARCH_ROFORMER) {
-        // src/roformer.cpp:251-278: masks of every band holding f, averaged, times z.
-        float2 al = make_float2(0.f, 0.f), ar = make_float2(0.f, 0.f);
-        const float* ms = m + (int64_t)s * p.stem_stride;
-        const int e1 = __ldg(p.bin_ebeg + f + 1);
-        for (int e = __ldg(p.bin_ebeg + f); e < e1; e++) {
-            const int2 en = __ldg(p.bin_ent + e);
-            const float* q = ms + en.x + (int64_t)t * en.y;
-            if (p.n_channels == 2) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(q));
-                al.x += v.x; al.y += v.y; ar.x += v.z; ar.y += v.w;
-            } else {
-                const float2 v = __ldg(reinterpret_cast<const float2*>(q));
-                al.x += v.x; al.y += v.y;
+// ---- the stand-in network ---------------------------------------------------------------
+// Each thread owns bins f = tid + i*T (i < BPT); prefetch() issues every mask load of its bins
+// for one (stem, frame) before apply() consumes them, so the loads overlap one another.
+template <int ARCH, int N, int T> struct MaskOp {
+    static constexpr int NBIN = N / 2 + 1;
+    static constexpr int BPT = (NBIN + T - 1) / T;
+    float4 a[BPT];
+    float4 b[BPT];   // RoFormer: the second band holding the bin
+    float inv[BPT];  // RoFormer: 1 / bands holding the bin (negative: more than two)
+
+    const int2* btab;   // RoFormer: the bin table's copy in shared memory
+
+    __device__ __forceinline__ void prefetch(const FusedParams& p, int ci, int s, int t, int tid) {
+        const float* __restrict__ m = p.mask + (int64_t)ci * p.mask_chunk_stride;
+        if constexpr (ARCH == ARCH_ROFORMER) {
+            // src/roformer.cpp:256-269: band b's mask for frame t is the row
+            // [off_b*T + t*din_b, +din_b) of the stem's block; entry (j*C + c)*2 + {re, im}.
+            const float* ms = m + (int64_t)s * p.stem_stride;
+#pragma unroll
+            for (int i = 0; i < BPT; i++) {
+                const int f = tid + i * T;
+                a[i] = b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                inv[i] = 0.0f;
+                if (f < NBIN) {
+                    // (offset / 2C) in bits 0-21, band size in bits 22-31; the band's row for
+                    // frame t starts size * t entries further on
+                    const int2 e = btab[f];
+                    const unsigned s0 = (unsigned)e.x >> 22, s1 = (unsigned)e.y >> 22;
+                    const int u0 = (e.x & 0x3fffff) + t * (int)s0, u1 = (e.y & 0x3fffff) + t * (int)s1;
+                    inv[i] = s1 ? 0.5f : (s0 ? 1.0f : 0.0f);
+                    if (p.n_channels == 2) {
+                        a[i] = ld_stream4(ms + 4 * u0);
+                        if (s1) b[i] = ld_stream4(ms + 4 * u1);
+                    } else {
+                        const float2 u = ld_stream2(ms + 2 * u0);
+                        a[i] = make_float4(u.x, u.y, 0.f, 0.f);
+                        if (s1) {
+                            const float2 v = ld_stream2(ms + 2 * u1);
+                            b[i] = make_float4(v.x, v.y, 0.f, 0.f);
+                        }
+                    }
+                }
+            }
+        } else if constexpr (ARCH == ARCH_HTDEMUCS) {
+            // src/htdemucs.cpp:463-469: planes [S][2C][F][T], re = 2c, im = 2c + 1.
+            const int F = N / 2;
+            const int64_t plane = (int64_t)F * p.g.T;
+            const float* ms = m + (int64_t)s * 2 * p.n_channels * plane + t;
+#pragma unroll
+            for (int i = 0; i < BPT; i++) {
+                const int f = tid + i * T;
+                a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (f < F) {
+                    const float* q = ms + (int64_t)f * p.g.T;
+                    a[i].x = ld_stream(q);
+                    a[i].y = ld_stream(q + plane);
+                    if (p.n_channels == 2) {
+                        a[i].z = ld_stream(q + 2 * plane);
+                        a[i].w = ld_stream(q + 3 * plane);
+                    }
+                }
+            }
+        } else {
+            // src/tfc_tdf.cpp:370-387: real planes [4S][dim_f][T]: L re, L im, R re, R im.
+            const int64_t plane = (int64_t)p.dim_f * p.g.T;
+            const float* ms = m + (int64_t)s * 4 * plane + t;
+#pragma unroll
+            for (int i = 0; i < BPT; i++) {
+                const int f = tid + i * T;
+                a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (f >= p.zero_bins && f < p.dim_f) {
+                    const float* q = ms + (int64_t)f * p.g.T;
+                    a[i] = make_float4(ld_stream(q), ld_stream(q + plane), ld_stream(q + 2 * plane),
+                                       ld_stream(q + 3 * plane));
+                }
             }
         }
-        const float inv = __ldg(p.bin_inv + f);
-        yl = cmul(zl, cscale(al, inv));
-        yr = cmul(zr, cscale(ar, inv));
-        if (p.zero_dc && f == 0) { yl = make_float2(0.f, 0.f); yr = yl; }
-    } else if constexpr (ARCH == ARCH_HTDEMUCS) {
-        // src/htdemucs.cpp:463-470 with the network output ox = Z * M; Nyquist dropped.
-        if (f >= N / 2) { yl = make_float2(0.f, 0.f); yr = yl; return; }
-        const int T = p.g.T, F = N / 2;
-        const int64_t plane = (int64_t)F * T, idx = (int64_t)f * T + t;
-        const float* ms = m + (int64_t)s * 2 * p.n_channels * plane;
-        const float2 ml = make_float2(__ldg(ms + idx), __ldg(ms + plane + idx));
-        yl = cmul(zl, ml);
-        if (p.n_channels == 2) {
-            const float2 mr = make_float2(__ldg(ms + 2 * plane + idx), __ldg(ms + 3 * plane + idx));
-            yr = cmul(zr, mr);
-        } else {
-            yr = make_float2(0.f, 0.f);
-        }
-    } else {
-        // src/tfc_tdf.cpp:370-387: CaC planes [4][dim_f][T], bins below zero_bins and at or
-        // above dim_f zero, network output y = in * mask.
-        if (f < p.zero_bins || f >= p.dim_f) { yl = make_float2(0.f, 0.f); yr = yl; return; }
-        const int T = p.g.T;
-        const int64_t plane = (int64_t)p.dim_f * T, idx = (int64_t)f * T + t;
-        const float* ms = m + (int64_t)s * 4 * plane;
-        yl = make_float2(zl.x * __ldg(ms + idx), zl.y * __ldg(ms + plane + idx));
-        yr = make_float2(zr.x * __ldg(ms + 2 * plane + idx), zr.y * __ldg(ms + 3 * plane + idx));
     }
+
+    // Bin f = tid + i*T of the two channels' spectra zl, zr -> the spectra the iSTFT consumes.
+    __device__ __forceinline__ void apply(const FusedParams& p, int ci, int s, int t, int f, int i,
+                                          float2 zl, float2 zr, float2& yl, float2& yr) const {
+        if constexpr (ARCH == ARCH_ROFORMER) {
+            // masks of every band holding f, averaged (src/roformer.cpp:270-276), times z
+            float2 al = make_float2(a[i].x + b[i].x, a[i].y + b[i].y);
+            float2 ar = make_float2(a[i].z + b[i].z, a[i].w + b[i].w);
+            float w = inv[i];
+            if (p.bin_multi) {   // bins in more than two bands: the rest straight from memory
+                const int e0 = __ldg(p.bin_ebeg + f), e1 = __ldg(p.bin_ebeg + f + 1);
+                w = __ldg(p.bin_inv + f);
+                const float* ms = p.mask + (int64_t)ci * p.mask_chunk_stride + (int64_t)s * p.stem_stride;
+                for (int k = e0 + 2; k < e1; k++) {
+                    const int2 en = __ldg(p.bin_ent + k);
+                    const float* q = ms + en.x + (int64_t)t * en.y;
+                    al.x += ld_stream(q); al.y += ld_stream(q + 1);
+                    if (p.n_channels == 2) { ar.x += ld_stream(q + 2); ar.y += ld_stream(q + 3); }
+                }
+            }
+            yl = cmul(zl, cscale(al, w));
+            yr = cmul(zr, cscale(ar, w));
+            if (p.zero_dc && f == 0) { yl = make_float2(0.f, 0.f); yr = yl; }      // :278
+        } else if constexpr (ARCH == ARCH_HTDEMUCS) {
+            // network output ox = Z * M; the Nyquist bin is dropped (src/stft.h:126)
+            yl = cmul(zl, make_float2(a[i].x, a[i].y));
+            yr = cmul(zr, make_float2(a[i].z, a[i].w));
+            if (f >= N / 2) { yl = make_float2(0.f, 0.f); yr = yl; }
+        } else {
+            // y = in * mask per CaC plane; zero below zero_bins and from dim_f up (the loads
+            // left a[i] at zero there)
+            yl = make_float2(zl.x * a[i].x, zl.y * a[i].y);
+            yr = make_float2(zr.x * a[i].z, zr.y * a[i].w);
+        }
+    }
+};
+
+// New input samples [q, q + hop) a frame needs beyond the previous one, per thread.
+template <int T, int HOPMAX> struct InPrefetch {
+    static constexpr int K = (HOPMAX + T - 1) / T;
+    float2 v[K];
+};
+
+__device__ __forceinline__ float2 frame_sample(const FusedParams& p, const ChunkDesc& cd, const float* chL,
+                                               const float* chR, int lxf, int q) {
+    int r = (int)reflect1((int64_t)q - p.g.n_fft / 2, lxf);
+    if (p.g.ht_pad) r = (int)reflect1(r - p.g.ht_pad, p.g.Lc);
+    const float a = chunk_sample(p, cd, chL, r);
+    const float b = p.n_channels > 1 ? chunk_sample(p, cd, chR, r) : 0.0f;
+    return make_float2(a, b);
+}
+
+template <int N> __device__ __forceinline__ int ring_slot(int q) {
+    if constexpr ((N & (N - 1)) == 0) return q & (N - 1);
+    else return q % N;
 }
 
 template <int ARCH, int N>
-__global__ void __launch_bounds__(FftCfg<N>::T) fused_kernel(const FusedParams p) {
+__global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(const FusedParams p) {
     constexpr int T = FftCfg<N>::T;
     using Plan = typename FftCfg<N>::Plan;
+    constexpr int R1 = Head<Plan>::first;                 // first forward pass
+    using FwdRest = typename Head<Plan>::tail;
+    using InvInit = typename Init<Plan>::type;            // inverse passes but the last
+    constexpr int RL = Init<Plan>::last, NSL = Init<Plan>::prod;
+    constexpr bool STW = FftCfg<N>::SMEM_TW, SWIN = FftCfg<N>::SMEM_WIN;
     extern __shared__ float4 smem_raw[];
-    float2* buf = reinterpret_cast<float2*>(smem_raw);
-    float* ring = reinterpret_cast<float*>(buf + padded_size(N));   // [2][N]
+    float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
+    float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
+    float2* out_ring = in_ring + N;                       // overlap-add sums (L, R) by position mod N
+    float2* tw_s = out_ring + N;                          // [STW] twiddle table copy
+    float* win_s = reinterpret_cast<float*>(tw_s + (STW ? N : 0));   // [SWIN] window copy
+    int2* btab_s = reinterpret_cast<int2*>(win_s + (SWIN ? N : 0));   // [RoFormer] bin table copy
+    using Tw = std::conditional_t<STW, TwShared, TwGlobal>;
+    const Tw tw{STW ? tw_s : p.tw};
+    const float* win = SWIN ? win_s : p.win;
 
     const int tid = threadIdx.x;
-    const int tile = blockIdx.x, ci = blockIdx.y;
-    const ChunkDesc cd = p.chunks[ci];
-    const FrameGeom G = p.g;
+    const FrameGeom& G = p.g;
     const int hop = G.hop;
-    const int t_begin = tile * p.K;
-    const int t_end = min(G.T, t_begin + p.K);
     const int C = p.n_channels;
     const float* chL = p.mix;
     const float* chR = p.mix + (C > 1 ? p.len : 0);
     const int lxf = G.ht_pad ? G.ht_lxf : G.Lc;
-    const bool last_tile = t_end == G.T;
+    const float half_fwd = 0.5f * p.fwd_scale;
 
-    for (int i = tid; i < 2 * N; i += T) ring[i] = 0.0f;
+    // every stem pass flushes the whole output ring at its last frame, so one zeroing lasts
+    for (int i = tid; i < N; i += T) out_ring[i] = make_float2(0.f, 0.f);
+    if constexpr (STW)
+        for (int i = tid; i < N; i += T) tw_s[i] = __ldg(p.tw + i);
+    if constexpr (SWIN)
+        for (int i = tid; i < N; i += T) win_s[i] = __ldg(p.win + i);
+
+    MaskOp<ARCH, N, T> mk;
+    InPrefetch<T, FftCfg<N>::HOPMAX> nx;
+    if constexpr (ARCH == ARCH_ROFORMER) {
+        for (int i = tid; i < N / 2 + 1; i += T) btab_s[i] = __ldg(p.bin_tab + i);
+        mk.btab = btab_s;
+    }
+
+    // persistent CTAs: work items are (chunk, tile) pairs, tiles of a chunk adjacent
+    for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
+    const int tile = item % p.n_tiles, ci = item / p.n_tiles;
+    const ChunkDesc cd = p.chunks[ci];
+    const int t_begin = tile * p.K;
+    const int t_end = min(G.T, t_begin + p.K);
+    const bool last_tile = t_end == G.T;
 
     for (int s = 0; s < p.S; s++) {
         float* Ys = p.Y + (int64_t)ci * p.y_chunk_stride + (int64_t)s * C * G.Lout;
         float* Trs = p.Tr + (int64_t)ci * p.tr_chunk_stride + ((int64_t)tile * p.S + s) * C * (N - hop);
+        // prologue of a stem pass: the first frame's window and the next frame's new samples
+        {
+            const int q0 = G.first_pos + t_begin * hop;
+            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = frame_sample(p, cd, chL, chR, lxf, q0 + n);
+#pragma unroll
+            for (int k = 0; k < nx.K; k++) {
+                const int u = tid + k * T;
+                if (u < hop && t_begin + 1 < t_end) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + N + u);
+            }
+            if constexpr (FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t_begin, tid);
+        }
+        __syncthreads();
         for (int t = t_begin; t < t_end; t++) {
-            const int64_t q0 = (int64_t)G.first_pos + (int64_t)t * hop;
-            // 1. frame load + window + stereo pack
-            for (int n = tid; n < N; n += T) {
-                int64_t r = reflect1(q0 + n - N / 2, lxf);
-                if (G.ht_pad) r = reflect1(r - G.ht_pad, G.Lc);
-                const float w = __ldg(p.win + n);
-                const float a = chunk_sample(p, cd, chL, r);
-                const float b = C > 1 ? chunk_sample(p, cd, chR, r) : 0.0f;
-                buf[pad_idx(n)] = make_float2(a * w, b * w);
-            }
+            const int q0 = G.first_pos + t * hop;
+            // forward pass 1: windowed frame straight from the input ring
+            pass_io<N, R1, 1, T, false, false>(
+                tw, tid,
+                [&](int j, int r) {
+                    const int n = j + r * (N / R1);
+                    const float2 x = in_ring[ring_slot<N>(q0 + n)];
+                    const float w = SWIN ? win[n] : __ldg(win + n);
+                    return make_float2(x.x * w, x.y * w);
+                },
+                [&](int base, int r, float2 v) { buf[pad_store<R1, 1>(base, r)] = v; });
             __syncthreads();
-            fft<N, T, false>(buf, p.tw, tid, Plan{});
-            // 3. split channels, spectral op, repack as one Hermitian pair
-            for (int f = tid; f <= N / 2; f += T) {
-                const int fm = f == 0 ? 0 : N - f;
-                const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
-                const float2 zl = make_float2(0.5f * p.fwd_scale * (X.x + Xm.x), 0.5f * p.fwd_scale * (X.y - Xm.y));
-                const float2 zr = make_float2(0.5f * p.fwd_scale * (X.y + Xm.y), -0.5f * p.fwd_scale * (X.x - Xm.x));
-                float2 yl, yr;
-                spectral_op<ARCH, N>(p, ci, s, t, f, zl, zr, yl, yr);
-                if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
-                buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
-                if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
-            }
-            __syncthreads();
-            fft<N, T, true>(buf, p.tw, tid, Plan{});
-            // 4. window + overlap-add into the ring
-            for (int n = tid; n < N; n += T) {
-                const float2 v = buf[pad_idx(n)];
-                const float w = __ldg(p.win + n) * p.inv_scale;
-                const int slot = (int)((q0 + n) % N);
-                ring[slot] += v.x * w;
-                ring[N + slot] += v.y * w;
-            }
-            __syncthreads();
-            // 5. flush what no later frame of this tile touches
-            const bool last = t == t_end - 1;
-            const int ny = (last && last_tile) ? N : hop;
-            for (int u = tid; u < N; u += T) {
-                if (u >= ny && !last) break;
-                const int64_t q = q0 + u;
-                const int slot = (int)(q % N);
-                const float v0 = ring[slot], v1 = ring[N + slot];
-                ring[slot] = 0.0f;
-                ring[N + slot] = 0.0f;
-                const int64_t j = q - G.out_offset;
-                const float ie = (j >= 0 && j < G.Lout) ? __ldg(p.inv_env + j) : 0.0f;
-                if (u < ny) {
-                    if (j >= 0 && j < G.Lout) {
-                        Ys[j] = v0 * ie;
-                        if (C > 1) Ys[G.Lout + j] = v1 * ie;
+            // the next frame's new samples replace the ones this frame was the last to use
+            if (t + 1 < t_end) {
+#pragma unroll
+                for (int k = 0; k < nx.K; k++) {
+                    const int u = tid + k * T;
+                    if (u < hop) in_ring[ring_slot<N>(q0 + N + u)] = nx.v[k];
+                }
+                if (t + 2 < t_end) {
+#pragma unroll
+                    for (int k = 0; k < nx.K; k++) {
+                        const int u = tid + k * T;
+                        if (u < hop) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + hop + N + u);
                     }
-                } else {
-                    Trs[u - hop] = v0 * ie;
-                    if (C > 1) Trs[(N - hop) + u - hop] = v1 * ie;
                 }
             }
+            passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
+            // all of this frame's mask loads in flight at once (or already, a frame ahead),
+            // then the spectral op
+            if constexpr (!FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t, tid);
+            // split the channels, apply the stand-in network, repack as one Hermitian pair
+#pragma unroll
+            for (int i = 0; i < MaskOp<ARCH, N, T>::BPT; i++) {
+                const int f = tid + i * T;
+                if (f <= N / 2) {
+                    const int fm = f == 0 ? 0 : N - f;
+                    const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
+                    const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
+                    const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
+                    float2 yl, yr;
+                    mk.apply(p, ci, s, t, f, i, zl, zr, yl, yr);
+                    if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
+                    buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
+                    if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
+                }
+            }
+            if constexpr (FftCfg<N>::AHEAD)
+                if (t + 1 < t_end) mk.prefetch(p, ci, s, t + 1, tid);
             __syncthreads();
+            passes<N, T, true, 1>(buf, tw, tid, InvInit{});
+            // inverse last pass: window and overlap-add straight into the output ring
+            pass_io<N, RL, NSL, T, true, false>(
+                tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
+                [&](int base, int r, float2 v) {
+                    const int n = base + r * NSL;
+                    const float w = (SWIN ? win[n] : __ldg(win + n)) * p.inv_scale;
+                    float2& o = out_ring[ring_slot<N>(q0 + n)];
+                    o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
+                });
+            __syncthreads();
+            // flush what no later frame of this tile touches
+            const bool last = t == t_end - 1;
+            const int ny = (last && last_tile) ? N : hop;
+            const int nflush = last ? N : hop;
+            for (int u = tid; u < nflush; u += T) {
+                const int q = q0 + u;
+                float2& o = out_ring[ring_slot<N>(q)];
+                const float2 v = o;
+                o = make_float2(0.f, 0.f);
+                const int j = q - G.out_offset;
+                const bool in = j >= 0 && j < G.Lout;
+                const float ie = in ? ld_stream(p.inv_env + j) : 0.0f;
+                if (u < ny) {
+                    if (in) {
+                        Ys[j] = v.x * ie;
+                        if (C > 1) Ys[G.Lout + j] = v.y * ie;
+                    }
+                } else {
+                    Trs[u - hop] = v.x * ie;
+                    if (C > 1) Trs[(N - hop) + u - hop] = v.y * ie;
+                }
+            }
+            // the next iteration's first barrier (after forward pass 1) orders these ring
+            // writes before any later read of the same slots
         }
+        __syncthreads();
+    }
     }
 }
 
 // ---- combine ------------------------------------------------------------------------------
-__device__ __forceinline__ float chunk_value(const CombineParams& p, int g, int k, int64_t j) {
-    const FrameGeom& G = p.g;
-    float v = __ldg(p.Y + (int64_t)g * p.y_chunk_stride + (int64_t)k * G.Lout + j);
-    const int64_t q = j + G.out_offset - G.first_pos;
-    const int64_t span = (int64_t)p.K * G.hop;
-    const int64_t tau = q / span;
-    const int64_t u = q - tau * span;
-    if (tau >= 1 && tau < p.n_tiles && u < G.n_fft - G.hop) {
-        const int s = k / p.C, c = k % p.C;
-        v += __ldg(p.Tr + (int64_t)g * p.tr_chunk_stride +
-                   (((tau - 1) * p.S + s) * p.C + c) * (int64_t)(G.n_fft - G.hop) + u);
-    }
-    return v;
-}
-
+// One thread per output sample and SC = stems x channels rows: sum the chunks covering the
+// sample in ascending chunk order (src/roformer.cpp:337-340, src/tfc_tdf.cpp:420-422,
+// src/htdemucs.cpp:598-601), each value the chunk output Y plus, on a tile boundary, the
+// previous tile's trailing partial Tr; divide by the summed weight; epilogue.
+template <int SC>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= p.len) return;
-    const int64_t P = i + p.out_shift;
-    const ChunkDesc c0 = p.chunks[0];
-    int64_t ghi = (P - c0.out0) / p.step_out;
-    if (ghi > p.n_chunks - 1) ghi = p.n_chunks - 1;
-    if (ghi < 0) ghi = 0;
-    const int SC = p.S * p.C;
-    constexpr int MAXK = 16;
-    float acc[MAXK];
+    const FrameGeom& G = p.g;
+    const int P = i + (int)p.out_shift;
+    const int out00 = (int)p.chunks[0].out0;
+    const int step = (int)p.step_out;
+    int ghi = (P - out00) / step;
+    ghi = min(ghi, p.n_chunks - 1);
+    int glo = (P - out00 - (int)p.max_out_len) / step;
+    glo = max(glo, 0);
+    const int span = p.K * G.hop, ov = G.n_fft - G.hop;
+    float acc[SC];
 #pragma unroll
-    for (int k = 0; k < MAXK; k++) acc[k] = 0.0f;
+    for (int k = 0; k < SC; k++) acc[k] = 0.0f;
     float wsum = 0.0f;
-    // chunks are ordered by out0; accumulate in ascending chunk order like the reference
-    int64_t glo = (P - c0.out0 - p.max_out_len) / p.step_out;
-    if (glo < 0) glo = 0;
-    for (int g = (int)glo; g <= (int)ghi + 1 && g < p.n_chunks; g++) {
-        const ChunkDesc d = p.chunks[g];
-        const int64_t u = P - d.out0;
+    for (int g = glo; g <= ghi + 1 && g < p.n_chunks; g++) {
+        const ChunkDesc& d = p.chunks[g];
+        const int u = P - (int)d.out0;
         if (u < 0 || u >= d.out_len) continue;
         const float w = __ldg(p.W + d.w_off + u);
         wsum += w;
+        const int j = d.y_off + u;
+        const float* y = p.Y + (int64_t)g * p.y_chunk_stride + j;
+        // the tile boundary region j falls in, if any
+        const int q = j + G.out_offset - G.first_pos;
+        const int tau = q / span;
+        const int uu = q - tau * span;
+        const float* tr = nullptr;
+        if (tau >= 1 && tau < p.n_tiles && uu < ov)
+            tr = p.Tr + (int64_t)g * p.tr_chunk_stride + (int64_t)(tau - 1) * SC * ov + uu;
 #pragma unroll
-        for (int k = 0; k < MAXK; k++)
-            if (k < SC) acc[k] += w * chunk_value(p, g, k, d.y_off + u);
-    }
-    float outv[MAXK];
-#pragma unroll
-    for (int k = 0; k < MAXK; k++) {
-        if (k < SC) {
-            float v = acc[k] / wsum;
-            if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
-            v *= p.compensate;
-            outv[k] = v;
-            p.out[(int64_t)k * p.len + i] = v;
+        for (int k = 0; k < SC; k++) {
+            float v = __ldg(y + (int64_t)k * G.Lout);
+            if (tr) v += __ldg(tr + k * ov);
+            acc[k] = fmaf(w, v, acc[k]);
         }
     }
-    if (p.complement) {
-        for (int c = 0; c < p.C; c++) {
-            float v = __ldg(p.mix + (int64_t)c * p.len + i);
-            if (p.complement == 1) {
-                v -= outv[c];
-            } else {
+    const float inv = 1.0f / wsum;
+    float outv[SC];
 #pragma unroll
-                for (int k = 0; k < MAXK; k++)
-                    if (k < SC && k % p.C == c) v -= outv[k];
+    for (int k = 0; k < SC; k++) {
+        float v = acc[k] * inv;
+        if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
+        v *= p.compensate;
+        outv[k] = v;
+        p.out[(int64_t)k * p.len + i] = v;
+    }
+    if (p.complement) {
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (c < p.C) {
+                float v = __ldg(p.mix + (int64_t)c * p.len + i);
+#pragma unroll
+                for (int k = 0; k < SC; k++)
+                    if (k % p.C == c && (p.complement == 2 || k < p.C)) v -= outv[k];
+                p.out[(int64_t)(SC + c) * p.len + i] = v;
             }
-            p.out[(int64_t)(SC + c) * p.len + i] = v;
         }
     }
 }
@@ -267,16 +457,59 @@ int fused_threads(int n) {
     }
 }
 
-size_t fused_smem_bytes(int n) {
-    return sizeof(float2) * (size_t)padded_size(n) + sizeof(float) * 2 * (size_t)n;
+template <int ARCH, int N> static size_t smem_bytes_t() {
+    return sizeof(float2) * ((size_t)padded_size(N) + 2 * (size_t)N) +
+           (FftCfg<N>::SMEM_TW ? sizeof(float2) * (size_t)N : 0) +
+           (FftCfg<N>::SMEM_WIN ? sizeof(float) * (size_t)N : 0) +
+           (ARCH == ARCH_ROFORMER ? sizeof(int2) * (size_t)(N / 2 + 2) : 0);
+}
+
+size_t fused_smem_bytes(int arch, int n) {
+    switch (n) {
+        case 2048: return arch == ARCH_ROFORMER ? smem_bytes_t<ARCH_ROFORMER, 2048>() : smem_bytes_t<ARCH_TFC, 2048>();
+        case 4096: return arch == ARCH_ROFORMER ? smem_bytes_t<ARCH_ROFORMER, 4096>() : smem_bytes_t<ARCH_TFC, 4096>();
+        case 7680: return smem_bytes_t<ARCH_TFC, 7680>();
+        default: return 0;
+    }
+}
+
+template <int... Rs> static std::vector<int> radix_vec(RadixList<Rs...>) { return {Rs...}; }
+
+std::vector<int> fused_radices(int n) {
+    switch (n) {
+        case 2048: return radix_vec(FftCfg<2048>::Plan{});
+        case 4096: return radix_vec(FftCfg<4096>::Plan{});
+        case 7680: return radix_vec(FftCfg<7680>::Plan{});
+        default: return {};
+    }
+}
+
+int fused_max_hop(int n) {
+    switch (n) {
+        case 2048: return FftCfg<2048>::HOPMAX;
+        case 4096: return FftCfg<4096>::HOPMAX;
+        case 7680: return FftCfg<7680>::HOPMAX;
+        default: return 0;
+    }
 }
 
 template <int ARCH, int N>
 static cudaError_t launch_fused_t(const FusedParams& p, cudaStream_t st) {
-    const size_t smem = fused_smem_bytes(N);
+    const size_t smem = smem_bytes_t<ARCH, N>();
     cudaError_t e = cudaFuncSetAttribute(fused_kernel<ARCH, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.n_tiles, p.n_chunks);
+    static int per_sm = 0, n_sm = 0;
+    if (!per_sm) {
+        int dev = 0;
+        e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_kernel<ARCH, N>, FftCfg<N>::T, smem);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    }
+    const int64_t items = (int64_t)p.n_tiles * p.n_chunks;
+    const int grid = (int)std::min<int64_t>(items, (int64_t)per_sm * n_sm);
     fused_kernel<ARCH, N><<<grid, FftCfg<N>::T, smem, st>>>(p);
     return cudaGetLastError();
 }
@@ -302,10 +535,23 @@ cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st) {
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
     if (p.len <= 0) return cudaSuccess;
-    if (p.S * p.C > 16) return cudaErrorInvalidValue;
     const int threads = 256;
-    const int64_t blocks = (p.len + threads - 1) / threads;
-    combine_kernel<<<(unsigned)blocks, threads, 0, st>>>(p);
+    const unsigned blocks = (unsigned)((p.len + threads - 1) / threads);
+    switch (p.S * p.C) {
+        case 1: combine_kernel<1><<<blocks, threads, 0, st>>>(p); break;
+        case 2: combine_kernel<2><<<blocks, threads, 0, st>>>(p); break;
+        case 3: combine_kernel<3><<<blocks, threads, 0, st>>>(p); break;
+        case 4: combine_kernel<4><<<blocks, threads, 0, st>>>(p); break;
+        case 5: combine_kernel<5><<<blocks, threads, 0, st>>>(p); break;
+        case 6: combine_kernel<6><<<blocks, threads, 0, st>>>(p); break;
+        case 7: combine_kernel<7><<<blocks, threads, 0, st>>>(p); break;
+        case 8: combine_kernel<8><<<blocks, threads, 0, st>>>(p); break;
+        case 10: combine_kernel<10><<<blocks, threads, 0, st>>>(p); break;
+        case 12: combine_kernel<12><<<blocks, threads, 0, st>>>(p); break;
+        case 14: combine_kernel<14><<<blocks, threads, 0, st>>>(p); break;
+        case 16: combine_kernel<16><<<blocks, threads, 0, st>>>(p); break;
+        default: return cudaErrorInvalidValue;   // S <= 8 and C <= 2 never get here
+    }
     return cudaGetLastError();
 }
 

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace stg {
 
 enum Arch : int { ARCH_ROFORMER = 0, ARCH_HTDEMUCS = 1, ARCH_TFC = 2 };
@@ -55,13 +57,18 @@ struct FusedParams {
     int n_tiles;
     int S;                     // stems
     const float* win;          // periodic Hann [n_fft]
-    const float2* tw;          // W_N^m, m in [0, n_fft)
+    const float2* tw;          // the FFT plan's per-pass twiddles (fft.cuh: twiddle_index)
     const float* inv_env;      // [Lout]: 1 / sum of squared windows, 0 where it vanishes
     float fwd_scale, inv_scale;
     // mask (the stand-in for the network's output), one block per chunk
     const float* mask;
     int64_t mask_chunk_stride;
-    // RoFormer: bin -> (band entry) inverse table, CSR over bins
+    // RoFormer: bin -> (band entry) inverse table. bin_tab[f] holds the first two bands holding
+    // f as (offset without the frame term) / (2C) in bits 0-21 and the band size (bins) in bits
+    // 22-31, 0 when absent; bin_ebeg/bin_ent list every entry (CSR over bins) for the bins that
+    // more than two bands hold (bin_multi).
+    const int2* bin_tab;       // [F] compact entries, see kernels.cu (RoFormer MaskOp)
+    int bin_multi;             // 1 when some bin is held by more than two bands
     const int* bin_ebeg;       // [F + 1]
     const int2* bin_ent;       // (offset of the entry in a stem's mask block without t, din_b)
     const float* bin_inv;      // [F] 1 / max(bands_per_freq, 1)
@@ -102,8 +109,11 @@ struct CombineParams {
 // Launchers. Return a cudaError_t from the launch (kernel errors surface on sync).
 cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
-size_t fused_smem_bytes(int n_fft);
+size_t fused_smem_bytes(int arch, int n_fft);
 int fused_threads(int n_fft);
+int fused_max_hop(int n_fft);      // the largest hop the fused kernel takes at this n_fft
+// The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
+std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
 
 } // namespace stg
