@@ -1,10 +1,10 @@
 #!/usr/bin/env python
 """bench.py -- throughput of the B200 spectral path (chunking -> STFT -> mask -> iSTFT -> OLA).
 
-Metric (BASELINE.json): audio-seconds per second of the whole separation, whole job over
+Metric: audio-seconds per second of the whole separation, whole job over
 all GPUs; plus the fused kernel's achieved HBM bandwidth against the measured peak.
 
-Workload (default ``cfg1``): Mel-Band RoFormer (Kim) front/back
+Workload (default ``cfg1``, the headline configuration): Mel-Band RoFormer (Kim) front/back
 end on 60 s of seeded stereo 44.1 kHz audio: chunks of 352800 samples, num_overlap 4
 (36 chunks), STFT n_fft 2048 / hop 441 (801 frames, 1025 bins), 60 mel bands (1979
 band-bin entries, duplicates averaged), complex mask N(0, 0.5) in the network's band-major
@@ -58,7 +58,7 @@ def load_pkg():
 
 
 def synth_audio(seed, length, channels=2):
-    """BASELINE.json's mix: 8 seeded sines (50-8000 Hz, amp 0.05-0.2) + N(0, 0.01) noise, clipped."""
+    """The benchmark mix: 8 seeded sines (50-8000 Hz, amp 0.05-0.2) + N(0, 0.01) noise, clipped."""
     rng = np.random.default_rng(seed)
     t = np.arange(length, dtype=np.float64) / SR
     out = np.empty((channels, length), np.float32)

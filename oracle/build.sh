@@ -8,7 +8,7 @@
 # Flags follow the reference's Release build (CMakeLists.txt: C++17, CMAKE_BUILD_TYPE Release).
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF_ROOT="${REF_ROOT:-/root/reference}"
+REF_ROOT="${REF_ROOT:-$HERE/../../reference}"
 REF_SRC="${REF_SRC:-$REF_ROOT/src}"
 
 gcc -O2 -std=c11 -fPIC -shared -Wall -Wno-unused-result "$HERE/oracle.c" -o "$HERE/liboracle.so" -lm -lpthread -ldl

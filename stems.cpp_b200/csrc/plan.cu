@@ -1,0 +1,396 @@
+// plan.cu -- see plan.h. Windows, envelopes and twiddles are computed in double with the C
+// library's cos/sin and rounded once to float.
+#include "plan.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+
+namespace stg {
+
+void fail(stg_status code, const std::string& msg) { throw Failure(code, msg); }
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    cudaGetLastError();   // clear a non-sticky launch error so the next call starts clean
+    fail(e == cudaErrorMemoryAllocation ? STG_OUT_OF_MEMORY : STG_INTERNAL_ERROR,
+         std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+
+// ---- STFT tables ----------------------------------------------------------------------------
+std::vector<double> hann_periodic(int n) {                        // src/stft.h:70-74
+    std::vector<double> w(n);
+    for (int i = 0; i < n; i++) w[i] = 0.5 - 0.5 * std::cos(2.0 * M_PI * i / n);
+    return w;
+}
+
+// 1 / sum_t w^2(q - t*hop) over env_frames frames, for the chunk's output samples j
+// (q = j + out_offset); 0 where the sum is not above 1e-11 (src/stft.h:137, 194).
+std::vector<float> inv_envelope(int n_fft, int hop, int env_frames, int out_offset, int Lout) {
+    const std::vector<double> w = hann_periodic(n_fft);
+    std::vector<float> out(Lout);
+    for (int j = 0; j < Lout; j++) {
+        const int64_t q = (int64_t)j + out_offset;
+        int64_t t = (q - n_fft) / hop;
+        if (t < 0) t = 0;
+        double env = 0.0;
+        for (; t < env_frames && t * hop <= q; t++) {
+            const int64_t k = q - t * hop;
+            if (k < n_fft) env += w[k] * w[k];
+        }
+        out[j] = env > 1e-11 ? (float)(1.0 / env) : 0.0f;
+    }
+    return out;
+}
+
+// torch.linspace(a, b, n) in float32 from both ends (src/tfc_tdf.cpp:55-62,
+// src/roformer.cpp:303-309).
+std::vector<float> torch_linspace(float a, float b, int n) {
+    std::vector<float> v(std::max(n, 0));
+    if (n == 1) v[0] = a;
+    if (n < 2) return v;
+    const float step = (b - a) / (float)(n - 1);
+    for (int i = 0; i < n; i++) v[i] = i < n / 2 ? a + step * (float)i : b - step * (float)(n - 1 - i);
+    return v;
+}
+
+// Sizes shared by every arch, and the window-sum envelope of a chunk's output.
+void finish_plan(HostPlan& P, int env_frames) {
+    const int N = P.g.n_fft, hop = P.g.hop;
+    if (!fused_supported(N)) fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
+    if (hop > fused_max_hop(N) || hop > N)
+        fail(STG_UNSUPPORTED, "hop " + std::to_string(hop) + " is too large for n_fft " + std::to_string(N));
+    if (P.K * hop < N - hop) P.K = (N - hop + hop - 1) / hop;   // one tile boundary per sample at most
+    P.n_tiles = (P.g.T + P.K - 1) / P.K;
+    P.y_chunk_stride = (int64_t)P.S * P.C * P.g.Lout;
+    P.tr_chunk_stride = (int64_t)P.n_tiles * P.S * P.C * (N - hop);
+    P.max_out_len = 0;
+    for (const ChunkDesc& c : P.chunks) P.max_out_len = std::max<int64_t>(P.max_out_len, c.out_len);
+    P.env = inv_envelope(N, hop, env_frames, P.g.out_offset, P.g.Lout);
+}
+
+} // namespace
+
+void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
+    const std::vector<double> w = hann_periodic(n);
+    win.assign(w.begin(), w.end());
+    // per-pass tables of the kernel's radix plan: the pass at stride NS (radix R) holds
+    // W_{NS*R}^{k*r} at (NS - 1) + (r - 1)*NS + k (fft.cuh: twiddle_index)
+    tw.assign(n, make_float2(1.0f, 0.0f));
+    int ns = 1;
+    for (int R : fused_radices(n)) {
+        for (int r = 1; r < R; r++)
+            for (int k = 0; k < ns; k++) {
+                const double th = -2.0 * M_PI * (double)k * r / ((double)ns * R);
+                tw[(ns - 1) + (r - 1) * ns + k] = make_float2((float)std::cos(th), (float)std::sin(th));
+            }
+        ns *= R;
+    }
+    if (ns != n) fail(STG_INTERNAL_ERROR, "radix plan does not multiply to n_fft");
+}
+
+// ---- HTDemucs: src/htdemucs.cpp:534-606 ---------------------------------------------------
+void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
+    const int N = 4096, hl = N / 4;                                   // htdemucs.cpp:35-36
+    if (c.n_channels < 1 || c.n_channels > 2 || c.n_sources < 1 || c.n_sources > 8)
+        fail(STG_INVALID_ARGUMENT, "htdemucs: n_channels must be 1..2 and n_sources 1..8");
+    const int seg = c.segment;
+    const int pad = hl / 2 * 3;
+    const int T = (seg + hl - 1) / hl;                                // :320
+    if (seg <= pad || seg <= pad + T * hl - seg)                      // stft.h:59 (reflect_pad)
+        fail(STG_INVALID_ARGUMENT, "htdemucs: segment too short for the reflect pads");
+    const double overlap = c.overlap < 0.0f ? 0.25 : (double)c.overlap;
+    if (!(c.overlap < 1.0f)) fail(STG_INVALID_ARGUMENT, "overlap must be < 1");
+    const int stride = (int)((1.0 - overlap) * seg);                  // :563-565
+    if (stride <= 0) fail(STG_INVALID_ARGUMENT, "overlap must be < 1");
+    P.arch = ARCH_HTDEMUCS;
+    P.C = c.n_channels; P.S = c.n_sources; P.S_out = P.S;
+    P.g = FrameGeom{N, hl, seg, T, 2 * hl, pad, 2 * pad + T * hl, N / 2 + pad, seg};
+    P.fwd_scale = (float)(1.0 / std::sqrt((double)N));                // stft.h:91
+    P.inv_scale = (float)(std::sqrt((double)N) / N);                  // stft.h:116
+    P.reflect_global = 0;                                             // padded(): zeros outside
+    P.mask_per_chunk = (int64_t)P.S * 2 * P.C * (N / 2) * T;
+    for (int64_t off = 0; off < len; off += stride) {                 // :592
+        const int length = (int)std::min<int64_t>(seg, len - off);
+        ChunkDesc d{};
+        d.src0 = off - (seg - length) / 2;                            // :553-554
+        d.valid = seg;
+        d.tail_reflect = 0;
+        d.out0 = off;
+        d.out_len = length;
+        d.y_off = (seg - length) / 2;                                 // center_trim (:597)
+        d.w_off = 0;
+        P.chunks.push_back(d);
+    }
+    std::vector<float>& weight = P.W;                                 // :566-573
+    weight.assign(seg, 0.0f);
+    const int half = seg / 2;
+    for (int i = 0; i < half; i++) weight[i] = (float)(i + 1);
+    for (int i = half; i < seg; i++) weight[i] = (float)(seg - i);
+    const float mx = *std::max_element(weight.begin(), weight.end());
+    for (float& w : weight) w /= mx;
+    P.step_out = stride;
+    P.out_shift = 0;
+    P.nan_to_zero = 0;
+    finish_plan(P, T + 4);                                            // 2 zero frames per side
+}
+
+// ---- RoFormer: src/roformer.cpp:286-357, 394-411, 436-486 -------------------------------
+void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
+    if (c.n_channels < 1 || c.n_channels > 2 || c.n_stems < 1 || c.n_stems > 8)
+        fail(STG_INVALID_ARGUMENT, "roformer: n_channels must be 1..2 and n_stems 1..8");
+    if (c.hop < 1 || c.chunk < 1 || c.chunk % c.hop)
+        fail(STG_MODEL_ERROR, "roformer: chunk_size is not a multiple of the hop");   // :396
+    if (c.n_bands < 1 || !c.band_sizes || !c.band_freqs) fail(STG_MODEL_ERROR, "roformer: no band table");
+    if (!(c.overlap < 1.0f)) fail(STG_INVALID_ARGUMENT, "overlap must be < 1");           // :440
+    if (c.overlap < 0.0f && c.num_overlap < 1) fail(STG_MODEL_ERROR, "roformer: num_overlap < 1");
+    const int N = c.n_fft, hop = c.hop, Cc = c.chunk, F = N / 2 + 1;
+    const int step = c.overlap < 0.0f ? Cc / c.num_overlap
+                                      : std::max(1, (int)std::lround(Cc * (1.0 - c.overlap)));   // :442-443
+    if (step < 1) fail(STG_INVALID_ARGUMENT, "roformer: step < 1");
+    if (Cc <= N / 2) fail(STG_INVALID_ARGUMENT, "roformer: chunk shorter than the STFT reflect pad");
+    P.arch = ARCH_ROFORMER;
+    P.C = c.n_channels; P.S = c.n_stems; P.S_out = P.S + (c.complement ? 1 : 0);
+    const int T = Cc / hop + 1;                                       // :83
+    P.g = FrameGeom{N, hop, Cc, T, 0, 0, 0, N / 2, hop * (T - 1)};
+    P.fwd_scale = c.normalized ? (float)(1.0 / std::sqrt((double)N)) : 1.0f;
+    P.inv_scale = (float)((c.normalized ? std::sqrt((double)N) : 1.0) / N);
+    P.zero_dc = c.zero_dc != 0;
+    // band table (:394-411) -> per-bin inverse table
+    std::vector<int> bpf(F, 0);
+    std::vector<std::vector<int2>> per_bin(F);
+    int64_t off = 0, foff = 0;
+    for (int b = 0; b < c.n_bands; b++) {
+        const int sz = c.band_sizes[b];
+        if (sz < 1) fail(STG_MODEL_ERROR, "roformer: empty band");
+        const int din = sz * P.C * 2;                                 // :85
+        if (din > 0xffff) fail(STG_UNSUPPORTED, "roformer: band too wide");
+        for (int j = 0; j < sz; j++) {
+            const int f = c.band_freqs[foff + j];
+            if (f < 0 || f >= F) fail(STG_MODEL_ERROR, "roformer: band frequency out of range");
+            bpf[f]++;
+            per_bin[f].push_back(make_int2((int)(off * T + (int64_t)j * P.C * 2), din));
+        }
+        foff += sz;
+        off += din;
+    }
+    if (off * T > INT32_MAX) fail(STG_UNSUPPORTED, "roformer: band table too large");
+    P.stem_stride = off * T;
+    P.mask_per_chunk = (int64_t)P.S * P.stem_stride;
+    std::vector<int>& ebeg = P.ebeg;
+    std::vector<int2>& ent = P.ent;
+    std::vector<float>& binv = P.binv;
+    ebeg.assign(F + 1, 0);
+    binv.assign(F, 0.0f);
+    // bin_tab[f]: the first two bands holding f, each as (entry offset without the frame term)
+    // / (2C) in bits 0-21 | band size in bits 22-31; 0 when absent. A bin no band holds gets
+    // weight 0: its mask average is 0 / 1 (src/roformer.cpp:272).
+    std::vector<int2>& btab = P.btab;
+    btab.assign(F, make_int2(0, 0));
+    int multi = 0;
+    for (int f = 0; f < F; f++) {
+        ebeg[f] = (int)ent.size();
+        ent.insert(ent.end(), per_bin[f].begin(), per_bin[f].end());
+        binv[f] = per_bin[f].empty() ? 0.0f : (float)(1.0 / bpf[f]);
+        const size_t n = per_bin[f].size();
+        int v[2] = {0, 0};
+        for (size_t k = 0; k < n && k < 2; k++) {
+            const int units = per_bin[f][k].x / (P.C * 2), size = per_bin[f][k].y / (P.C * 2);
+            if (units >= (1 << 22) || size >= (1 << 10)) fail(STG_UNSUPPORTED, "roformer: band table too large");
+            v[k] = (int)((unsigned)units | ((unsigned)size << 22));
+        }
+        btab[f] = make_int2(v[0], v[1]);
+        if (n > 2) multi = 1;
+    }
+    P.bin_multi = multi;
+    ebeg[F] = (int)ent.size();
+    // chunking (:288-341)
+    const int fade = Cc / 10, border = Cc - step;
+    const bool pad = len > 2 * (int64_t)border && border > 0;
+    const int64_t Lp = pad ? len + 2 * (int64_t)border : len;
+    std::vector<float> fade_in(std::max(fade, 0), 0.0f);
+    if (fade > 1) {
+        const float stp = 1.0f / (float)(fade - 1);
+        for (int i = 0; i < fade; i++) fade_in[i] = i < fade / 2 ? (float)i * stp : 1.0f - (float)(fade - 1 - i) * stp;
+    }
+    std::vector<float> window(Cc, 1.0f);
+    for (int i = 0; i < fade; i++) { window[i] *= fade_in[i]; window[Cc - 1 - i] *= fade_in[i]; }
+    // weight tables: [normal][first][last]
+    std::vector<float>& W = P.W;
+    W.assign((size_t)3 * Cc, 0.0f);
+    for (int v = 0; v < 3; v++) {
+        float* w = &W[(size_t)v * Cc];
+        std::copy(window.begin(), window.end(), w);
+        if (v == 1) std::fill(w, w + fade, 1.0f);                     // :335
+        if (v == 2) std::fill(w + Cc - fade, w + Cc, 1.0f);           // :336
+    }
+    for (int64_t i = 0; i < Lp; i += step) {                          // :317
+        const int length = (int)std::min<int64_t>(Cc, Lp - i);
+        ChunkDesc d{};
+        d.src0 = i - (pad ? border : 0);
+        d.valid = length;
+        d.tail_reflect = length < Cc && length > Cc / 2 + 1;          // :323-330
+        d.out0 = i;
+        d.out_len = length;
+        d.y_off = 0;
+        d.w_off = i == 0 ? Cc : (i + Cc >= Lp ? 2 * Cc : 0);
+        P.chunks.push_back(d);
+    }
+    P.reflect_global = pad;
+    P.step_out = step;
+    P.out_shift = pad ? border : 0;                                   // :344
+    P.nan_to_zero = 1;                                                // :348
+    P.complement = c.complement ? 1 : 0;                              // :481-485
+    P.K = 16;
+    finish_plan(P, T);
+}
+
+// ---- TFC-TDF: src/tfc_tdf.cpp:398-495, 570-598 -------------------------------------------
+void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len) {
+    if (c.n_stems < 1 || c.n_stems > 7) fail(STG_INVALID_ARGUMENT, "tfc_tdf: n_stems must be 1..7");
+    const int N = c.n_fft, hop = c.hop;
+    if (N < 16 || N % 2 || hop < 1 || hop > N || c.dim_f < 1 || c.dim_f > N / 2 + 1 || c.dim_t < 2 ||
+        c.zero_bins < 0 || c.zero_bins > c.dim_f || (c.chunking != 0 && c.chunking != 1) ||
+        (c.chunking == 1 && c.num_overlap < 1) || !std::isfinite(c.compensate) || c.compensate <= 0)
+        fail(STG_MODEL_ERROR, "tfc_tdf: invalid configuration");      // :537-549
+    if (!(c.overlap < 1.0f)) fail(STG_INVALID_ARGUMENT, "overlap must be < 1");
+    const int Cc = hop * (c.dim_t - 1);                               // :94
+    if (Cc <= N / 2) fail(STG_MODEL_ERROR, "tfc_tdf: chunk shorter than the FFT");
+    P.arch = ARCH_TFC;
+    P.C = 2; P.S = c.n_stems; P.S_out = P.S + (c.complement ? 1 : 0);
+    P.g = FrameGeom{N, hop, Cc, c.dim_t, 0, 0, 0, N / 2, Cc};
+    P.fwd_scale = 1.0f;
+    P.inv_scale = (float)(1.0 / N);
+    P.dim_f = c.dim_f;
+    P.zero_bins = c.chunking == 0 ? c.zero_bins : 0;                  // :532
+    P.mask_per_chunk = (int64_t)4 * P.S * c.dim_f * c.dim_t;
+    std::vector<float>& W = P.W;
+    if (c.chunking == 0) {                                            // demix_uvr :398-429
+        const int trim = N / 2, gen = Cc - 2 * trim;
+        if (gen <= 0) fail(STG_MODEL_ERROR, "tfc_tdf: chunk shorter than the FFT");
+        const int64_t M = (int64_t)trim + len + gen + trim - len % gen;
+        const int64_t step = c.overlap < 0 ? Cc - N : (int64_t)((1.0 - (double)c.overlap) * Cc);
+        if (step <= 0) fail(STG_INVALID_ARGUMENT, "overlap too large for this model");
+        std::map<int, int> table_of;   // chunk length -> offset of its np.hanning table
+        for (int64_t i = 0; i < M; i += step) {
+            const int actual = (int)std::min<int64_t>(Cc, M - i);
+            auto it = table_of.find(actual);
+            if (it == table_of.end()) {
+                const int o = (int)W.size();
+                for (int k = 0; k < actual; k++)                      // np.hanning (:65-70), or ones
+                    W.push_back(c.overlap == 0 || actual == 1 ? 1.0f
+                                : (float)(0.5 - 0.5 * std::cos(2.0 * M_PI * k / (actual - 1))));
+                it = table_of.emplace(actual, o).first;
+            }
+            ChunkDesc d{};
+            d.src0 = i - trim;
+            d.valid = actual;
+            d.tail_reflect = 0;
+            d.out0 = i;
+            d.out_len = actual;
+            d.y_off = 0;
+            d.w_off = it->second;
+            P.chunks.push_back(d);
+        }
+        P.reflect_global = 0;
+        P.step_out = step;
+        P.out_shift = trim;
+        P.nan_to_zero = 0;
+    } else {                                                          // demix_msst :434-495
+        const int step = c.overlap < 0 ? Cc / c.num_overlap
+                                       : std::max(1, (int)std::lround(Cc * (1.0 - c.overlap)));
+        const int fade = Cc / 10, border = Cc - step;
+        const bool pad = len > 2 * (int64_t)border && border > 0;
+        const int64_t Lp = pad ? len + 2 * (int64_t)border : len;
+        std::vector<float> window(Cc, 1.0f);
+        if (fade > 0) {
+            const std::vector<float> in = torch_linspace(0, 1, fade), out = torch_linspace(1, 0, fade);
+            std::copy(out.begin(), out.end(), window.end() - fade);
+            std::copy(in.begin(), in.end(), window.begin());
+        }
+        W.resize((size_t)3 * Cc);
+        for (int v = 0; v < 3; v++) {
+            float* w = &W[(size_t)v * Cc];
+            std::copy(window.begin(), window.end(), w);
+            if (v == 1) std::fill(w, w + fade, 1.0f);                 // :480
+            if (v == 2) std::fill(w + Cc - fade, w + Cc, 1.0f);       // :481
+        }
+        for (int64_t i = 0; i < Lp; i += step) {
+            const int n = (int)std::min<int64_t>(Cc, Lp - i);
+            ChunkDesc d{};
+            d.src0 = i - (pad ? border : 0);
+            d.valid = n;
+            d.tail_reflect = n < Cc && n > Cc / 2;                    // :467-474
+            d.out0 = i;
+            d.out_len = n;
+            d.y_off = 0;
+            d.w_off = i == 0 ? Cc : (i + step >= Lp ? 2 * Cc : 0);
+            P.chunks.push_back(d);
+        }
+        P.reflect_global = pad;
+        P.step_out = step;
+        P.out_shift = pad ? border : 0;
+        P.nan_to_zero = 1;
+    }
+    P.compensate = c.compensate;                                      // :586-587
+    P.complement = c.complement ? 2 : 0;                              // :588-596
+    P.K = 16;
+    finish_plan(P, c.dim_t);
+}
+
+void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
+                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing) {
+    if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+    if (reinterpret_cast<uintptr_t>(d_mask) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+    FusedParams f{};
+    f.mix = d_mix; f.len = P.len; f.n_channels = P.C; f.reflect_global = P.reflect_global;
+    f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
+    f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
+    f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
+    f.mask_chunk_stride = P.mask_per_chunk;
+    f.bin_tab = D.btab;
+    f.bin_multi = P.bin_multi;
+    f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
+    f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
+    f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
+    f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+    const int G = (int)P.chunks.size();
+    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : G;
+    const bool timed = timing && timing->timed;
+    if (timing) timing->launches = 0;
+    if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
+    for (int b0 = 0; b0 < G; b0 += per) {
+        if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
+        const int nb = std::min(per, G - b0);
+        f.chunks = D.chunks + b0;
+        f.n_chunks = nb;
+        f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
+        f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
+        f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
+        cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+        if (timing) timing->launches++;
+        if (opt && opt->on_progress) {
+            cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
+            opt->on_progress(opt->user, b0 + nb, G);
+        }
+    }
+    CombineParams c{};
+    c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
+    c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
+    c.chunks = D.chunks; c.n_chunks = G;
+    c.step_out = P.step_out; c.max_out_len = P.max_out_len;
+    c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
+    c.W = D.W;
+    c.S = P.S; c.C = P.C; c.len = P.len; c.out_shift = P.out_shift;
+    c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
+    c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    if (timed) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
+    cuda_check(launch_combine(c, st), "combine kernel launch");
+    if (timing) timing->launches++;
+    if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
+}
+
+} // namespace stg

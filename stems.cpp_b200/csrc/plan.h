@@ -1,0 +1,93 @@
+// plan.h -- host-side schedule of one separation, independent of where its tables live.
+//
+// build_* restate, for one model configuration and one track length, what each reference
+// separator computes on the host before and around its chunk loop:
+//   HTDemucs   src/htdemucs.cpp:534-606  (segments, centre padding, triangular weight)
+//   RoFormer   src/roformer.cpp:286-357  (reflect-padded borders, linear fades, tails)
+//   TFC-TDF    src/tfc_tdf.cpp:398-495   (UVR trim + np.hanning, or MSST fades)
+// into a HostPlan (chunk table, weight tables, window-sum envelope, band tables). The caller
+// copies the tables to device memory it owns (engine.cu: buffers per plan; noalloc.cu: a
+// static arena) and launch_plan runs the kernels on those copies.
+#pragma once
+#include "../../include/stems_gpu_v1.h"
+#include "kernels.h"
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace stg {
+
+// Errors thrown by the host code and mapped to a stg_status at the C ABI.
+struct Failure : std::runtime_error {
+    stg_status code;
+    Failure(stg_status c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+[[noreturn]] void fail(stg_status code, const std::string& msg);
+void cuda_check(cudaError_t e, const char* what);
+
+struct HostPlan {
+    int arch = 0;
+    int64_t len = 0;
+    int C = 2, S = 1, S_out = 1;
+    int64_t mask_per_chunk = 0;
+    std::vector<ChunkDesc> chunks;
+    FrameGeom g{};
+    int K = 16, n_tiles = 0;
+    float fwd_scale = 1.0f, inv_scale = 1.0f;
+    int reflect_global = 0;
+    int64_t step_out = 1, out_shift = 0, max_out_len = 0;
+    int nan_to_zero = 0, complement = 0;
+    float compensate = 1.0f;
+    int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
+    int64_t stem_stride = 0;
+    int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
+    std::vector<float> W;          // crossfade weight tables (ChunkDesc::w_off)
+    std::vector<float> env;        // inverse window-sum envelope of a chunk's output
+    std::vector<int2> btab;        // RoFormer bin table (kernels.h: FusedParams::bin_tab)
+    std::vector<int> ebeg;         // RoFormer CSR over bins
+    std::vector<int2> ent;
+    std::vector<float> binv;
+
+    int64_t n_chunks() const { return (int64_t)chunks.size(); }
+    int64_t out_floats() const { return (int64_t)S_out * C * len; }
+    size_t y_bytes() const { return sizeof(float) * (size_t)y_chunk_stride * chunks.size(); }
+    size_t tr_bytes() const { return sizeof(float) * (size_t)tr_chunk_stride * chunks.size(); }
+};
+
+// Where the device copies of a plan's tables and scratch live.
+struct PlanDevice {
+    const ChunkDesc* chunks = nullptr;
+    const float* W = nullptr;
+    const float* env = nullptr;
+    const int2* btab = nullptr;
+    const int* ebeg = nullptr;
+    const int2* ent = nullptr;
+    const float* binv = nullptr;
+    const float* win = nullptr;    // periodic Hann [n_fft]
+    const float2* tw = nullptr;    // FFT twiddles (fft_tables)
+    float* Y = nullptr;            // scratch: chunk outputs
+    float* Tr = nullptr;           // scratch: tile-boundary partials
+};
+
+void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
+void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len);
+void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len);
+
+// The window and twiddle tables the fused kernel reads for n_fft (host copies).
+void fft_tables(int n_fft, std::vector<float>& win, std::vector<float2>& tw);
+
+// Optional timing of one run: events recorded on the run's stream around the kernels.
+struct RunTiming {
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // fused start, fused end, combine end
+    bool timed = false;
+    int launches = 0;
+};
+
+// Run a separation on device buffers with the plan's device tables: the fused kernel over
+// chunk batches (progress and cancellation between batches), then the combine.
+void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
+                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing);
+
+} // namespace stg

@@ -1,4 +1,4 @@
-"""Helpers shared by the tests: parity metrics and BASELINE.json's synthetic inputs."""
+"""Helpers shared by the tests: parity metrics and the benchmark's synthetic inputs."""
 from __future__ import annotations
 
 import numpy as np
@@ -27,7 +27,7 @@ def snr_db(got, want):
 
 
 def synth_audio(seed, length, channels=2, sr=44100):
-    """BASELINE.json's synthetic mix: per channel 8 seeded sines (50-8000 Hz, amplitude
+    """The benchmark's synthetic mix: per channel 8 seeded sines (50-8000 Hz, amplitude
     0.05-0.2, random phase) plus white noise sigma 0.01, clipped to [-1, 1]."""
     rng = np.random.default_rng(seed)
     t = np.arange(length, dtype=np.float64) / sr

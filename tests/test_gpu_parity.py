@@ -1,7 +1,7 @@
 """GPU parity: the fused CUDA path, called through the C ABI, against the CPU oracle.
 
-Bar: per stem, max |got - ref| / max |ref| <= 1e-5, and the SNR
-is reported as well. Inputs are seeded synthetic audio and masks;
+Bar: per stem, max |got - ref| / max |ref| <= 1e-5 (the SNR is reported as well). Inputs
+are seeded synthetic audio and masks of the benchmark configurations' kind;
 sizes here keep the oracle to seconds.
 """
 from __future__ import annotations
