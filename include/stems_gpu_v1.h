@@ -192,6 +192,31 @@ typedef struct {
 STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream, const stg_run_options* options);
 
+/* ---- a separation that allocates no device memory ---------------------------------------- */
+
+/* No counterpart in the reference: the reference runs this path on the host.
+ *
+ * For callers that cannot call cudaMalloc: plug-ins hosted inside an audio application that
+ * owns the CUDA context and hands out all device memory itself, and real-time code that must
+ * not block on the device allocator. The caller passes the mix, the masks and the output
+ * (device buffers, same layouts as stg_separate with a RoFormer plan); everything else the
+ * separation needs, its tables and the fused kernel's scratch, lives in one static device
+ * array of 64 MiB that every GPU loading this library reserves until the process exits.
+ * With 352800-sample chunks of a stereo one-stem model that is 16 chunks: a 20 s track at
+ * num_overlap 4, 56 s at num_overlap 2. Longer inputs are rejected with
+ * STG_INVALID_ARGUMENT and a message saying how much they need.
+ *
+ * The first call on a device looks up the array's device address; make that first call
+ * before capturing the stream into a CUDA graph. Every call writes the same array (the
+ * fused kernel writes all the scratch a call reads, so nothing needs clearing), so calls that
+ * overlap on the GPU, for instance on two streams of the same device, race: serialise them.
+ * Asynchronous on `stream`; `message` (optional, message_size bytes) receives the reason for
+ * a failure. `device` is made current for the call and the previous device restored. */
+STG_API stg_status stg_separate_roformer_noalloc(int device, const stg_roformer_config* config,
+                                                 int64_t n_samples, const float* d_mix,
+                                                 const float* d_mask, float* d_out, void* stream,
+                                                 char* message, size_t message_size);
+
 #ifdef __cplusplus
 }
 #endif

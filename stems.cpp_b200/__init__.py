@@ -94,6 +94,8 @@ _SIGNATURES = {
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.POINTER(RunOptions)]),
+    "stg_separate_roformer_noalloc": (C.c_int32, [C.c_int, C.POINTER(RoFormerConfig), C.c_int64, C.c_void_p,
+                                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
 }
 
 _lib = None
