@@ -49,6 +49,8 @@ WORKLOADS = {
     "cfg3": dict(arch="tfc", seconds=180, n_fft=7680, hop=1024, dim_f=3072, dim_t=256, zero_bins=3,
                  overlap=0.5, sigma=1.0, seed=3,
                  desc="MDX TFC-TDF (Kim_Vocal_2) framing, 180 s stereo, n_fft 7680, UVR 50% overlap"),
+    "cfg4": dict(arch="htdemucs", seconds=240, segment=343980, sources=4, sigma=1.0, seed=4, tracks=64,
+                 desc="batch of 64 tracks of 240 s through the HTDemucs spectral path, round-robin over GPUs"),
 }
 
 
@@ -211,7 +213,7 @@ def run_reference(args, w, rank):
     mix = synth_audio(w["seed"], length)
     n_chunks = _n_chunks(w, length)
     n_sample = max(1, min(n_chunks, threads))
-    mask = _host_mask(w, length, n_chunks)
+    mask = _host_mask(w, n_sample)
     times, kind = [], "port"
     for k in range(args.warmup + args.steps):
         dt, kind = cpu_run(w, length, mix, mask, n_sample, threads)
@@ -254,7 +256,8 @@ def _mask_floats_per_chunk(w):
     return 4 * w["dim_f"] * w["dim_t"]
 
 
-def _host_mask(w, length, n_chunks):
+def _host_mask(w, n_chunks):
+    """Masks for the first n_chunks chunks (the CPU legs only touch the chunks they time)."""
     rng = np.random.default_rng(w["seed"] + 1000)
     n = n_chunks * _mask_floats_per_chunk(w)
     return (w["sigma"] * rng.standard_normal(n, dtype=np.float32)).astype(np.float32)
@@ -284,15 +287,20 @@ def run_ours(args, w, rank, world, local_rank):
             dist.barrier(device_ids=[local_rank])
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return pkg.sharding.max_over_ranks(x, device=dev)
+
+    # tracks this rank separates per step: one replica of the single-track workloads, or its
+    # round-robin share of a batch (the buffers are reused; the kernels do not look at values)
+    n_tracks = w.get("tracks", world)
+    mine = len(pkg.sharding.tracks_for_rank(n_tracks, rank, world))
+
+    def step():
+        for _ in range(mine):
+            plan.separate(d_mix, d_mask, d_out, stream=stream)
 
     def timed_region():
         for _ in range(args.warmup):
-            plan.separate(d_mix, d_mask, d_out, stream=stream)
+            step()
         torch.cuda.synchronize(dev)
         barrier()
         torch.cuda.synchronize(dev)
@@ -300,7 +308,7 @@ def run_ours(args, w, rank, world, local_rank):
         with ClockSampler(local_rank) as clk:
             e0.record(stream)
             for _ in range(args.steps):
-                plan.separate(d_mix, d_mask, d_out, stream=stream)
+                step()
             e1.record(stream)
             torch.cuda.synchronize(dev)
         barrier()
@@ -341,7 +349,7 @@ def run_ours(args, w, rank, world, local_rank):
     e2e_s = max_over_ranks(e2e_s)
     barrier()
 
-    audio_s = w["seconds"] * world
+    audio_s = w["seconds"] * n_tracks
     value = audio_s / (ms / 1e3)
     peak, peak_kind = measured_peak()
     fbytes = fused_algorithmic_bytes(plan, w)
@@ -354,7 +362,7 @@ def run_ours(args, w, rank, world, local_rank):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded sines + noise; N(0, sigma) masks standing in for the network)",
-            "config": {"workload": args.workload, "desc": w["desc"], "tracks_per_step_per_gpu": 1,
+            "config": {"workload": args.workload, "desc": w["desc"], "tracks_per_step": n_tracks,
                        "chunks_per_track": plan.n_chunks, "frames_per_chunk": plan.n_frames,
                        "mask_bytes_per_track": 4 * plan.mask_floats,
                        "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"replicas x{world}"},
@@ -365,10 +373,10 @@ def run_ours(args, w, rank, world, local_rank):
             "path": {"algorithmic_bytes_per_step": path_algorithmic_bytes(plan, w),
                      "gbs": path_algorithmic_bytes(plan, w) / (ms / 1e3) / 1e9},
             "clocks": dict(clk.summary(), remeasured=remeasured),
-            "e2e": {"value": audio_s / e2e_s, "unit": "audio-s/s",
+            "e2e": {"value": w["seconds"] * world / e2e_s, "unit": "audio-s/s",
                     "h2d_bytes_per_step": 4 * (plan.n_channels * plan.n_samples + plan.mask_floats),
                     "d2h_bytes_per_step": 4 * plan.out_floats},
-            "gpu_launches": n_launch * args.steps,
+            "gpu_launches": n_launch * args.steps * mine,
         }
     plan.close()
     eng.close()
@@ -413,7 +421,7 @@ def main():
             n_chunks = _n_chunks(w, length)
             n_sample = max(1, min(n_chunks, 2 * threads))
             mix = synth_audio(w["seed"], length)
-            dt, kind = cpu_run(w, length, mix, _host_mask(w, length, n_chunks), n_sample, threads)
+            dt, kind = cpu_run(w, length, mix, _host_mask(w, n_sample), n_sample, threads)
             line["cpu_baseline"] = {"value": n_sample * (w["seconds"] / n_chunks) / dt, "unit": "audio-s/s",
                                     "cores": threads, "kind": kind,
                                     "sample": f"{n_sample} of {n_chunks} chunks of one {w['seconds']} s track"}

@@ -18,6 +18,7 @@ import os
 import numpy as np
 
 from . import bands  # noqa: F401  (band tables for RoFormer configurations)
+from . import sharding  # noqa: F401  (work split across GPUs)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libstems_gpu.so")
