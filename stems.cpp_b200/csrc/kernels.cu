@@ -31,18 +31,21 @@ namespace stg {
 template <int N> struct FftCfg;
 template <> struct FftCfg<2048> {
     static constexpr int T = 128, MINB = 3, HOPMAX = 512;
+    static constexpr int PF_GROUPS = 1;     // mask loads issued in this many groups
     static constexpr bool AHEAD = false;    // mask loads issued one frame ahead
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;   // table copies in shared memory
     using Plan = RadixList<8, 16, 16>;
 };
 template <> struct FftCfg<4096> {
     static constexpr int T = 256, MINB = 2, HOPMAX = 1024;
+    static constexpr int PF_GROUPS = 1;
     static constexpr bool AHEAD = false;
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;
     using Plan = RadixList<16, 16, 16>;
 };
 template <> struct FftCfg<7680> {
     static constexpr int T = 512, MINB = 1, HOPMAX = 1024;
+    static constexpr int PF_GROUPS = 1;
     static constexpr bool AHEAD = false;
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;
     using Plan = RadixList<15, 8, 8, 8>;
@@ -96,7 +99,9 @@ template <int ARCH, int N, int T> struct MaskOp {
 
     const int2* btab;   // RoFormer: the bin table's copy in shared memory
 
-    __device__ __forceinline__ void prefetch(const FusedParams& p, int ci, int s, int t, int tid) {
+    // Issue the mask loads of the bin slots [i0, i1) (compile-time constants at every call).
+    __device__ __forceinline__ void prefetch(const FusedParams& p, int ci, int s, int t, int tid,
+                                             int i0 = 0, int i1 = BPT) {
         const float* __restrict__ m = p.mask + (int64_t)ci * p.mask_chunk_stride;
         if constexpr (ARCH == ARCH_ROFORMER) {
             // src/roformer.cpp:256-269: band b's mask for frame t is the row
@@ -104,6 +109,7 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + (int64_t)s * p.stem_stride;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
+                if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 inv[i] = 0.0f;
@@ -134,6 +140,7 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + (int64_t)s * 2 * p.n_channels * plane + t;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
+                if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (f < F) {
@@ -152,6 +159,7 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + (int64_t)s * 4 * plane + t;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
+                if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (f >= p.zero_bins && f < p.dim_f) {
@@ -316,10 +324,16 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
             // all of this frame's mask loads in flight at once (or already, a frame ahead),
             // then the spectral op
-            if constexpr (!FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t, tid);
+            // (in PF_GROUPS groups of bin slots, the next group's loads issued before the
+            // current group is applied, to bound the registers they hold)
+            constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
+            constexpr int NG = FftCfg<N>::PF_GROUPS, PER = (BPT + NG - 1) / NG;
+            if constexpr (!FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t, tid, 0, PER);
             // split the channels, apply the stand-in network, repack as one Hermitian pair
 #pragma unroll
-            for (int i = 0; i < MaskOp<ARCH, N, T>::BPT; i++) {
+            for (int i = 0; i < BPT; i++) {
+                if constexpr (!FftCfg<N>::AHEAD)
+                    if (i % PER == 0 && i + PER < BPT) mk.prefetch(p, ci, s, t, tid, i + PER, i + 2 * PER);
                 const int f = tid + i * T;
                 if (f <= N / 2) {
                     const int fm = f == 0 ? 0 : N - f;
@@ -482,6 +496,38 @@ std::vector<int> fused_radices(int n) {
         case 7680: return radix_vec(FftCfg<7680>::Plan{});
         default: return {};
     }
+}
+
+template <int ARCH, int N> static int resident_t() {
+    int per_sm = 0, n_sm = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(fused_kernel<ARCH, N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bytes_t<ARCH, N>()) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_kernel<ARCH, N>, FftCfg<N>::T,
+                                                      smem_bytes_t<ARCH, N>()) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return per_sm * n_sm;
+}
+
+int fused_resident_ctas(int arch, int n) {
+    switch (arch) {
+        case ARCH_ROFORMER:
+            if (n == 2048) return resident_t<ARCH_ROFORMER, 2048>();
+            if (n == 4096) return resident_t<ARCH_ROFORMER, 4096>();
+            break;
+        case ARCH_HTDEMUCS:
+            if (n == 4096) return resident_t<ARCH_HTDEMUCS, 4096>();
+            break;
+        case ARCH_TFC:
+            if (n == 7680) return resident_t<ARCH_TFC, 7680>();
+            if (n == 4096) return resident_t<ARCH_TFC, 4096>();
+            if (n == 2048) return resident_t<ARCH_TFC, 2048>();
+            break;
+    }
+    return 0;
 }
 
 int fused_max_hop(int n) {

@@ -112,6 +112,8 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 size_t fused_smem_bytes(int arch, int n_fft);
 int fused_threads(int n_fft);
 int fused_max_hop(int n_fft);      // the largest hop the fused kernel takes at this n_fft
+// CTAs of the fused kernel resident at once on the current device (0 when unknown).
+int fused_resident_ctas(int arch, int n_fft);
 // The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);

@@ -63,6 +63,11 @@ void finish_plan(HostPlan& P, int env_frames) {
     if (!fused_supported(N)) fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
     if (hop > fused_max_hop(N) || hop > N)
         fail(STG_UNSUPPORTED, "hop " + std::to_string(hop) + " is too large for n_fft " + std::to_string(N));
+    // Frames per tile: 16, halved while the plan has fewer than two work items (chunk, tile)
+    // per resident CTA, so that short inputs still fill the GPU.
+    const int slots = fused_resident_ctas(P.arch, N);
+    P.K = 16;
+    while (P.K > 4 && (int64_t)P.chunks.size() * ((P.g.T + P.K - 1) / P.K) < 2 * (int64_t)slots) P.K /= 2;
     if (P.K * hop < N - hop) P.K = (N - hop + hop - 1) / hop;   // one tile boundary per sample at most
     P.n_tiles = (P.g.T + P.K - 1) / P.K;
     P.y_chunk_stride = (int64_t)P.S * P.C * P.g.Lout;
@@ -244,7 +249,6 @@ void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
     P.out_shift = pad ? border : 0;                                   // :344
     P.nan_to_zero = 1;                                                // :348
     P.complement = c.complement ? 1 : 0;                              // :481-485
-    P.K = 16;
     finish_plan(P, T);
 }
 
@@ -337,7 +341,6 @@ void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len) {
     }
     P.compensate = c.compensate;                                      // :586-587
     P.complement = c.complement ? 2 : 0;                              // :588-596
-    P.K = 16;
     finish_plan(P, c.dim_t);
 }
 
