@@ -192,6 +192,67 @@ typedef struct {
 STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream, const stg_run_options* options);
 
+/* ---- the halves around a real network --------------------------------------------------- */
+
+/* The same separation with the network between the halves, as the reference runs it: for
+ * each batch of chunks, the front half writes the network's input, the network runs, the
+ * back half reads the network's output; once every chunk went through the back half,
+ * stg_finish overlap-adds the chunks into the result.
+ *   HTDemucs  input  in_x  [2C][2048][T] float CaC planes (src/htdemucs.cpp:423-433, before
+ *                    the mean/std normalisation of :434-436);
+ *             output ox    [S][2C][2048][T] (:463-469, after the denormalisation).
+ *   RoFormer  input  feat  [sum_b din_b * T] band-major (src/roformer.cpp:226-241);
+ *             output the per-band masks, the plan's mask layout (:251-269).
+ *   TFC-TDF   input  in    [4][dim_f][T], bins below zero_bins 0 (src/tfc_tdf.cpp:366-376);
+ *             output y     [4S][dim_f][T] (:381-387).
+ * Chunk k of a batch starting at first_chunk sits at k * (floats per chunk) in the buffers. */
+typedef struct {
+    uint32_t size;
+    int64_t net_in_floats_per_chunk;
+    int64_t net_out_floats_per_chunk;
+} stg_network_info;
+STG_API stg_status stg_plan_network_info(const stg_plan* plan, stg_network_info* info);
+STG_API stg_status stg_front(stg_plan* plan, const float* d_mix, int32_t first_chunk, int32_t n_chunks,
+                             float* d_net_in, void* stream);
+STG_API stg_status stg_back(stg_plan* plan, const float* d_mix, const float* d_net_out,
+                            int32_t first_chunk, int32_t n_chunks, void* stream);
+STG_API stg_status stg_finish(stg_plan* plan, const float* d_mix, float* d_out, void* stream);
+
+/* The whole loop with the network as a callback, run on the calling thread between the
+ * halves: network(user, first_chunk, n_chunks, d_net_in, d_net_out, stream) enqueues the
+ * network on `stream` and returns 0, or non-zero to fail the separation with
+ * STG_MODEL_ERROR. The batch buffers belong to the plan. Progress and cancellation as in
+ * stg_separate_ex (options may be NULL). Replaces the chunk loops of the separators with the
+ * graph call in the middle (src/htdemucs.cpp:589-606, src/roformer.cpp:317-341,
+ * src/tfc_tdf.cpp:411-424). */
+typedef int32_t (*stg_network_fn)(void* user, int32_t first_chunk, int32_t n_chunks, const float* d_net_in,
+                                  float* d_net_out, void* stream);
+STG_API stg_status stg_separate_network(stg_plan* plan, const float* d_mix, float* d_out,
+                                        int32_t chunks_per_batch, stg_network_fn network, void* user,
+                                        const stg_run_options* options, void* stream);
+
+/* ---- the DSP primitives of src/stft.h on the device -------------------------------------- */
+
+/* torch.stft (src/stft.h:146-164) of each channel: periodic Hann, centre reflect pad,
+ * onesided, 1/sqrt(n_fft) when normalized. d_x [C][n_samples]; d_spec complex (interleaved
+ * float re, im) [C][n_fft/2 + 1][T], T = n_samples / hop + 1. n_fft 2048, 4096 or 7680. */
+STG_API stg_status stg_torch_stft(stg_engine* engine, int32_t n_fft, int32_t hop, int32_t normalized,
+                                  const float* d_x, int32_t n_channels, int64_t n_samples, float* d_spec,
+                                  void* stream);
+/* torch.istft (src/stft.h:167-197): d_spec complex [C][n_fft/2 + 1][n_frames] ->
+ * d_y [C][hop * (n_frames - 1)], window-sum normalised. */
+STG_API stg_status stg_torch_istft(stg_engine* engine, int32_t n_fft, int32_t hop, int32_t normalized,
+                                   const float* d_spec, int32_t n_channels, int32_t n_frames, float* d_y,
+                                   void* stream);
+/* HTDemucs _spec (src/stft.h:79-103): d_x [C][n_samples] -> complex [C][2048][T],
+ * T = ceil(n_samples / 1024). */
+STG_API stg_status stg_htdemucs_spec(stg_engine* engine, const float* d_x, int32_t n_channels, int64_t n_samples,
+                                     float* d_spec, void* stream);
+/* HTDemucs _ispec (src/stft.h:106-140): complex [C][2048][n_frames] -> d_y [C][length];
+ * n_frames must be ceil(length / 1024), as the model calls it. */
+STG_API stg_status stg_htdemucs_ispec(stg_engine* engine, const float* d_spec, int32_t n_channels,
+                                      int32_t n_frames, int64_t length, float* d_y, void* stream);
+
 /* ---- a separation that allocates no device memory ---------------------------------------- */
 
 /* No counterpart in the reference: the reference runs this path on the host.

@@ -76,6 +76,14 @@ class RunOptions(C.Structure):
                 ("on_progress", PROGRESS_FN), ("should_cancel", CANCEL_FN), ("user", C.c_void_p)]
 
 
+class NetworkInfo(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("net_in_floats_per_chunk", C.c_int64),
+                ("net_out_floats_per_chunk", C.c_int64)]
+
+
+NETWORK_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p)
+
+
 # Every symbol include/stems_gpu_v1.h declares, with its ctypes signature.
 _SIGNATURES = {
     "stg_version": (C.c_char_p, []),
@@ -95,6 +103,19 @@ _SIGNATURES = {
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.POINTER(RunOptions)]),
+    "stg_plan_network_info": (C.c_int32, [C.c_void_p, C.POINTER(NetworkInfo)]),
+    "stg_front": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
+    "stg_back": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "stg_finish": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_network": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, NETWORK_FN, C.c_void_p,
+                                         C.POINTER(RunOptions), C.c_void_p]),
+    "stg_torch_stft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int64,
+                                   C.c_void_p, C.c_void_p]),
+    "stg_torch_istft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32,
+                                    C.c_void_p, C.c_void_p]),
+    "stg_htdemucs_spec": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
+    "stg_htdemucs_ispec": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p,
+                                       C.c_void_p]),
     "stg_separate_roformer_noalloc": (C.c_int32, [C.c_int, C.POINTER(RoFormerConfig), C.c_int64, C.c_void_p,
                                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
 }
@@ -189,6 +210,46 @@ class Engine:
                 raise Cancelled(rc, msg or what)
             raise StemsError(rc, f"{what}: {msg}")
 
+    # -- the DSP primitives of src/stft.h on the device ----------------------------------
+    def torch_stft(self, x, n_fft, hop, normalized=False, stream=None):
+        """torch.stft of each channel of x [C][n] (CUDA float32): complex64 [C][n_fft/2+1][n/hop+1]."""
+        import torch
+        C_, n = x.shape
+        T = n // hop + 1
+        spec = torch.empty((C_, n_fft // 2 + 1, T), dtype=torch.complex64, device=x.device)
+        self._check(lib().stg_torch_stft(self._h, n_fft, hop, int(normalized), _ptr(x), C_, n, spec.data_ptr(),
+                                         _stream_of(stream, x)), "torch_stft")
+        return spec
+
+    def torch_istft(self, spec, n_fft, hop, normalized=False, stream=None):
+        """torch.istft of complex64 [C][n_fft/2+1][T]: float32 [C][hop*(T-1)]."""
+        import torch
+        spec = spec.contiguous()
+        C_, _, T = spec.shape
+        y = torch.empty((C_, hop * (T - 1)), dtype=torch.float32, device=spec.device)
+        self._check(lib().stg_torch_istft(self._h, n_fft, hop, int(normalized), spec.data_ptr(), C_, T, _ptr(y),
+                                          _stream_of(stream, spec)), "torch_istft")
+        return y
+
+    def htdemucs_spec(self, x, stream=None):
+        """HTDemucs _spec of x [C][n]: complex64 [C][2048][ceil(n/1024)]."""
+        import torch
+        C_, n = x.shape
+        spec = torch.empty((C_, 2048, (n + 1023) // 1024), dtype=torch.complex64, device=x.device)
+        self._check(lib().stg_htdemucs_spec(self._h, _ptr(x), C_, n, spec.data_ptr(), _stream_of(stream, x)),
+                    "htdemucs_spec")
+        return spec
+
+    def htdemucs_ispec(self, spec, length, stream=None):
+        """HTDemucs _ispec of complex64 [C][2048][T]: float32 [C][length]."""
+        import torch
+        spec = spec.contiguous()
+        C_, _, T = spec.shape
+        y = torch.empty((C_, length), dtype=torch.float32, device=spec.device)
+        self._check(lib().stg_htdemucs_ispec(self._h, spec.data_ptr(), C_, T, length, _ptr(y),
+                                             _stream_of(stream, spec)), "htdemucs_ispec")
+        return y
+
     # -- plans ---------------------------------------------------------------------------
     def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0):
         cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap)
@@ -267,6 +328,44 @@ class Plan:
                                   else CANCEL_FN())
             rc = lib().stg_separate_ex(self._h, _ptr(mix), _ptr(mask), _ptr(out), st, C.byref(opts))
         self.engine._check(rc, "separate")
+        return out
+
+    # -- the halves around a real network ------------------------------------------------
+    def network_info(self):
+        """(network input floats per chunk, network output floats per chunk)."""
+        info = NetworkInfo()
+        info.size = C.sizeof(NetworkInfo)
+        self.engine._check(lib().stg_plan_network_info(self._h, C.byref(info)), "network_info")
+        return info.net_in_floats_per_chunk, info.net_out_floats_per_chunk
+
+    def front(self, mix, first_chunk, n_chunks, net_in, stream=None):
+        self.engine._check(lib().stg_front(self._h, _ptr(mix), first_chunk, n_chunks, _ptr(net_in),
+                                           _stream_of(stream, mix)), "front")
+
+    def back(self, mix, net_out, first_chunk, n_chunks, stream=None):
+        self.engine._check(lib().stg_back(self._h, _ptr(mix), _ptr(net_out), first_chunk, n_chunks,
+                                          _stream_of(stream, net_out)), "back")
+
+    def finish(self, mix, out, stream=None):
+        self.engine._check(lib().stg_finish(self._h, _ptr(mix), _ptr(out), _stream_of(stream, out)), "finish")
+
+    def separate_network(self, mix, out, network, chunks_per_batch=0, stream=None):
+        """network(first_chunk, n_chunks, net_in_ptr, net_out_ptr, stream_handle) runs the model."""
+        st = _stream_of(stream, mix, out)
+        errors = []
+
+        def cb(user, first, n, p_in, p_out, s):
+            try:
+                network(first, n, p_in, p_out, s)
+                return 0
+            except Exception as e:   # reported through the status
+                errors.append(e)
+                return 1
+        fn = NETWORK_FN(cb)
+        rc = lib().stg_separate_network(self._h, _ptr(mix), _ptr(out), chunks_per_batch, fn, None, None, st)
+        if errors:
+            raise errors[0]
+        self.engine._check(rc, "separate_network")
         return out
 
     def last_timing(self):

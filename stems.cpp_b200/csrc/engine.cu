@@ -11,6 +11,7 @@
 #include <memory>
 #include <new>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #define STG_VERSION_STRING "stems-b200 spectral 0.1 (stems_gpu abi 1)"
@@ -55,6 +56,8 @@ struct stg_engine {
     bool profiling = false;
     std::string last_error;
     std::map<int, std::unique_ptr<FftTables>> tables;
+    // single-chunk plans of the DSP primitives, by (kind, n_fft, hop, normalized, C, length)
+    std::map<std::tuple<int, int, int, int, int, int64_t>, std::unique_ptr<stg_plan>> primitives;
 
     const FftTables& fft_tables_for(int n) {
         auto& t = tables[n];
@@ -78,6 +81,7 @@ struct stg_plan {
     DevBuf d_chunks, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
+    DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
 
     ~stg_plan() {
@@ -160,6 +164,21 @@ stg_status make_plan(stg_engine* e, const Cfg* cfg, int64_t n, stg_plan** out, F
         p->upload_all();
         *out = p.release();
     });
+}
+
+// The engine's cached single-chunk plan of a DSP primitive (kind 0: torch.stft geometry,
+// 1: torch.istft, 2: HTDemucs _spec/_ispec).
+stg_plan& primitive_plan(stg_engine* e, int kind, int n_fft, int hop, int normalized, int C, int64_t len) {
+    const auto key = std::make_tuple(kind, n_fft, hop, normalized, C, len);
+    auto it = e->primitives.find(key);
+    if (it != e->primitives.end()) return *it->second;
+    auto p = std::make_unique<stg_plan>();
+    p->engine = e;
+    if (kind == 2) build_htdemucs_spec(p->H, C, len);
+    else build_torch_stft(p->H, n_fft, hop, normalized != 0, C, len, kind == 1);
+    p->upload_all();
+    if (e->primitives.size() >= 64) e->primitives.clear();   // keep the cache bounded
+    return *(e->primitives[key] = std::move(p));
 }
 
 } // namespace
@@ -284,6 +303,117 @@ STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const floa
         p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr);
         cuda_check(cudaMemcpyAsync(h_out, p->s_out.p, out_b, cudaMemcpyDeviceToHost, st), "copy result out");
         cuda_check(cudaStreamSynchronize(st), "separation");
+    });
+}
+
+// ---- the halves around a real network ----------------------------------------------------
+STG_API stg_status stg_plan_network_info(const stg_plan* p, stg_network_info* info) {
+    if (!p || !info || info->size < sizeof(stg_network_info)) return STG_INVALID_ARGUMENT;
+    info->net_in_floats_per_chunk = p->H.net_in_per_chunk;
+    info->net_out_floats_per_chunk = p->H.net_out_per_chunk;
+    return STG_OK;
+}
+
+STG_API stg_status stg_front(stg_plan* p, const float* d_mix, int32_t first, int32_t n, float* d_net_in, void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+        launch_front(p->H, p->D, d_mix, first, n, d_net_in, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_back(stg_plan* p, const float* d_mix, const float* d_net_out, int32_t first, int32_t n,
+                            void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+        launch_back(p->H, p->D, d_mix, d_net_out, first, n, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_finish(stg_plan* p, const float* d_mix, float* d_out, void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+        launch_finish(p->H, p->D, d_mix, d_out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_separate_network(stg_plan* p, const float* d_mix, float* d_out, int32_t per_batch,
+                                        stg_network_fn network, void* user, const stg_run_options* opt,
+                                        void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        if (!network || !d_mix || !d_out) fail(STG_INVALID_ARGUMENT, "null argument");
+        if (opt && opt->size < sizeof(stg_run_options)) fail(STG_INVALID_ARGUMENT, "options.size is too small");
+        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const HostPlan& H = p->H;
+        const int G = (int)H.chunks.size();
+        const int per = per_batch > 0 ? std::min(per_batch, G) : G;
+        p->n_in.reserve(std::max<size_t>(16, sizeof(float) * (size_t)H.net_in_per_chunk * per), "network input");
+        p->n_out.reserve(std::max<size_t>(16, sizeof(float) * (size_t)H.net_out_per_chunk * per), "network output");
+        for (int b0 = 0; b0 < G; b0 += per) {
+            if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
+            const int nb = std::min(per, G - b0);
+            launch_front(H, p->D, d_mix, b0, nb, p->n_in.as<float>(), st);
+            if (network(user, b0, nb, p->n_in.as<float>(), p->n_out.as<float>(), stream) != 0)
+                fail(STG_MODEL_ERROR, "the network callback failed");
+            launch_back(H, p->D, d_mix, p->n_out.as<float>(), b0, nb, st);
+            if (opt && opt->on_progress) {
+                cuda_check(cudaStreamSynchronize(st), "spectral kernels");
+                opt->on_progress(opt->user, b0 + nb, G);
+            }
+        }
+        launch_finish(H, p->D, d_mix, d_out, st);
+    });
+}
+
+// ---- the DSP primitives of src/stft.h --------------------------------------------------
+STG_API stg_status stg_torch_stft(stg_engine* e, int32_t n_fft, int32_t hop, int32_t normalized, const float* d_x,
+                                  int32_t C, int64_t n, float* d_spec, void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        cuda_check(cudaSetDevice(e->device), "cudaSetDevice");
+        stg_plan& p = primitive_plan(e, 0, n_fft, hop, normalized, C, n);
+        launch_front(p.H, p.D, d_x, 0, 1, d_spec, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_torch_istft(stg_engine* e, int32_t n_fft, int32_t hop, int32_t normalized,
+                                   const float* d_spec, int32_t C, int32_t n_frames, float* d_y, void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        if (n_frames < 2 || hop < 1) fail(STG_INVALID_ARGUMENT, "need at least two frames");
+        cuda_check(cudaSetDevice(e->device), "cudaSetDevice");
+        stg_plan& p = primitive_plan(e, 1, n_fft, hop, normalized, C, (int64_t)hop * (n_frames - 1));
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        launch_back(p.H, p.D, nullptr, d_spec, 0, 1, st);
+        launch_finish(p.H, p.D, nullptr, d_y, st);
+    });
+}
+
+STG_API stg_status stg_htdemucs_spec(stg_engine* e, const float* d_x, int32_t C, int64_t n, float* d_spec,
+                                     void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        cuda_check(cudaSetDevice(e->device), "cudaSetDevice");
+        stg_plan& p = primitive_plan(e, 2, 4096, 1024, 1, C, n);
+        launch_front(p.H, p.D, d_x, 0, 1, d_spec, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_htdemucs_ispec(stg_engine* e, const float* d_spec, int32_t C, int32_t n_frames, int64_t length,
+                                      float* d_y, void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        if (length < 1 || n_frames != (int)((length + 1023) / 1024))
+            fail(STG_INVALID_ARGUMENT, "n_frames must be ceil(length / 1024)");
+        cuda_check(cudaSetDevice(e->device), "cudaSetDevice");
+        stg_plan& p = primitive_plan(e, 2, 4096, 1024, 1, C, length);
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        launch_back(p.H, p.D, nullptr, d_spec, 0, 1, st);
+        launch_finish(p.H, p.D, nullptr, d_y, st);
     });
 }
 

@@ -1,0 +1,96 @@
+// frame.cuh -- what the spectral kernels share: the FFT configuration per n_fft, the padded
+// frame loader, streaming loads and the ring-buffer index. Included by kernels.cu (fused
+// separation) and split.cu (front and back halves around a network).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fft.cuh"
+#include "kernels.h"
+
+namespace stg {
+
+// Threads per CTA, radix plan, the CTAs per SM the register budget aims at, and the largest
+// hop the input prefetch registers cover.
+template <int N> struct FftCfg;
+template <> struct FftCfg<2048> {
+    static constexpr int T = 128, MINB = 3, HOPMAX = 512;
+    static constexpr int PF_GROUPS = 1;     // mask loads issued in this many groups
+    static constexpr bool AHEAD = false;    // mask loads issued one frame ahead
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;   // table copies in shared memory
+    using Plan = RadixList<8, 16, 16>;
+};
+template <> struct FftCfg<4096> {
+    static constexpr int T = 256, MINB = 2, HOPMAX = 1024;
+    static constexpr int PF_GROUPS = 1;
+    static constexpr bool AHEAD = false;
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    using Plan = RadixList<16, 16, 16>;
+};
+template <> struct FftCfg<7680> {
+    static constexpr int T = 512, MINB = 1, HOPMAX = 1024;
+    static constexpr int PF_GROUPS = 1;
+    static constexpr bool AHEAD = false;
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    using Plan = RadixList<15, 8, 8, 8>;
+};
+
+__device__ __forceinline__ int64_t reflect1(int64_t j, int64_t n) {
+    if (j < 0) j = -j;
+    if (j >= n) j = 2 * (n - 1) - j;
+    return j;
+}
+
+// Loads for data read once per kernel (the masks): bypass L1 so the tables stay resident.
+__device__ __forceinline__ float ld_stream(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float2 ld_stream2(const float* p) {
+    float2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+    return v;
+}
+
+template <class Params>
+__device__ __forceinline__ float chunk_sample(const Params& p, const ChunkDesc& cd,
+                                              const float* __restrict__ chan, int64_t pl) {
+    if (pl >= cd.valid) {
+        if (!cd.tail_reflect) return 0.0f;
+        pl = 2 * (int64_t)(cd.valid - 1) - pl;
+    }
+    int64_t x = cd.src0 + pl;
+    if (p.reflect_global) x = reflect1(x, p.len);
+    else if (x < 0 || x >= p.len) return 0.0f;
+    return ld_stream(chan + x);
+}
+
+// New input samples [q, q + hop) a frame needs beyond the previous one, per thread.
+template <int T, int HOPMAX> struct InPrefetch {
+    static constexpr int K = (HOPMAX + T - 1) / T;
+    float2 v[K];
+};
+
+template <class Params>
+__device__ __forceinline__ float2 frame_sample(const Params& p, const ChunkDesc& cd, const float* chL,
+                                               const float* chR, int lxf, int q) {
+    int r = (int)reflect1((int64_t)q - p.g.n_fft / 2, lxf);
+    if (p.g.ht_pad) r = (int)reflect1(r - p.g.ht_pad, p.g.Lc);
+    const float a = chunk_sample(p, cd, chL, r);
+    const float b = p.n_channels > 1 ? chunk_sample(p, cd, chR, r) : 0.0f;
+    return make_float2(a, b);
+}
+
+template <int N> __device__ __forceinline__ int ring_slot(int q) {
+    if constexpr ((N & (N - 1)) == 0) return q & (N - 1);
+    else return q % N;
+}
+
+} // namespace stg

@@ -106,8 +106,55 @@ struct CombineParams {
     float* out;                // [S(+1)][C][len]
 };
 
+// The two halves of the path around a real network (split.cu). The front half computes the
+// STFT of every chunk and writes it in the network's input layout; the back half reads a
+// spectrogram in the network's output layout and runs the iSTFT and the overlap-add into
+// the same Y / Tr scratch as the fused kernel (the combine then finishes the separation).
+enum FrontLayout : int {
+    FRONT_COMPLEX = 0,   // complex [C][F][T], F = n_bins (torch_stft, htdemucs_spec)
+    FRONT_CAC = 1,       // float planes [2C][F][T]: re = 2c, im = 2c + 1 (HTDemucs input)
+    FRONT_BANDS = 2,     // RoFormer band-major features [sum_b din_b * T]
+    FRONT_TFC = 3        // float planes [4][dim_f][T], bins below zero_bins 0 (TFC-TDF input)
+};
+enum BackLayout : int {
+    BACK_COMPLEX = 0,    // complex [C][F][T] (torch_istft, htdemucs_ispec)
+    BACK_CAC = 1,        // float planes [S][2C][F][T] (HTDemucs output)
+    BACK_TFC = 2         // float planes [4S][dim_f][T] (TFC-TDF output)
+};
+
+struct SplitParams {
+    const float* mix;          // front: the track
+    int64_t len;
+    int n_channels;
+    int reflect_global;
+    const ChunkDesc* chunks;
+    int n_chunks;
+    FrameGeom g;
+    int K, n_tiles;
+    int S;                     // back: stems in the network output
+    const float* win;
+    const float2* tw;
+    float fwd_scale, inv_scale;
+    const float* inv_env;
+    int layout;                // FrontLayout or BackLayout
+    int n_bins;                // bins the layout holds
+    int zero_bins;             // FRONT_TFC
+    const int2* bin_tab;       // FRONT_BANDS (FusedParams::bin_tab)
+    int bin_multi;
+    const int* bin_ebeg;
+    const int2* bin_ent;
+    float* net;                // front: written; back: read
+    int64_t net_chunk_stride;
+    float* Y;                  // back
+    int64_t y_chunk_stride;
+    float* Tr;
+    int64_t tr_chunk_stride;
+};
+
 // Launchers. Return a cudaError_t from the launch (kernel errors surface on sync).
 cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st);
+cudaError_t launch_front(const SplitParams& p, cudaStream_t st);
+cudaError_t launch_back(const SplitParams& p, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 size_t fused_smem_bytes(int arch, int n_fft);
 int fused_threads(int n_fft);

@@ -140,6 +140,11 @@ void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     P.step_out = stride;
     P.out_shift = 0;
     P.nan_to_zero = 0;
+    P.front_layout = FRONT_CAC;                                       // in_x (:423-433)
+    P.back_layout = BACK_CAC;                                         // ox (:463-469)
+    P.front_bins = P.back_bins = N / 2;
+    P.net_in_per_chunk = (int64_t)2 * P.C * (N / 2) * T;
+    P.net_out_per_chunk = P.mask_per_chunk;
     finish_plan(P, T + 4);                                            // 2 zero frames per side
 }
 
@@ -249,6 +254,11 @@ void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
     P.out_shift = pad ? border : 0;                                   // :344
     P.nan_to_zero = 1;                                                // :348
     P.complement = c.complement ? 1 : 0;                              // :481-485
+    P.front_layout = FRONT_BANDS;                                     // feat (:226-241)
+    P.front_bins = F;
+    P.net_in_per_chunk = P.stem_stride;
+    P.net_out_per_chunk = P.mask_per_chunk;                           // masks (:251-269)
+    P.back_is_fused = true;
     finish_plan(P, T);
 }
 
@@ -341,7 +351,75 @@ void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len) {
     }
     P.compensate = c.compensate;                                      // :586-587
     P.complement = c.complement ? 2 : 0;                              // :588-596
+    P.front_layout = FRONT_TFC;                                       // in (:366-376)
+    P.back_layout = BACK_TFC;                                         // y (:381-387)
+    P.front_bins = P.back_bins = c.dim_f;
+    P.net_in_per_chunk = (int64_t)4 * c.dim_f * c.dim_t;
+    P.net_out_per_chunk = P.mask_per_chunk;
     finish_plan(P, c.dim_t);
+}
+
+// ---- the DSP primitives as single-chunk plans -----------------------------------------------
+namespace {
+void single_chunk(HostPlan& P, int64_t len) {
+    ChunkDesc d{};
+    d.src0 = 0;
+    d.valid = (int32_t)len;
+    d.tail_reflect = 0;
+    d.out0 = 0;
+    d.out_len = P.g.Lout;
+    d.y_off = 0;
+    d.w_off = 0;
+    P.chunks.assign(1, d);
+    P.W.assign(std::max(P.g.Lout, 1), 1.0f);
+    P.reflect_global = 0;
+    P.step_out = std::max(P.g.Lout, 1);
+    P.out_shift = 0;
+    P.nan_to_zero = 0;
+    P.S = P.S_out = 1;
+    P.primitive = true;
+}
+} // namespace
+
+void build_torch_stft(HostPlan& P, int n_fft, int hop, bool normalized, int n_channels, int64_t len,
+                      bool inverse) {
+    if (n_channels < 1 || n_channels > 2) fail(STG_INVALID_ARGUMENT, "n_channels must be 1 or 2");
+    if (hop < 1 || len < 1 || len > INT32_MAX / 4) fail(STG_INVALID_ARGUMENT, "bad hop or length");
+    if (!inverse && len <= n_fft / 2)
+        fail(STG_INVALID_ARGUMENT, "reflect pad larger than the signal");   // stft.h:59
+    P.arch = ARCH_TFC;                                                // plain CaC-free spectra
+    P.len = len;
+    P.C = n_channels;
+    const int T = (int)(len / hop) + 1;                               // stft.h:153
+    P.g = FrameGeom{n_fft, hop, (int)len, T, 0, 0, 0, n_fft / 2, hop * (T - 1)};
+    P.fwd_scale = normalized ? (float)(1.0 / std::sqrt((double)n_fft)) : 1.0f;
+    P.inv_scale = (float)((normalized ? std::sqrt((double)n_fft) : 1.0) / n_fft);
+    single_chunk(P, len);
+    P.front_layout = FRONT_COMPLEX;
+    P.back_layout = BACK_COMPLEX;
+    P.front_bins = P.back_bins = n_fft / 2 + 1;
+    P.net_in_per_chunk = P.net_out_per_chunk = (int64_t)2 * n_channels * (n_fft / 2 + 1) * T;
+    finish_plan(P, T);
+}
+
+void build_htdemucs_spec(HostPlan& P, int n_channels, int64_t len) {
+    const int N = 4096, hl = N / 4, pad = hl / 2 * 3;
+    if (n_channels < 1 || n_channels > 2) fail(STG_INVALID_ARGUMENT, "n_channels must be 1 or 2");
+    if (len < 1 || len > INT32_MAX / 4) fail(STG_INVALID_ARGUMENT, "bad length");
+    const int L = (int)len, T = (L + hl - 1) / hl;                   // stft.h:81
+    if (L <= pad || L <= pad + T * hl - L) fail(STG_INVALID_ARGUMENT, "reflect pad larger than the signal");
+    P.arch = ARCH_HTDEMUCS;
+    P.len = len;
+    P.C = n_channels;
+    P.g = FrameGeom{N, hl, L, T, 2 * hl, pad, 2 * pad + T * hl, N / 2 + pad, L};
+    P.fwd_scale = (float)(1.0 / std::sqrt((double)N));
+    P.inv_scale = (float)(std::sqrt((double)N) / N);
+    single_chunk(P, len);
+    P.front_layout = FRONT_COMPLEX;
+    P.back_layout = BACK_COMPLEX;
+    P.front_bins = P.back_bins = N / 2;
+    P.net_in_per_chunk = P.net_out_per_chunk = (int64_t)2 * n_channels * (N / 2) * T;
+    finish_plan(P, T + 4);
 }
 
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
@@ -394,6 +472,104 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     cuda_check(launch_combine(c, st), "combine kernel launch");
     if (timing) timing->launches++;
     if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
+}
+
+// ---- the halves around a real network ----------------------------------------------------------
+namespace {
+SplitParams split_params(const HostPlan& P, const PlanDevice& D, const float* d_mix, int first, int n) {
+    SplitParams s{};
+    s.mix = d_mix;
+    s.len = P.len;
+    s.n_channels = P.C;
+    s.reflect_global = P.reflect_global;
+    s.chunks = D.chunks + first;
+    s.n_chunks = n;
+    s.g = P.g;
+    s.K = P.K;
+    s.n_tiles = P.n_tiles;
+    s.S = P.S;
+    s.win = D.win;
+    s.tw = D.tw;
+    s.fwd_scale = P.fwd_scale;
+    s.inv_scale = P.inv_scale;
+    s.inv_env = D.env;
+    s.bin_tab = D.btab;
+    s.bin_multi = P.bin_multi;
+    s.bin_ebeg = D.ebeg;
+    s.bin_ent = D.ent;
+    s.zero_bins = P.zero_bins;
+    s.Y = D.Y + (int64_t)first * P.y_chunk_stride;
+    s.y_chunk_stride = P.y_chunk_stride;
+    s.Tr = D.Tr + (int64_t)first * P.tr_chunk_stride;
+    s.tr_chunk_stride = P.tr_chunk_stride;
+    return s;
+}
+
+void check_range(const HostPlan& P, int first, int n) {
+    if (first < 0 || n < 1 || (int64_t)first + n > (int64_t)P.chunks.size())
+        fail(STG_INVALID_ARGUMENT, "chunk range outside the plan");
+}
+} // namespace
+
+void launch_front(const HostPlan& P, const PlanDevice& D, const float* d_mix, int first, int n, float* d_net_in,
+                  cudaStream_t st) {
+    if (!d_mix || !d_net_in) fail(STG_INVALID_ARGUMENT, "null buffer");
+    check_range(P, first, n);
+    if (P.front_layout == FRONT_BANDS && reinterpret_cast<uintptr_t>(d_net_in) % 16)
+        fail(STG_INVALID_ARGUMENT, "the feature buffer must be 16-byte aligned");
+    SplitParams s = split_params(P, D, d_mix, first, n);
+    s.layout = P.front_layout;
+    s.n_bins = P.front_bins;
+    s.net = d_net_in;
+    s.net_chunk_stride = P.net_in_per_chunk;
+    cuda_check(stg::launch_front(s, st), "front kernel launch");
+}
+
+void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_net_out, int first,
+                 int n, cudaStream_t st) {
+    if (!d_net_out || (P.back_is_fused && !d_mix)) fail(STG_INVALID_ARGUMENT, "null buffer");
+    check_range(P, first, n);
+    if (P.back_is_fused) {
+        // RoFormer: the network's masks are exactly the fused kernel's mask input
+        if (reinterpret_cast<uintptr_t>(d_net_out) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+        FusedParams f{};
+        f.mix = d_mix; f.len = P.len; f.n_channels = P.C; f.reflect_global = P.reflect_global;
+        f.chunks = D.chunks + first; f.n_chunks = n;
+        f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
+        f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
+        f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
+        f.mask = d_net_out; f.mask_chunk_stride = P.mask_per_chunk;
+        f.bin_tab = D.btab; f.bin_multi = P.bin_multi;
+        f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
+        f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
+        f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
+        f.Y = D.Y + (int64_t)first * P.y_chunk_stride; f.y_chunk_stride = P.y_chunk_stride;
+        f.Tr = D.Tr + (int64_t)first * P.tr_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+        cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+        return;
+    }
+    SplitParams s = split_params(P, D, d_mix, first, n);
+    s.layout = P.back_layout;
+    s.n_bins = P.back_bins;
+    s.net = const_cast<float*>(d_net_out);
+    s.net_chunk_stride = P.net_out_per_chunk;
+    cuda_check(stg::launch_back(s, st), "back kernel launch");
+}
+
+void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st) {
+    if (!d_out || (P.complement && !d_mix)) fail(STG_INVALID_ARGUMENT, "null buffer");
+    CombineParams c{};
+    c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
+    c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
+    c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
+    c.step_out = P.step_out; c.max_out_len = P.max_out_len;
+    c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
+    c.W = D.W;
+    c.S = P.S; c.C = P.C; c.len = P.arch_out_len();
+    c.out_shift = P.out_shift;
+    c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
+    c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    cuda_check(launch_combine(c, st), "combine kernel launch");
 }
 
 } // namespace stg

@@ -49,7 +49,14 @@ struct HostPlan {
     std::vector<int> ebeg;         // RoFormer CSR over bins
     std::vector<int2> ent;
     std::vector<float> binv;
+    // the network between the halves: layouts and floats per chunk of its input and output
+    int front_layout = FRONT_COMPLEX, back_layout = BACK_COMPLEX;
+    int front_bins = 0, back_bins = 0;
+    int64_t net_in_per_chunk = 0, net_out_per_chunk = 0;
+    bool back_is_fused = false;    // RoFormer: the network outputs a mask; the fused kernel applies it
 
+    bool primitive = false;        // a single-chunk DSP primitive: the output is the chunk's
+    int64_t arch_out_len() const { return primitive ? g.Lout : len; }
     int64_t n_chunks() const { return (int64_t)chunks.size(); }
     int64_t out_floats() const { return (int64_t)S_out * C * len; }
     size_t y_bytes() const { return sizeof(float) * (size_t)y_chunk_stride * chunks.size(); }
@@ -72,6 +79,12 @@ struct PlanDevice {
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
+// Single-chunk plans of the DSP primitives: torch.stft / torch.istft (src/stft.h:146-197) of
+// `len` samples (the istft's output length), HTDemucs _spec/_ispec (src/stft.h:79-140).
+// For the inverse, len = hop * (frames - 1), the istft's output length.
+void build_torch_stft(HostPlan& P, int n_fft, int hop, bool normalized, int n_channels, int64_t len,
+                      bool inverse);
+void build_htdemucs_spec(HostPlan& P, int n_channels, int64_t len);
 void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len);
 void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len);
 
@@ -89,5 +102,15 @@ struct RunTiming {
 // chunk batches (progress and cancellation between batches), then the combine.
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing);
+
+// The halves around a real network, on chunks [first, first + n): the front writes the
+// network's input (net_in_per_chunk floats per chunk) into d_net_in; the back reads its
+// output (net_out_per_chunk floats per chunk) and leaves the chunks' results in the scratch;
+// finish (the combine) produces the separation once every chunk went through the back.
+void launch_front(const HostPlan& P, const PlanDevice& D, const float* d_mix, int first, int n,
+                  float* d_net_in, cudaStream_t st);
+void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_net_out, int first,
+                 int n, cudaStream_t st);
+void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st);
 
 } // namespace stg

@@ -1,0 +1,302 @@
+// split.cu -- the front and back halves of the path, for a real network between them.
+//
+// front_kernel: for every frame of every chunk, the same padded load and stereo-packed
+// forward FFT as the fused kernel, then the two channels' spectra written in the network's
+// input layout: complex [C][F][T] (src/stft.h:146-164 torch_stft, 79-103 htdemucs_spec),
+// HTDemucs CaC planes (src/htdemucs.cpp:423-433), RoFormer band-major features
+// (src/roformer.cpp:226-241) or TFC-TDF CaC planes with the low bins zero
+// (src/tfc_tdf.cpp:366-376).
+// back_kernel: for every stem and frame, a spectrogram read from the network's output layout
+// (src/htdemucs.cpp:463-469, src/tfc_tdf.cpp:381-387, or complex for torch_istft /
+// htdemucs_ispec), the c2r conventions (DC and Nyquist imaginary parts dropped, the HTDemucs
+// Nyquist bin zero), the inverse FFT, the window, and the overlap-add into the fused kernel's
+// Y / Tr scratch.
+#include <algorithm>
+
+#include "fft.cuh"
+#include "frame.cuh"
+#include "kernels.h"
+
+namespace stg {
+
+namespace {
+
+// The spectra of bin f (zl, zr) to the front layout, frame t of chunk ci.
+template <int N>
+__device__ __forceinline__ void front_store(const SplitParams& p, const int2* btab, int ci, int t, int f,
+                                            float2 zl, float2 zr) {
+    const int T = p.g.T, C = p.n_channels;
+    float* out = p.net + (int64_t)ci * p.net_chunk_stride;
+    const int64_t plane = (int64_t)p.n_bins * T, idx = (int64_t)f * T + t;
+    switch (p.layout) {
+        case FRONT_COMPLEX:
+            if (f < p.n_bins) {
+                reinterpret_cast<float2*>(out)[idx] = zl;
+                if (C > 1) reinterpret_cast<float2*>(out)[plane + idx] = zr;
+            }
+            break;
+        case FRONT_CAC:
+            if (f < p.n_bins) {
+                out[idx] = zl.x;
+                out[plane + idx] = zl.y;
+                if (C > 1) {
+                    out[2 * plane + idx] = zr.x;
+                    out[3 * plane + idx] = zr.y;
+                }
+            }
+            break;
+        case FRONT_TFC:
+            if (f < p.n_bins) {
+                const bool z = f < p.zero_bins;
+                out[idx] = z ? 0.0f : zl.x;
+                out[plane + idx] = z ? 0.0f : zl.y;
+                out[2 * plane + idx] = z ? 0.0f : zr.x;
+                out[3 * plane + idx] = z ? 0.0f : zr.y;
+            }
+            break;
+        default: {   // FRONT_BANDS: every band holding f gets the bin's entry (j*C + c)*2 + {re, im}
+            if (f >= p.n_bins) break;
+            const int2 e = btab[f];
+            const int v[2] = {e.x, e.y};
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const unsigned size = (unsigned)v[k] >> 22;
+                if (!size) continue;
+                float* q = out + (int64_t)((v[k] & 0x3fffff) + t * (int)size) * (2 * C);
+                if (C > 1) *reinterpret_cast<float4*>(q) = make_float4(zl.x, zl.y, zr.x, zr.y);
+                else *reinterpret_cast<float2*>(q) = zl;
+            }
+            if (p.bin_multi) {
+                const int e1 = __ldg(p.bin_ebeg + f + 1);
+                for (int k = __ldg(p.bin_ebeg + f) + 2; k < e1; k++) {
+                    const int2 en = __ldg(p.bin_ent + k);
+                    float* q = out + en.x + (int64_t)t * en.y;
+                    q[0] = zl.x; q[1] = zl.y;
+                    if (C > 1) { q[2] = zr.x; q[3] = zr.y; }
+                }
+            }
+        }
+    }
+}
+
+// Bin f of stem s, frame t, from the back layout: the two channels' spectra.
+__device__ __forceinline__ void back_load(const SplitParams& p, int ci, int s, int t, int f, float2& yl, float2& yr) {
+    const int T = p.g.T, C = p.n_channels;
+    const float* in = p.net + (int64_t)ci * p.net_chunk_stride;
+    yl = yr = make_float2(0.f, 0.f);
+    if (f >= p.n_bins) return;   // the HTDemucs Nyquist bin, TFC-TDF bins from dim_f up
+    const int64_t plane = (int64_t)p.n_bins * T, idx = (int64_t)f * T + t;
+    switch (p.layout) {
+        case BACK_COMPLEX: {
+            const float2* z = reinterpret_cast<const float2*>(in);
+            yl = z[idx];
+            if (C > 1) yr = z[plane + idx];
+            break;
+        }
+        case BACK_CAC: {
+            const float* q = in + (int64_t)s * 2 * C * plane + idx;
+            yl = make_float2(q[0], q[plane]);
+            if (C > 1) yr = make_float2(q[2 * plane], q[3 * plane]);
+            break;
+        }
+        default: {   // BACK_TFC
+            const float* q = in + (int64_t)s * 4 * plane + idx;
+            yl = make_float2(q[0], q[plane]);
+            yr = make_float2(q[2 * plane], q[3 * plane]);
+        }
+    }
+}
+
+template <int N>
+__global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p) {
+    constexpr int T = FftCfg<N>::T;
+    using Plan = typename FftCfg<N>::Plan;
+    constexpr int R1 = Head<Plan>::first;
+    using FwdRest = typename Head<Plan>::tail;
+    extern __shared__ float4 smem_raw[];
+    float2* buf = reinterpret_cast<float2*>(smem_raw);
+    float2* in_ring = buf + padded_size(N);
+    int2* btab = reinterpret_cast<int2*>(in_ring + N);
+    const TwGlobal tw{p.tw};
+    const int tid = threadIdx.x;
+    const FrameGeom& G = p.g;
+    const int hop = G.hop, C = p.n_channels;
+    const float* chL = p.mix;
+    const float* chR = p.mix + (C > 1 ? p.len : 0);
+    const int lxf = G.ht_pad ? G.ht_lxf : G.Lc;
+    const float half_fwd = 0.5f * p.fwd_scale;
+    if (p.layout == FRONT_BANDS)
+        for (int i = tid; i < p.n_bins; i += T) btab[i] = __ldg(p.bin_tab + i);
+    InPrefetch<T, FftCfg<N>::HOPMAX> nx;
+
+    for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
+        const int tile = item % p.n_tiles, ci = item / p.n_tiles;
+        const ChunkDesc cd = p.chunks[ci];
+        const int t_begin = tile * p.K, t_end = min(G.T, t_begin + p.K);
+        {
+            const int q0 = G.first_pos + t_begin * hop;
+            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = frame_sample(p, cd, chL, chR, lxf, q0 + n);
+#pragma unroll
+            for (int k = 0; k < nx.K; k++) {
+                const int u = tid + k * T;
+                if (u < hop && t_begin + 1 < t_end) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + N + u);
+            }
+        }
+        __syncthreads();
+        for (int t = t_begin; t < t_end; t++) {
+            const int q0 = G.first_pos + t * hop;
+            pass_io<N, R1, 1, T, false, false>(
+                tw, tid,
+                [&](int j, int r) {
+                    const int n = j + r * (N / R1);
+                    const float2 x = in_ring[ring_slot<N>(q0 + n)];
+                    const float w = __ldg(p.win + n);
+                    return make_float2(x.x * w, x.y * w);
+                },
+                [&](int base, int r, float2 v) { buf[pad_store<R1, 1>(base, r)] = v; });
+            __syncthreads();
+            if (t + 1 < t_end) {
+#pragma unroll
+                for (int k = 0; k < nx.K; k++) {
+                    const int u = tid + k * T;
+                    if (u < hop) in_ring[ring_slot<N>(q0 + N + u)] = nx.v[k];
+                }
+                if (t + 2 < t_end) {
+#pragma unroll
+                    for (int k = 0; k < nx.K; k++) {
+                        const int u = tid + k * T;
+                        if (u < hop) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + hop + N + u);
+                    }
+                }
+            }
+            passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
+            for (int f = tid; f < p.n_bins && f <= N / 2; f += T) {
+                const int fm = f == 0 ? 0 : N - f;
+                const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
+                const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
+                const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
+                front_store<N>(p, btab, ci, t, f, zl, zr);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <int N>
+__global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p) {
+    constexpr int T = FftCfg<N>::T;
+    using Plan = typename FftCfg<N>::Plan;
+    using InvInit = typename Init<Plan>::type;
+    constexpr int RL = Init<Plan>::last, NSL = Init<Plan>::prod;
+    extern __shared__ float4 smem_raw[];
+    float2* buf = reinterpret_cast<float2*>(smem_raw);
+    float2* out_ring = buf + padded_size(N);
+    const TwGlobal tw{p.tw};
+    const int tid = threadIdx.x;
+    const FrameGeom& G = p.g;
+    const int hop = G.hop, C = p.n_channels;
+    for (int i = tid; i < N; i += T) out_ring[i] = make_float2(0.f, 0.f);
+
+    for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
+        const int tile = item % p.n_tiles, ci = item / p.n_tiles;
+        const int t_begin = tile * p.K, t_end = min(G.T, t_begin + p.K);
+        const bool last_tile = t_end == G.T;
+        for (int s = 0; s < p.S; s++) {
+            float* Ys = p.Y + (int64_t)ci * p.y_chunk_stride + (int64_t)s * C * G.Lout;
+            float* Trs = p.Tr + (int64_t)ci * p.tr_chunk_stride + ((int64_t)tile * p.S + s) * C * (N - hop);
+            for (int t = t_begin; t < t_end; t++) {
+                const int q0 = G.first_pos + t * hop;
+                for (int f = tid; f <= N / 2; f += T) {
+                    float2 yl, yr;
+                    back_load(p, ci, s, t, f, yl, yr);
+                    if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
+                    const int fm = f == 0 ? 0 : N - f;
+                    buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
+                    if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
+                }
+                __syncthreads();
+                passes<N, T, true, 1>(buf, tw, tid, InvInit{});
+                pass_io<N, RL, NSL, T, true, false>(
+                    tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
+                    [&](int base, int r, float2 v) {
+                        const int n = base + r * NSL;
+                        const float w = __ldg(p.win + n) * p.inv_scale;
+                        float2& o = out_ring[ring_slot<N>(q0 + n)];
+                        o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
+                    });
+                __syncthreads();
+                const bool last = t == t_end - 1;
+                const int ny = (last && last_tile) ? N : hop;
+                const int nflush = last ? N : hop;
+                for (int u = tid; u < nflush; u += T) {
+                    const int q = q0 + u;
+                    float2& o = out_ring[ring_slot<N>(q)];
+                    const float2 v = o;
+                    o = make_float2(0.f, 0.f);
+                    const int j = q - G.out_offset;
+                    const bool in = j >= 0 && j < G.Lout;
+                    const float ie = in ? ld_stream(p.inv_env + j) : 0.0f;
+                    if (u < ny) {
+                        if (in) {
+                            Ys[j] = v.x * ie;
+                            if (C > 1) Ys[G.Lout + j] = v.y * ie;
+                        }
+                    } else {
+                        Trs[u - hop] = v.x * ie;
+                        if (C > 1) Trs[(N - hop) + u - hop] = v.y * ie;
+                    }
+                }
+                // the next frame's first barrier orders these ring writes before later reads
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <class K>
+cudaError_t launch_persistent(K kernel, int threads, size_t smem, int64_t items, cudaStream_t st,
+                              const SplitParams& p) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0, n_sm = 0, dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem)) != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const int grid = (int)std::min<int64_t>(items, (int64_t)per_sm * n_sm);
+    kernel<<<grid, threads, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <int N> cudaError_t front_t(const SplitParams& p, cudaStream_t st) {
+    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N) + sizeof(int2) * (size_t)(N / 2 + 2);
+    return launch_persistent(front_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
+}
+template <int N> cudaError_t back_t(const SplitParams& p, cudaStream_t st) {
+    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N);
+    return launch_persistent(back_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
+}
+
+} // namespace
+
+cudaError_t launch_front(const SplitParams& p, cudaStream_t st) {
+    if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
+    switch (p.g.n_fft) {
+        case 2048: return front_t<2048>(p, st);
+        case 4096: return front_t<4096>(p, st);
+        case 7680: return front_t<7680>(p, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_back(const SplitParams& p, cudaStream_t st) {
+    if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
+    switch (p.g.n_fft) {
+        case 2048: return back_t<2048>(p, st);
+        case 4096: return back_t<4096>(p, st);
+        case 7680: return back_t<7680>(p, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+} // namespace stg
