@@ -192,8 +192,8 @@ def cpu_run(w, length, mix, mask_host, n_sample, threads):
                              sample_first=0, sample_count=n_sample, threads=threads)
         fn = oracle.rf_separate
     elif w["arch"] == "htdemucs":
-        p = oracle.ht_params(n_sources=w["sources"], segment=w["segment"], sample_first=0,
-                             sample_count=n_sample, threads=threads)
+        p = oracle.ht_params(n_sources=w["sources"], segment=w["segment"], mono_norm=1, cac_norm=1,
+                             sample_first=0, sample_count=n_sample, threads=threads)
         fn = oracle.ht_separate
     else:
         p = oracle.tfc_params(n_fft=w["n_fft"], hop=w["hop"], dim_f=w["dim_f"], dim_t=w["dim_t"],

@@ -77,13 +77,19 @@ STG_API stg_status stg_plan_last_timing(stg_plan* plan, float* fused_ms, float* 
 
 /* ---- model configurations (the GGUF metadata the reference reads) ------------------------ */
 
-/* HTDemucs (src/htdemucs.cpp:478-500; n_fft 4096 and hop 1024 are fixed, :35-36). */
+/* HTDemucs (src/htdemucs.cpp:478-500; n_fft 4096 and hop 1024 are fixed, :35-36).
+ * The reference always applies both normalisations; 0 turns one off (the stand-in network
+ * then sees the raw spectrogram, or the raw mix). */
 typedef struct {
     uint32_t size;
     int32_t n_channels;      /* stems.audio_channels (2) */
     int32_t n_sources;       /* len(stems.sources) (4 or 6) */
     int32_t segment;         /* segment_samples() = seg_num * sr / seg_den (343980) */
     float overlap;           /* SeparateOptions.overlap; < 0 = 0.25 */
+    int32_t mono_norm;       /* 1: the mix / mono std normalisation and the stems' inverse
+                                (src/htdemucs.cpp:539-549, 638-642) */
+    int32_t cac_norm;        /* 1: per-segment mean / std of the CaC spectrogram around the
+                                network (src/htdemucs.cpp:434-436, 466-469) */
 } stg_htdemucs_config;
 
 /* Mel-Band / BS-RoFormer (src/roformer.cpp:360-412). */
@@ -198,9 +204,13 @@ STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const flo
  * each batch of chunks, the front half writes the network's input, the network runs, the
  * back half reads the network's output; once every chunk went through the back half,
  * stg_finish overlap-adds the chunks into the result.
- *   HTDemucs  input  in_x  [2C][2048][T] float CaC planes (src/htdemucs.cpp:423-433, before
- *                    the mean/std normalisation of :434-436);
- *             output ox    [S][2C][2048][T] (:463-469, after the denormalisation).
+ *   HTDemucs  input  in_x  [2C][2048][T] float CaC planes (src/htdemucs.cpp:423-433), with
+ *                    cac_norm normalised by the segment's mean / std (:434-436);
+ *             output ox    [S][2C][2048][T] (:463-469), with cac_norm mapped back by the
+ *                    segment's std and mean (:469) in the back half.
+ *             With mono_norm, the call with first_chunk 0 normalises the whole track into
+ *             the plan's scratch (:539-549) and later calls read that copy: batches start at
+ *             chunk 0 with the same d_mix; stg_finish maps the stems back (:638-642).
  *   RoFormer  input  feat  [sum_b din_b * T] band-major (src/roformer.cpp:226-241);
  *             output the per-band masks, the plan's mask layout (:251-269).
  *   TFC-TDF   input  in    [4][dim_f][T], bins below zero_bins 0 (src/tfc_tdf.cpp:366-376);

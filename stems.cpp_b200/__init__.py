@@ -42,7 +42,8 @@ class Cancelled(StemsError):
 
 class HTDemucsConfig(C.Structure):
     _fields_ = [("size", C.c_uint32), ("n_channels", C.c_int32), ("n_sources", C.c_int32),
-                ("segment", C.c_int32), ("overlap", C.c_float)]
+                ("segment", C.c_int32), ("overlap", C.c_float), ("mono_norm", C.c_int32),
+                ("cac_norm", C.c_int32)]
 
 
 class RoFormerConfig(C.Structure):
@@ -251,8 +252,12 @@ class Engine:
         return y
 
     # -- plans ---------------------------------------------------------------------------
-    def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0):
-        cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap)
+    def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0,
+                      mono_norm=True, cac_norm=True):
+        """HTDemucs.separate (src/htdemucs.cpp:534-642). Both normalisations are on by default,
+        as in the reference; mono_norm / cac_norm False leave the mix / spectrogram raw."""
+        cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap,
+                             int(bool(mono_norm)), int(bool(cac_norm)))
         h = C.c_void_p()
         self._check(lib().stg_plan_htdemucs(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_htdemucs")
         return Plan(self, h)

@@ -80,6 +80,8 @@ struct stg_plan {
     PlanDevice D;
     DevBuf d_chunks, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
+    DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
+    const float* mono_src = nullptr;                  // the track d_mixn was normalised from
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
@@ -101,6 +103,18 @@ struct stg_plan {
         upload(d_binv, H.binv, "band table");
         d_y.reserve(std::max<size_t>(16, H.y_bytes()), "chunk outputs");
         d_tr.reserve(std::max<size_t>(16, H.tr_bytes()), "tile partials");
+        if (H.mono_norm) {
+            d_mixn.reserve(H.mixn_bytes(), "normalised mix");
+            d_mono.reserve(H.mono_bytes(), "mono statistics");
+            D.mixn = d_mixn.as<float>();
+            D.mono = reinterpret_cast<double*>(d_mono.p);
+        }
+        if (H.cac_norm) {
+            d_cac_part.reserve(H.cac_part_bytes(), "CaC partial sums");
+            d_cac_stats.reserve(H.cac_stats_bytes(), "CaC statistics");
+            D.cac_part = reinterpret_cast<double2*>(d_cac_part.p);
+            D.cac_stats = reinterpret_cast<double2*>(d_cac_stats.p);
+        }
         D.chunks = d_chunks.as<ChunkDesc>();
         D.W = d_w.as<float>();
         D.env = d_env.as<float>();
@@ -123,6 +137,20 @@ struct stg_plan {
             for (cudaEvent_t& e : timing.ev)
                 if (!e) cuda_check(cudaEventCreate(&e), "cudaEventCreate");
         launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing);
+    }
+
+    // The mix the front half reads: with the mono normalisation, chunk 0's call normalises
+    // the track into d_mixn and later calls of the same track read it.
+    const float* front_mix(const float* d_mix, int first, cudaStream_t st) {
+        if (!H.mono_norm) return d_mix;
+        if (!d_mix) fail(STG_INVALID_ARGUMENT, "null buffer");
+        if (first == 0) {
+            normalise_mix(H, D, d_mix, st);
+            mono_src = d_mix;
+        } else if (mono_src != d_mix) {
+            fail(STG_INVALID_ARGUMENT, "with the mono normalisation, the first batch must start at chunk 0");
+        }
+        return D.mixn;
     }
 };
 
@@ -267,7 +295,8 @@ STG_API stg_status stg_plan_get_info(const stg_plan* p, stg_plan_info* info) {
     info->n_frames = H.g.T;
     info->mask_floats_per_chunk = H.mask_per_chunk;
     info->out_floats = H.out_floats();
-    info->scratch_bytes = (int64_t)(p->d_y.bytes + p->d_tr.bytes);
+    info->scratch_bytes = (int64_t)(p->d_y.bytes + p->d_tr.bytes + p->d_mixn.bytes + p->d_mono.bytes +
+                                    p->d_cac_part.bytes + p->d_cac_stats.bytes);
     return STG_OK;
 }
 
@@ -318,7 +347,8 @@ STG_API stg_status stg_front(stg_plan* p, const float* d_mix, int32_t first, int
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] {
         cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
-        launch_front(p->H, p->D, d_mix, first, n, d_net_in, static_cast<cudaStream_t>(stream));
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        launch_front(p->H, p->D, p->front_mix(d_mix, first, st), first, n, d_net_in, st);
     });
 }
 
@@ -356,7 +386,7 @@ STG_API stg_status stg_separate_network(stg_plan* p, const float* d_mix, float* 
         for (int b0 = 0; b0 < G; b0 += per) {
             if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
             const int nb = std::min(per, G - b0);
-            launch_front(H, p->D, d_mix, b0, nb, p->n_in.as<float>(), st);
+            launch_front(H, p->D, p->front_mix(d_mix, b0, st), b0, nb, p->n_in.as<float>(), st);
             if (network(user, b0, nb, p->n_in.as<float>(), p->n_out.as<float>(), stream) != 0)
                 fail(STG_MODEL_ERROR, "the network callback failed");
             launch_back(H, p->D, d_mix, p->n_out.as<float>(), b0, nb, st);

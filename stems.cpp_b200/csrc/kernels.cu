@@ -134,9 +134,23 @@ template <int ARCH, int N, int T> struct MaskOp {
             yr = cmul(zr, cscale(ar, w));
             if (p.zero_dc && f == 0) { yl = make_float2(0.f, 0.f); yr = yl; }      // :278
         } else if constexpr (ARCH == ARCH_HTDEMUCS) {
-            // network output ox = Z * M; the Nyquist bin is dropped (src/stft.h:126)
-            yl = cmul(zl, make_float2(a[i].x, a[i].y));
-            yr = cmul(zr, make_float2(a[i].z, a[i].w));
+            // network output ox = Z * M; the Nyquist bin is dropped (src/stft.h:126). With the
+            // CaC normalisation the stand-in sees (Z - mean) / (1e-5 + std) and its output is
+            // mapped back by ox * std + mean on both parts (src/htdemucs.cpp:434-436, 469).
+            if (p.cac_stats) {
+                const double2 st = p.cac_stats[ci];
+                const float mean = (float)st.x, sd = (float)st.y, inv = (float)(1.0 / (1e-5 + st.y));
+                zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
+                zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
+                yl = cmul(zl, make_float2(a[i].x, a[i].y));
+                yr = cmul(zr, make_float2(a[i].z, a[i].w));
+                yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
+                yr = p.n_channels == 2 ? make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean))
+                                       : make_float2(0.f, 0.f);
+            } else {
+                yl = cmul(zl, make_float2(a[i].x, a[i].y));
+                yr = cmul(zr, make_float2(a[i].z, a[i].w));
+            }
             if (f >= N / 2) { yl = make_float2(0.f, 0.f); yr = yl; }
         } else {
             // y = in * mask per CaC plane; zero below zero_bins and from dim_f up (the loads
@@ -362,6 +376,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
         float v = acc[k] * inv;
         if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
         v *= p.compensate;
+        if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
         outv[k] = v;
         p.out[(int64_t)k * p.len + i] = v;
     }

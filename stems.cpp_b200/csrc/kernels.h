@@ -76,6 +76,8 @@ struct FusedParams {
     int64_t stem_stride;       // floats per stem within a chunk's mask block
     // TFC-TDF
     int dim_f, zero_bins;
+    // HTDemucs CaC normalisation: (mean, std) of every chunk's spectrogram, or null
+    const double2* cac_stats;
     // outputs
     float* Y;                  // [chunk][S*C][Lout]
     int64_t y_chunk_stride;
@@ -103,6 +105,7 @@ struct CombineParams {
     float compensate;          // multiplies the stems (1 = off)
     int complement;            // 1: first stem; 2: all stems (TFC-TDF) subtracted from the mix
     const float* mix;          // for the complement
+    const double* mono_stats;  // HTDemucs mono-mix normalisation (mean, std), or null
     float* out;                // [S(+1)][C][len]
 };
 
@@ -114,7 +117,8 @@ enum FrontLayout : int {
     FRONT_COMPLEX = 0,   // complex [C][F][T], F = n_bins (torch_stft, htdemucs_spec)
     FRONT_CAC = 1,       // float planes [2C][F][T]: re = 2c, im = 2c + 1 (HTDemucs input)
     FRONT_BANDS = 2,     // RoFormer band-major features [sum_b din_b * T]
-    FRONT_TFC = 3        // float planes [4][dim_f][T], bins below zero_bins 0 (TFC-TDF input)
+    FRONT_TFC = 3,       // float planes [4][dim_f][T], bins below zero_bins 0 (TFC-TDF input)
+    FRONT_STATS = 4      // no output: (sum, sum of squares) of the CaC values per (chunk, tile)
 };
 enum BackLayout : int {
     BACK_COMPLEX = 0,    // complex [C][F][T] (torch_istft, htdemucs_ispec)
@@ -145,6 +149,8 @@ struct SplitParams {
     const int2* bin_ent;
     float* net;                // front: written; back: read
     int64_t net_chunk_stride;
+    const double2* cac_stats;  // FRONT_CAC / BACK_CAC: per-chunk (mean, std), or null
+    double2* stats_out;        // FRONT_STATS: [chunk][tile] partial sums
     float* Y;                  // back
     int64_t y_chunk_stride;
     float* Tr;
@@ -164,5 +170,13 @@ int fused_resident_ctas(int arch, int n_fft);
 // The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
+
+// norm.cu. Mono-mix normalisation of mix [C][len] into out, with scratch of
+// mono_scratch_doubles() doubles (scratch[0] = mean, scratch[1] = std afterwards).
+size_t mono_scratch_doubles();
+cudaError_t launch_mono_norm(const float* mix, int64_t len, int C, double* scratch, float* out, cudaStream_t st);
+// Per-chunk (mean, std) of the CaC values from the FRONT_STATS partials ([chunk][tile]).
+cudaError_t launch_cac_finish(const double2* partial, int n_chunks, int n_tiles, double count, double2* stats,
+                              cudaStream_t st);
 
 } // namespace stg

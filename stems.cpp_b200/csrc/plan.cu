@@ -113,6 +113,8 @@ void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     if (stride <= 0) fail(STG_INVALID_ARGUMENT, "overlap must be < 1");
     P.arch = ARCH_HTDEMUCS;
     P.C = c.n_channels; P.S = c.n_sources; P.S_out = P.S;
+    P.mono_norm = c.mono_norm != 0;                                   // :539-549, 638-642
+    P.cac_norm = c.cac_norm != 0;                                     // :434-436, 466-469
     P.g = FrameGeom{N, hl, seg, T, 2 * hl, pad, 2 * pad + T * hl, N / 2 + pad, seg};
     P.fwd_scale = (float)(1.0 / std::sqrt((double)N));                // stft.h:91
     P.inv_scale = (float)(std::sqrt((double)N) / N);                  // stft.h:116
@@ -422,10 +424,45 @@ void build_htdemucs_spec(HostPlan& P, int n_channels, int64_t len) {
     finish_plan(P, T + 4);
 }
 
-void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
+namespace {
+SplitParams split_params(const HostPlan& P, const PlanDevice& D, const float* d_mix, int first, int n);
+
+// The (mean, std) of every chunk of [first, first + n) over its 2C x F x T CaC values
+// (src/htdemucs.cpp:434-435): a front pass that only sums, then the per-chunk finish.
+int cac_statistics(const HostPlan& P, const PlanDevice& D, const float* mix, int first, int n, cudaStream_t st) {
+    if (!D.cac_part || !D.cac_stats) fail(STG_INTERNAL_ERROR, "no scratch for the CaC normalisation");
+    SplitParams s = split_params(P, D, mix, first, n);
+    s.layout = FRONT_STATS;
+    s.n_bins = P.front_bins;
+    s.stats_out = D.cac_part + (int64_t)first * P.n_tiles;
+    cuda_check(stg::launch_front(s, st), "CaC statistics launch");
+    const double count = 2.0 * P.C * P.front_bins * P.g.T;
+    cuda_check(launch_cac_finish(s.stats_out, n, P.n_tiles, count, D.cac_stats + first, st), "CaC statistics launch");
+    return 2;
+}
+} // namespace
+
+const float* normalise_mix(const HostPlan& P, const PlanDevice& D, const float* d_mix, cudaStream_t st) {
+    if (!P.mono_norm) return d_mix;
+    if (!D.mixn || !D.mono) fail(STG_INTERNAL_ERROR, "no scratch for the mono normalisation");
+    cuda_check(launch_mono_norm(d_mix, P.len, P.C, D.mono, D.mixn, st), "mono normalisation launch");
+    return D.mixn;
+}
+
+void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing) {
-    if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+    if (!d_mix_in || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
     if (reinterpret_cast<uintptr_t>(d_mask) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+    const bool timed = timing && timing->timed;
+    if (timing) timing->launches = 0;
+    if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
+    const float* d_mix = normalise_mix(P, D, d_mix_in, st);
+    if (timing && P.mono_norm) timing->launches += 5;
+    const int G = (int)P.chunks.size();
+    if (P.cac_norm) {
+        const int k = cac_statistics(P, D, d_mix, 0, G, st);
+        if (timing) timing->launches += k;
+    }
     FusedParams f{};
     f.mix = d_mix; f.len = P.len; f.n_channels = P.C; f.reflect_global = P.reflect_global;
     f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
@@ -438,11 +475,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
     f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
     f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
-    const int G = (int)P.chunks.size();
     const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : G;
-    const bool timed = timing && timing->timed;
-    if (timing) timing->launches = 0;
-    if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
     for (int b0 = 0; b0 < G; b0 += per) {
         if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
         const int nb = std::min(per, G - b0);
@@ -451,6 +484,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
         f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
         f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
         f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
+        f.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
         cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
         if (timing) timing->launches++;
         if (opt && opt->on_progress) {
@@ -468,6 +502,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     c.S = P.S; c.C = P.C; c.len = P.len; c.out_shift = P.out_shift;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    c.mono_stats = P.mono_norm ? D.mono : nullptr;
     if (timed) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
     cuda_check(launch_combine(c, st), "combine kernel launch");
     if (timing) timing->launches++;
@@ -518,10 +553,12 @@ void launch_front(const HostPlan& P, const PlanDevice& D, const float* d_mix, in
     if (P.front_layout == FRONT_BANDS && reinterpret_cast<uintptr_t>(d_net_in) % 16)
         fail(STG_INVALID_ARGUMENT, "the feature buffer must be 16-byte aligned");
     SplitParams s = split_params(P, D, d_mix, first, n);
+    if (P.cac_norm) cac_statistics(P, D, d_mix, first, n, st);
     s.layout = P.front_layout;
     s.n_bins = P.front_bins;
     s.net = d_net_in;
     s.net_chunk_stride = P.net_in_per_chunk;
+    s.cac_stats = P.cac_norm ? D.cac_stats + first : nullptr;
     cuda_check(stg::launch_front(s, st), "front kernel launch");
 }
 
@@ -553,6 +590,7 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     s.n_bins = P.back_bins;
     s.net = const_cast<float*>(d_net_out);
     s.net_chunk_stride = P.net_out_per_chunk;
+    s.cac_stats = P.cac_norm ? D.cac_stats + first : nullptr;
     cuda_check(stg::launch_back(s, st), "back kernel launch");
 }
 
@@ -569,6 +607,7 @@ void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, f
     c.out_shift = P.out_shift;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    c.mono_stats = P.mono_norm ? D.mono : nullptr;
     cuda_check(launch_combine(c, st), "combine kernel launch");
 }
 

@@ -41,6 +41,7 @@ struct HostPlan {
     int nan_to_zero = 0, complement = 0;
     float compensate = 1.0f;
     int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
+    int mono_norm = 0, cac_norm = 0;   // HTDemucs: mono-mix and CaC normalisation
     int64_t stem_stride = 0;
     int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
     std::vector<float> W;          // crossfade weight tables (ChunkDesc::w_off)
@@ -61,6 +62,12 @@ struct HostPlan {
     int64_t out_floats() const { return (int64_t)S_out * C * len; }
     size_t y_bytes() const { return sizeof(float) * (size_t)y_chunk_stride * chunks.size(); }
     size_t tr_bytes() const { return sizeof(float) * (size_t)tr_chunk_stride * chunks.size(); }
+    // scratch of the normalisations: the normalised mix, the mono statistics, the CaC partial
+    // sums ([chunk][tile]) and the CaC statistics ([chunk])
+    size_t mixn_bytes() const { return mono_norm ? sizeof(float) * (size_t)C * len : 0; }
+    size_t mono_bytes() const { return mono_norm ? sizeof(double) * mono_scratch_doubles() : 0; }
+    size_t cac_part_bytes() const { return cac_norm ? sizeof(double2) * (size_t)n_tiles * chunks.size() : 0; }
+    size_t cac_stats_bytes() const { return cac_norm ? sizeof(double2) * chunks.size() : 0; }
 };
 
 // Where the device copies of a plan's tables and scratch live.
@@ -76,6 +83,10 @@ struct PlanDevice {
     const float2* tw = nullptr;    // FFT twiddles (fft_tables)
     float* Y = nullptr;            // scratch: chunk outputs
     float* Tr = nullptr;           // scratch: tile-boundary partials
+    float* mixn = nullptr;         // scratch: the mono-normalised mix (HostPlan::mono_norm)
+    double* mono = nullptr;        // scratch: mono statistics, mean and std at [0], [1]
+    double2* cac_part = nullptr;   // scratch: CaC partial sums (HostPlan::cac_norm)
+    double2* cac_stats = nullptr;  // scratch: per-chunk CaC (mean, std)
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
@@ -107,6 +118,9 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
 // network's input (net_in_per_chunk floats per chunk) into d_net_in; the back reads its
 // output (net_out_per_chunk floats per chunk) and leaves the chunks' results in the scratch;
 // finish (the combine) produces the separation once every chunk went through the back.
+// With HostPlan::mono_norm, d_mix of launch_front and launch_back is the normalised mix that
+// normalise_mix left in D.mixn; normalise_mix returns the mix the kernels read.
+const float* normalise_mix(const HostPlan& P, const PlanDevice& D, const float* d_mix, cudaStream_t st);
 void launch_front(const HostPlan& P, const PlanDevice& D, const float* d_mix, int first, int n,
                   float* d_net_in, cudaStream_t st);
 void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_net_out, int first,

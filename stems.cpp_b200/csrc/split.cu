@@ -37,6 +37,12 @@ __device__ __forceinline__ void front_store(const SplitParams& p, const int2* bt
             break;
         case FRONT_CAC:
             if (f < p.n_bins) {
+                if (p.cac_stats) {   // (v - mean) / (1e-5 + std) (src/htdemucs.cpp:436)
+                    const double2 st = p.cac_stats[ci];
+                    const float mean = (float)st.x, inv = (float)(1.0 / (1e-5 + st.y));
+                    zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
+                    zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
+                }
                 out[idx] = zl.x;
                 out[plane + idx] = zl.y;
                 if (C > 1) {
@@ -97,6 +103,13 @@ __device__ __forceinline__ void back_load(const SplitParams& p, int ci, int s, i
             const float* q = in + (int64_t)s * 2 * C * plane + idx;
             yl = make_float2(q[0], q[plane]);
             if (C > 1) yr = make_float2(q[2 * plane], q[3 * plane]);
+            if (p.cac_stats) {   // v * std + mean (src/htdemucs.cpp:469)
+                const double2 st = p.cac_stats[ci];
+                const float mean = (float)st.x, sd = (float)st.y;
+                yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
+                yr = make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean));
+                if (C == 1) yr = make_float2(0.f, 0.f);
+            }
             break;
         }
         default: {   // BACK_TFC
@@ -128,11 +141,13 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
     if (p.layout == FRONT_BANDS)
         for (int i = tid; i < p.n_bins; i += T) btab[i] = __ldg(p.bin_tab + i);
     InPrefetch<T, FftCfg<N>::HOPMAX> nx;
+    __shared__ double red[2 * (T / 32)];
 
     for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
         const int tile = item % p.n_tiles, ci = item / p.n_tiles;
         const ChunkDesc cd = p.chunks[ci];
         const int t_begin = tile * p.K, t_end = min(G.T, t_begin + p.K);
+        double acc_s = 0.0, acc_q = 0.0;   // FRONT_STATS
         {
             const int q0 = G.first_pos + t_begin * hop;
             for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = frame_sample(p, cd, chL, chR, lxf, q0 + n);
@@ -175,7 +190,30 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
                 const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
                 const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
                 const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
-                front_store<N>(p, btab, ci, t, f, zl, zr);
+                if (p.layout == FRONT_STATS) {
+                    acc_s += (double)zl.x + (double)zl.y;
+                    acc_q += (double)zl.x * zl.x + (double)zl.y * zl.y;
+                    if (C > 1) {
+                        acc_s += (double)zr.x + (double)zr.y;
+                        acc_q += (double)zr.x * zr.x + (double)zr.y * zr.y;
+                    }
+                } else {
+                    front_store<N>(p, btab, ci, t, f, zl, zr);
+                }
+            }
+            __syncthreads();
+        }
+        if (p.layout == FRONT_STATS) {   // block sums in a fixed order, one partial per item
+            for (int o = 16; o > 0; o >>= 1) {
+                acc_s += __shfl_down_sync(0xffffffffu, acc_s, o);
+                acc_q += __shfl_down_sync(0xffffffffu, acc_q, o);
+            }
+            if ((tid & 31) == 0) { red[2 * (tid >> 5)] = acc_s; red[2 * (tid >> 5) + 1] = acc_q; }
+            __syncthreads();
+            if (tid == 0) {
+                double s = 0.0, q = 0.0;
+                for (int w = 0; w < T / 32; w++) { s += red[2 * w]; q += red[2 * w + 1]; }
+                p.stats_out[(int64_t)ci * p.n_tiles + tile] = make_double2(s, q);
             }
             __syncthreads();
         }

@@ -71,7 +71,8 @@ def test_cfg0_htdemucs_20s(engine, oracle_mod):
     assert plan.n_chunks == 4 and plan.n_frames == 336
     mix = synth_audio(5, n)
     mask = synth_mask(6, plan.mask_floats, 1.0)
-    want = oracle_mod.ht_separate(oracle_mod.ht_params(n_sources=4, segment=343980, threads=THREADS), mix, mask)
+    p = oracle_mod.ht_params(n_sources=4, segment=343980, mono_norm=1, cac_norm=1, threads=THREADS)
+    want = oracle_mod.ht_separate(p, mix, mask)
     _check(_gpu(plan, mix, mask), want, "cfg0")
 
 
@@ -91,7 +92,7 @@ def test_cfg4_batch_htdemucs_two_tracks(engine, oracle_mod):
     n = 240 * SR
     plan = engine.plan_htdemucs(n, n_sources=4, segment=343980)
     assert plan.n_chunks == 42
-    p = oracle_mod.ht_params(n_sources=4, segment=343980, threads=THREADS)
+    p = oracle_mod.ht_params(n_sources=4, segment=343980, mono_norm=1, cac_norm=1, threads=THREADS)
     for track in range(2):
         mix = synth_audio(40 + track, n)
         mask = synth_mask(50 + track, plan.mask_floats, 1.0)

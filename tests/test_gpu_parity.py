@@ -63,21 +63,27 @@ def test_roformer_matches_oracle(case, pkg, engine, oracle_mod):
 
 # ---- HTDemucs ------------------------------------------------------------------------------
 HT_CASES = [
-    # name, segment, length, sources, overlap
-    ("seg24k_4src", 1024 * 24, 60000, 4, -1.0),
-    ("seg24k_short", 1024 * 24, 9000, 2, -1.0),          # one segment, centre-padded
-    ("seg_odd_ov05", 1024 * 20 + 333, 51001, 4, 0.5),
+    # name, segment, length, sources, overlap, channels, mono_norm, cac_norm
+    ("seg24k_4src", 1024 * 24, 60000, 4, -1.0, 2, 1, 1),   # the reference's normalisations
+    ("seg24k_raw", 1024 * 24, 60000, 4, -1.0, 2, 0, 0),
+    ("seg24k_short", 1024 * 24, 9000, 2, -1.0, 2, 1, 1),   # one segment, centre-padded
+    ("seg_odd_ov05", 1024 * 20 + 333, 51001, 4, 0.5, 2, 1, 1),
+    ("seg24k_mono_norm_only", 1024 * 24, 70001, 4, -1.0, 2, 1, 0),
+    ("seg24k_cac_norm_only", 1024 * 24, 70001, 6, -1.0, 2, 0, 1),
+    ("seg24k_one_channel", 1024 * 24, 60000, 4, -1.0, 1, 1, 1),
 ]
 
 
 @pytest.mark.parametrize("case", HT_CASES, ids=[c[0] for c in HT_CASES])
 def test_htdemucs_matches_oracle(case, pkg, engine, oracle_mod):
-    name, seg, length, S, ov = case
-    plan = engine.plan_htdemucs(length, n_sources=S, segment=seg, overlap=ov)
-    mix = synth_audio(21, length)
+    name, seg, length, S, ov, ch, mono, cac = case
+    plan = engine.plan_htdemucs(length, n_channels=ch, n_sources=S, segment=seg, overlap=ov, mono_norm=mono,
+                                cac_norm=cac)
+    mix = synth_audio(21, length, channels=ch)
     mask = synth_mask(22, plan.mask_floats, 1.0)
     got = run_gpu(plan, mix, mask)
-    p = oracle_mod.ht_params(n_sources=S, segment=seg, overlap=ov, threads=8)
+    p = oracle_mod.ht_params(n_channels=ch, n_sources=S, segment=seg, overlap=ov, mono_norm=mono, cac_norm=cac,
+                             threads=8)
     assert plan.n_chunks == oracle_mod.ht_n_segments(p, length)
     want = oracle_mod.ht_separate(p, mix, mask)
     check(got, want, name)

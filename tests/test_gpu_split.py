@@ -85,7 +85,7 @@ def test_htdemucs_front_cac(engine, oracle_mod):
     import torch
     seg = 343980
     n = seg + 100000
-    plan = engine.plan_htdemucs(n, n_sources=4, segment=seg)
+    plan = engine.plan_htdemucs(n, n_sources=4, segment=seg, mono_norm=False, cac_norm=False)
     n_in, n_out = plan.network_info()
     assert n_out == plan.mask_floats_per_chunk
     mix = synth_audio(64, n)
@@ -97,6 +97,37 @@ def test_htdemucs_front_cac(engine, oracle_mod):
     for c in range(2):
         z = oracle_mod.htdemucs_spec(mix[c, :seg])
         assert _rel(got[2 * c], z.real) <= TOL and _rel(got[2 * c + 1], z.imag) <= TOL
+
+
+def test_htdemucs_front_cac_normalised(engine, oracle_mod):
+    """The front half with both normalisations: the mix divided by its mono std, then the
+    segment's CaC planes mapped to (v - mean) / (1e-5 + std) (src/htdemucs.cpp:434-436, 539-549)."""
+    import torch
+    seg = 1024 * 24
+    n = 3 * seg
+    plan = engine.plan_htdemucs(n, n_sources=4, segment=seg)
+    n_in, _ = plan.network_info()
+    mix = synth_audio(71, n)
+    cac = torch.empty(n_in * 2, device="cuda")
+    d_mix = torch.from_numpy(mix).cuda()
+    plan.front(d_mix, 0, 2, cac)
+    torch.cuda.synchronize()
+    T = plan.n_frames
+    mono = mix.astype(np.float64).mean(axis=0).astype(np.float32).astype(np.float64)
+    mixn = ((mix - mono.mean()) / mono.std(ddof=1)).astype(np.float32)
+    stride = int(0.75 * seg)
+    for k in range(2):
+        planes = np.concatenate([
+            np.stack([z.real, z.imag]) for z in
+            (oracle_mod.htdemucs_spec(mixn[c, k * stride:k * stride + seg]) for c in range(2))])
+        v = planes.astype(np.float32).astype(np.float64)
+        want = (v - v.mean()) / (1e-5 + v.std(ddof=1))
+        got = cac[k * n_in:(k + 1) * n_in].cpu().numpy().reshape(4, 2048, T)
+        assert _rel(got, want) <= TOL, f"segment {k}"
+    # a later batch of the same track reads the normalised copy; a different track may not
+    plan.front(d_mix, 1, 1, cac)
+    with pytest.raises(Exception):
+        plan.front(d_mix.clone(), 1, 1, cac)
 
 
 # ---- whole separations through the network callback -----------------------------------------
@@ -139,10 +170,11 @@ def test_roformer_network_loop_matches_fused(pkg, engine, oracle_mod):
     assert max_rel_err(got, oracle_mod.rf_separate(p, mix, mask)) <= TOL
 
 
-def test_htdemucs_network_loop(engine, oracle_mod):
+@pytest.mark.parametrize("norm", [False, True], ids=["raw", "normalised"])
+def test_htdemucs_network_loop(engine, oracle_mod, norm):
     import torch
     seg, n, S = 1024 * 24, 60000, 4
-    plan = engine.plan_htdemucs(n, n_sources=S, segment=seg)
+    plan = engine.plan_htdemucs(n, n_sources=S, segment=seg, mono_norm=norm, cac_norm=norm)
     mix = synth_audio(67, n)
     mask = synth_mask(68, plan.mask_floats, 1.0)
     d_mask = torch.from_numpy(mask).cuda()
@@ -157,7 +189,7 @@ def test_htdemucs_network_loop(engine, oracle_mod):
         _view(p_out, k * n_out).view(k, S, 2, 2, 2048, T).copy_(torch.stack([re, im], dim=3))
 
     got = _run_network(plan, mix, net, per_batch=2)
-    p = oracle_mod.ht_params(n_sources=S, segment=seg, threads=8)
+    p = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=int(norm), cac_norm=int(norm), threads=8)
     assert max_rel_err(got, oracle_mod.ht_separate(p, mix, mask)) <= TOL
 
 
