@@ -70,10 +70,17 @@ STG_API const char* stg_engine_last_error(const stg_engine* engine);
 /* Kernel timing, the counterpart of the reference's wall-clock timers
  * (tools/stems-split.cpp:94-97): when enabled, every run records CUDA events around its
  * kernels on the run's stream; stg_plan_last_timing waits for the last run and returns the
- * milliseconds of the fused spectral kernels and of the combine kernel. */
+ * milliseconds of the kernels before the combine (the fused spectral kernels and their
+ * preparation) and of the combine kernel. */
 STG_API stg_status stg_engine_set_profiling(stg_engine* engine, int32_t enabled);
 STG_API stg_status stg_plan_last_timing(stg_plan* plan, float* fused_ms, float* combine_ms,
                                         int32_t* kernel_launches);
+/* The same run split three ways: prep_ms = the kernels before the first fused launch (HTDemucs
+ * normalisations, the first batch's mask transposition), fused_ms = from the first fused launch
+ * to the combine (later batches' transpositions included), combine_ms = the combine. No
+ * reference counterpart beyond the timers of stg_plan_last_timing. */
+STG_API stg_status stg_plan_last_timing_detail(stg_plan* plan, float* prep_ms, float* fused_ms,
+                                               float* combine_ms, int32_t* kernel_launches);
 
 /* ---- model configurations (the GGUF metadata the reference reads) ------------------------ */
 

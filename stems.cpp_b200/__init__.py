@@ -95,6 +95,8 @@ _SIGNATURES = {
     "stg_engine_set_profiling": (C.c_int32, [C.c_void_p, C.c_int32]),
     "stg_plan_last_timing": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float),
                                          C.POINTER(C.c_int32)]),
+    "stg_plan_last_timing_detail": (C.c_int32, [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                                C.POINTER(C.c_float), C.POINTER(C.c_int32)]),
     "stg_plan_htdemucs": (C.c_int32, [C.c_void_p, C.POINTER(HTDemucsConfig), C.c_int64, C.POINTER(C.c_void_p)]),
     "stg_plan_roformer": (C.c_int32, [C.c_void_p, C.POINTER(RoFormerConfig), C.c_int64, C.POINTER(C.c_void_p)]),
     "stg_plan_tfc": (C.c_int32, [C.c_void_p, C.POINTER(TFCConfig), C.c_int64, C.POINTER(C.c_void_p)]),
@@ -374,11 +376,18 @@ class Plan:
         return out
 
     def last_timing(self):
-        """(fused kernel ms, combine kernel ms, kernel launches) of the last run."""
+        """(ms before the combine, combine kernel ms, kernel launches) of the last run."""
         a, b, n = C.c_float(), C.c_float(), C.c_int32()
         self.engine._check(lib().stg_plan_last_timing(self._h, C.byref(a), C.byref(b), C.byref(n)),
                            "last_timing")
         return a.value, b.value, n.value
+
+    def last_timing_detail(self):
+        """(preparation ms, fused kernel ms, combine kernel ms, kernel launches) of the last run."""
+        a, b, c, n = C.c_float(), C.c_float(), C.c_float(), C.c_int32()
+        self.engine._check(lib().stg_plan_last_timing_detail(self._h, C.byref(a), C.byref(b), C.byref(c),
+                                                             C.byref(n)), "last_timing_detail")
+        return a.value, b.value, c.value, n.value
 
     def separate_host_ptr(self, h_mix: int, h_mask: int, h_out: int, stream=None):
         """Host pointers (e.g. pinned torch tensors' data_ptr()); blocks until h_out is filled."""

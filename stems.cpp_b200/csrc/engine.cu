@@ -81,6 +81,7 @@ struct stg_plan {
     DevBuf d_chunks, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
     DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
+    DevBuf d_mask_t;                                  // t-major masks (HTDemucs, TFC-TDF)
     const float* mono_src = nullptr;                  // the track d_mixn was normalised from
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
@@ -108,6 +109,10 @@ struct stg_plan {
             d_mono.reserve(H.mono_bytes(), "mono statistics");
             D.mixn = d_mixn.as<float>();
             D.mono = reinterpret_cast<double*>(d_mono.p);
+        }
+        if (H.mask_planes) {
+            d_mask_t.reserve(H.mask_t_bytes(), "t-major masks");
+            D.mask_t = reinterpret_cast<float4*>(d_mask_t.p);
         }
         if (H.cac_norm) {
             d_cac_part.reserve(H.cac_part_bytes(), "CaC partial sums");
@@ -258,12 +263,28 @@ STG_API stg_status stg_plan_last_timing(stg_plan* p, float* fused_ms, float* com
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] {
         if (!p->timing.timed) fail(STG_INVALID_ARGUMENT, "the last run was not timed (stg_engine_set_profiling)");
-        cuda_check(cudaEventSynchronize(p->timing.ev[2]), "cudaEventSynchronize");
+        cuda_check(cudaEventSynchronize(p->timing.ev[3]), "cudaEventSynchronize");
         float a = 0.0f, b = 0.0f;
-        cuda_check(cudaEventElapsedTime(&a, p->timing.ev[0], p->timing.ev[1]), "cudaEventElapsedTime");
-        cuda_check(cudaEventElapsedTime(&b, p->timing.ev[1], p->timing.ev[2]), "cudaEventElapsedTime");
+        cuda_check(cudaEventElapsedTime(&a, p->timing.ev[0], p->timing.ev[2]), "cudaEventElapsedTime");
+        cuda_check(cudaEventElapsedTime(&b, p->timing.ev[2], p->timing.ev[3]), "cudaEventElapsedTime");
         if (fused_ms) *fused_ms = a;
         if (combine_ms) *combine_ms = b;
+        if (launches) *launches = p->timing.launches;
+    });
+}
+
+STG_API stg_status stg_plan_last_timing_detail(stg_plan* p, float* prep_ms, float* fused_ms, float* combine_ms,
+                                               int32_t* launches) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        if (!p->timing.timed) fail(STG_INVALID_ARGUMENT, "the last run was not timed (stg_engine_set_profiling)");
+        cuda_check(cudaEventSynchronize(p->timing.ev[3]), "cudaEventSynchronize");
+        float t[3] = {0.0f, 0.0f, 0.0f};
+        for (int k = 0; k < 3; k++)
+            cuda_check(cudaEventElapsedTime(&t[k], p->timing.ev[k], p->timing.ev[k + 1]), "cudaEventElapsedTime");
+        if (prep_ms) *prep_ms = t[0];
+        if (fused_ms) *fused_ms = t[1];
+        if (combine_ms) *combine_ms = t[2];
         if (launches) *launches = p->timing.launches;
     });
 }
@@ -296,7 +317,7 @@ STG_API stg_status stg_plan_get_info(const stg_plan* p, stg_plan_info* info) {
     info->mask_floats_per_chunk = H.mask_per_chunk;
     info->out_floats = H.out_floats();
     info->scratch_bytes = (int64_t)(p->d_y.bytes + p->d_tr.bytes + p->d_mixn.bytes + p->d_mono.bytes +
-                                    p->d_cac_part.bytes + p->d_cac_stats.bytes);
+                                    p->d_cac_part.bytes + p->d_cac_stats.bytes + p->d_mask_t.bytes);
     return STG_OK;
 }
 

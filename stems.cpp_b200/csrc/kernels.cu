@@ -73,40 +73,19 @@ template <int ARCH, int N, int T> struct MaskOp {
                     }
                 }
             }
-        } else if constexpr (ARCH == ARCH_HTDEMUCS) {
-            // src/htdemucs.cpp:463-469: planes [S][2C][F][T], re = 2c, im = 2c + 1.
-            const int F = N / 2;
-            const int64_t plane = (int64_t)F * p.g.T;
-            const float* ms = m + (int64_t)s * 2 * p.n_channels * plane + t;
-#pragma unroll
-            for (int i = 0; i < BPT; i++) {
-                if (i < i0 || i >= i1) continue;
-                const int f = tid + i * T;
-                a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (f < F) {
-                    const float* q = ms + (int64_t)f * p.g.T;
-                    a[i].x = ld_stream(q);
-                    a[i].y = ld_stream(q + plane);
-                    if (p.n_channels == 2) {
-                        a[i].z = ld_stream(q + 2 * plane);
-                        a[i].w = ld_stream(q + 3 * plane);
-                    }
-                }
-            }
         } else {
-            // src/tfc_tdf.cpp:370-387: real planes [4S][dim_f][T]: L re, L im, R re, R im.
-            const int64_t plane = (int64_t)p.dim_f * p.g.T;
-            const float* ms = m + (int64_t)s * 4 * plane + t;
+            // HTDemucs ox planes [S][2C][F][T] (src/htdemucs.cpp:463-469) and TFC-TDF y planes
+            // [4S][dim_f][T] (src/tfc_tdf.cpp:370-387), rewritten t-major by mask_transpose:
+            // [S][T][F] float4 (L re, L im, R re, R im), so frame t's bins are contiguous.
+            const int F = ARCH == ARCH_HTDEMUCS ? N / 2 : p.dim_f;
+            const int f_lo = ARCH == ARCH_HTDEMUCS ? 0 : p.zero_bins;
+            const float* ms = m + ((int64_t)s * p.g.T + t) * F * 4;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
                 if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (f >= p.zero_bins && f < p.dim_f) {
-                    const float* q = ms + (int64_t)f * p.g.T;
-                    a[i] = make_float4(ld_stream(q), ld_stream(q + plane), ld_stream(q + 2 * plane),
-                                       ld_stream(q + 3 * plane));
-                }
+                if (f >= f_lo && f < F) a[i] = ld_stream4(ms + 4 * f);
             }
         }
     }
@@ -512,6 +491,48 @@ cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st) {
             break;
     }
     return cudaErrorInvalidValue;
+}
+
+// ---- mask transposition -------------------------------------------------------------------
+// f-major planes [S][P][F][T] per chunk (t fastest) -> t-major [S][T][F] float4 per chunk,
+// component p = plane p (zero from P up). One CTA moves a 32 x 32 (f, t) tile of every plane:
+// rows read 32 consecutive t (128 bytes), rows written 32 consecutive f (512 bytes of float4).
+constexpr int kTile = 32;
+
+__global__ void __launch_bounds__(256) mask_transpose(const float* __restrict__ in, int64_t in_chunk_stride,
+                                                      int n_cs, int S, int P, int F, int T,
+                                                      float4* __restrict__ out, int64_t out_chunk_stride) {
+    __shared__ float tile[4][kTile][kTile + 1];
+    const int lx = threadIdx.x & 31, ly = threadIdx.x >> 5;
+    const int f0 = blockIdx.y * kTile, t0 = blockIdx.x * kTile;
+    for (int cs = blockIdx.z; cs < n_cs; cs += gridDim.z) {
+        const int ci = cs / S, s = cs - ci * S;
+        const float* src = in + ci * in_chunk_stride + (int64_t)s * P * F * T;
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+            for (int r = ly; r < kTile; r += 8) {
+                const int f = f0 + r, t = t0 + lx;
+                tile[p][r][lx] = (p < P && f < F && t < T) ? ld_stream(src + ((int64_t)p * F + f) * T + t) : 0.0f;
+            }
+        __syncthreads();
+        float4* dst = out + ci * out_chunk_stride + (int64_t)s * T * F;
+        for (int r = ly; r < kTile; r += 8) {
+            const int t = t0 + r, f = f0 + lx;
+            if (t < T && f < F)
+                dst[(int64_t)t * F + f] = make_float4(tile[0][lx][r], tile[1][lx][r], tile[2][lx][r], tile[3][lx][r]);
+        }
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int n_chunks, int S, int P, int F,
+                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st) {
+    if (n_chunks <= 0) return cudaSuccess;
+    if (P < 1 || P > 4 || F < 1 || T < 1 || S < 1) return cudaErrorInvalidValue;
+    const int n_cs = n_chunks * S;
+    const dim3 grid((T + kTile - 1) / kTile, (F + kTile - 1) / kTile, std::min(n_cs, 65535));
+    mask_transpose<<<grid, 256, 0, st>>>(in, in_chunk_stride, n_cs, S, P, F, T, out, out_chunk_stride);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {

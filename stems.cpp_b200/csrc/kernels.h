@@ -60,7 +60,8 @@ struct FusedParams {
     const float2* tw;          // the FFT plan's per-pass twiddles (fft.cuh: twiddle_index)
     const float* inv_env;      // [Lout]: 1 / sum of squared windows, 0 where it vanishes
     float fwd_scale, inv_scale;
-    // mask (the stand-in for the network's output), one block per chunk
+    // mask (the stand-in for the network's output), one block per chunk; HTDemucs and TFC-TDF
+    // masks in the t-major layout of launch_mask_transpose
     const float* mask;
     int64_t mask_chunk_stride;
     // RoFormer: bin -> (band entry) inverse table. bin_tab[f] holds the first two bands holding
@@ -162,6 +163,10 @@ cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st);
 cudaError_t launch_front(const SplitParams& p, cudaStream_t st);
 cudaError_t launch_back(const SplitParams& p, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
+// f-major mask planes [S][P][F][T] per chunk (in_chunk_stride floats apart) -> t-major
+// [S][T][F] float4 per chunk (out_chunk_stride float4 apart), plane p in component p.
+cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int n_chunks, int S, int P, int F,
+                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st);
 size_t fused_smem_bytes(int arch, int n_fft);
 int fused_threads(int n_fft);
 int fused_max_hop(int n_fft);      // the largest hop the fused kernel takes at this n_fft

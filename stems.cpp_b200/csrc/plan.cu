@@ -63,12 +63,20 @@ void finish_plan(HostPlan& P, int env_frames) {
     if (!fused_supported(N)) fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
     if (hop > fused_max_hop(N) || hop > N)
         fail(STG_UNSUPPORTED, "hop " + std::to_string(hop) + " is too large for n_fft " + std::to_string(N));
-    // Frames per tile: 16, halved while the plan has fewer than two work items (chunk, tile)
-    // per resident CTA, so that short inputs still fill the GPU.
-    const int slots = fused_resident_ctas(P.arch, N);
-    P.K = 16;
-    while (P.K > 4 && (int64_t)P.chunks.size() * ((P.g.T + P.K - 1) / P.K) < 2 * (int64_t)slots) P.K /= 2;
-    if (P.K * hop < N - hop) P.K = (N - hop + hop - 1) / hop;   // one tile boundary per sample at most
+    // Frames per tile. The persistent CTAs take work items (chunk, tile) round-robin, so a
+    // launch lasts ceil(items / resident CTAs) rounds of one tile each; a tile costs its K
+    // frames plus about one frame of prologue (the first window) and flush. K is the one in
+    // [K_min, 16] with the shortest critical path, the larger on ties. K_min keeps every
+    // sample within one tile boundary (K * hop >= n_fft - hop).
+    const int64_t slots = std::max(1, fused_resident_ctas(P.arch, N));
+    const int k_min = std::max(1, (N - hop + hop - 1) / hop);
+    P.K = std::max(16, k_min);
+    int64_t best = INT64_MAX;
+    for (int K = std::max(16, k_min); K >= k_min; K--) {
+        const int64_t items = (int64_t)P.chunks.size() * ((P.g.T + K - 1) / K);
+        const int64_t cost = (items + slots - 1) / slots * (K + 1);
+        if (cost < best) { best = cost; P.K = K; }
+    }
     P.n_tiles = (P.g.T + P.K - 1) / P.K;
     P.y_chunk_stride = (int64_t)P.S * P.C * P.g.Lout;
     P.tr_chunk_stride = (int64_t)P.n_tiles * P.S * P.C * (N - hop);
@@ -120,6 +128,8 @@ void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     P.inv_scale = (float)(std::sqrt((double)N) / N);                  // stft.h:116
     P.reflect_global = 0;                                             // padded(): zeros outside
     P.mask_per_chunk = (int64_t)P.S * 2 * P.C * (N / 2) * T;
+    P.mask_planes = 2 * P.C;
+    P.mask_bins = N / 2;
     for (int64_t off = 0; off < len; off += stride) {                 // :592
         const int length = (int)std::min<int64_t>(seg, len - off);
         ChunkDesc d{};
@@ -283,6 +293,8 @@ void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len) {
     P.dim_f = c.dim_f;
     P.zero_bins = c.chunking == 0 ? c.zero_bins : 0;                  // :532
     P.mask_per_chunk = (int64_t)4 * P.S * c.dim_f * c.dim_t;
+    P.mask_planes = 4;
+    P.mask_bins = c.dim_f;
     std::vector<float>& W = P.W;
     if (c.chunking == 0) {                                            // demix_uvr :398-429
         const int trim = N / 2, gen = Cc - 2 * trim;
@@ -485,6 +497,16 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
         f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
         f.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
+        if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
+            if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
+            cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins, P.g.T,
+                                             D.mask_t, P.mask_t_per_chunk(), st),
+                       "mask transposition launch");
+            if (timing) timing->launches++;
+            f.mask = reinterpret_cast<const float*>(D.mask_t);
+            f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
+        }
+        if (timed && b0 == 0) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
         cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
         if (timing) timing->launches++;
         if (opt && opt->on_progress) {
@@ -503,10 +525,10 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
     c.mono_stats = P.mono_norm ? D.mono : nullptr;
-    if (timed) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
+    if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
     cuda_check(launch_combine(c, st), "combine kernel launch");
     if (timing) timing->launches++;
-    if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
+    if (timed) cuda_check(cudaEventRecord(timing->ev[3], st), "cudaEventRecord");
 }
 
 // ---- the halves around a real network ----------------------------------------------------------

@@ -42,6 +42,9 @@ struct HostPlan {
     float compensate = 1.0f;
     int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
     int mono_norm = 0, cac_norm = 0;   // HTDemucs: mono-mix and CaC normalisation
+    // f-major masks (HTDemucs, TFC-TDF): planes and bins per stem; the fused kernel reads
+    // them after launch_mask_transpose, 0 planes for the other layouts
+    int mask_planes = 0, mask_bins = 0;
     int64_t stem_stride = 0;
     int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
     std::vector<float> W;          // crossfade weight tables (ChunkDesc::w_off)
@@ -68,6 +71,8 @@ struct HostPlan {
     size_t mono_bytes() const { return mono_norm ? sizeof(double) * mono_scratch_doubles() : 0; }
     size_t cac_part_bytes() const { return cac_norm ? sizeof(double2) * (size_t)n_tiles * chunks.size() : 0; }
     size_t cac_stats_bytes() const { return cac_norm ? sizeof(double2) * chunks.size() : 0; }
+    int64_t mask_t_per_chunk() const { return mask_planes ? (int64_t)S * g.T * mask_bins : 0; }   // float4
+    size_t mask_t_bytes() const { return sizeof(float4) * (size_t)mask_t_per_chunk() * chunks.size(); }
 };
 
 // Where the device copies of a plan's tables and scratch live.
@@ -87,6 +92,7 @@ struct PlanDevice {
     double* mono = nullptr;        // scratch: mono statistics, mean and std at [0], [1]
     double2* cac_part = nullptr;   // scratch: CaC partial sums (HostPlan::cac_norm)
     double2* cac_stats = nullptr;  // scratch: per-chunk CaC (mean, std)
+    float4* mask_t = nullptr;      // scratch: t-major masks (HostPlan::mask_planes)
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
@@ -104,7 +110,8 @@ void fft_tables(int n_fft, std::vector<float>& win, std::vector<float2>& tw);
 
 // Optional timing of one run: events recorded on the run's stream around the kernels.
 struct RunTiming {
-    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // fused start, fused end, combine end
+    // run start, first fused launch, combine start, combine end
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     bool timed = false;
     int launches = 0;
 };
