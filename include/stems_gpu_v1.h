@@ -97,6 +97,11 @@ typedef struct {
                                 (src/htdemucs.cpp:539-549, 638-642) */
     int32_t cac_norm;        /* 1: per-segment mean / std of the CaC spectrogram around the
                                 network (src/htdemucs.cpp:434-436, 466-469) */
+    int32_t shifts;          /* SeparateOptions.shifts: random time shifts averaged, 0 = one pass
+                                (src/htdemucs.cpp:610-626); every shift's segments are chunks of
+                                the plan, shift by shift */
+    uint32_t seed;           /* SeparateOptions.seed: std::mt19937 seed of the shift offsets */
+    int32_t sample_rate;     /* the model's sample rate (max shift = sample_rate / 2); 0 = 44100 */
 } stg_htdemucs_config;
 
 /* Mel-Band / BS-RoFormer (src/roformer.cpp:360-412). */
@@ -115,6 +120,10 @@ typedef struct {
     const int32_t* band_sizes;   /* roformer.band_sizes [n_bands] */
     const int32_t* band_freqs;   /* roformer.band_freqs [sum band_sizes] */
     int32_t complement;      /* stems.complement present: append mix - first stem */
+    int32_t shifts;          /* SeparateOptions.shifts (src/roformer.cpp:456-478); every shift's
+                                chunks are chunks of the plan, shift by shift */
+    uint32_t seed;           /* SeparateOptions.seed: std::mt19937 seed of the shift offsets */
+    int32_t sample_rate;     /* the model's sample rate (max shift = sample_rate / 2); 0 = 44100 */
 } stg_roformer_config;
 
 /* TFC-TDF / MDX (src/tfc_tdf.cpp:498-553). */

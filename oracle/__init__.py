@@ -31,7 +31,8 @@ _I32P = C.POINTER(C.c_int)
 class HtParams(C.Structure):
     _fields_ = [("n_channels", C.c_int), ("n_sources", C.c_int), ("segment", C.c_int),
                 ("overlap", C.c_float), ("cac_norm", C.c_int), ("mono_norm", C.c_int),
-                ("sample_first", C.c_int), ("sample_count", C.c_int), ("threads", C.c_int)]
+                ("sample_first", C.c_int), ("sample_count", C.c_int), ("threads", C.c_int),
+                ("shifts", C.c_int), ("seed", C.c_uint), ("sample_rate", C.c_int)]
 
 
 class RfParams(C.Structure):
@@ -39,7 +40,8 @@ class RfParams(C.Structure):
                 ("hop", C.c_int), ("normalized", C.c_int), ("zero_dc", C.c_int),
                 ("chunk", C.c_int), ("step", C.c_int), ("n_bands", C.c_int),
                 ("band_sizes", _I32P), ("band_freqs", _I32P), ("complement", C.c_int),
-                ("sample_first", C.c_int), ("sample_count", C.c_int), ("threads", C.c_int)]
+                ("sample_first", C.c_int), ("sample_count", C.c_int), ("threads", C.c_int),
+                ("shifts", C.c_int), ("seed", C.c_uint), ("sample_rate", C.c_int)]
 
 
 class TfcParams(C.Structure):
@@ -69,6 +71,7 @@ def lib():
         L.or_htdemucs_spec.argtypes = [C.c_int, _F32, C.c_int, _F64, _I32P]
         L.or_htdemucs_ispec.argtypes = [C.c_int, _F64, C.c_int, C.c_int, _F32]
         L.or_use_reference.argtypes = [C.c_char_p]
+        L.or_shift_offsets.argtypes = [C.c_uint, C.c_int, C.c_int, _I32P]
         L.or_ht_n_segments.argtypes = [C.POINTER(HtParams), C.c_int]
         L.or_ht_n_frames.argtypes = [C.POINTER(HtParams)]
         L.or_ht_separate.argtypes = [C.POINTER(HtParams), _F32, C.c_int, _F32, _F32]
@@ -169,9 +172,17 @@ def htdemucs_ispec(spec, length, n_fft=4096, impl=None):
 
 # ---- glue --------------------------------------------------------------------------------
 def ht_params(n_channels=2, n_sources=4, segment=343980, overlap=-1.0, cac_norm=0, mono_norm=0,
-              sample_first=0, sample_count=0, threads=1):
+              sample_first=0, sample_count=0, threads=1, shifts=0, seed=0, sample_rate=44100):
     return HtParams(n_channels, n_sources, segment, overlap, cac_norm, mono_norm, sample_first,
-                    sample_count, threads)
+                    sample_count, threads, shifts, seed, sample_rate)
+
+
+def shift_offsets(seed, shifts, hi):
+    """The separators' random-shift offsets (std::mt19937 + uniform_int_distribution(0, hi))."""
+    out = np.zeros(max(shifts, 1), dtype=np.int32)
+    if lib().or_shift_offsets(seed, shifts, hi, out.ctypes.data_as(_I32P)) != 0:
+        raise ValueError("bad shift arguments")
+    return out[:shifts].copy()
 
 
 def ht_n_segments(p, length):
@@ -202,12 +213,13 @@ class _Bands:
 
 def rf_params(band_sizes, band_freqs, n_channels=2, n_stems=1, n_fft=2048, hop=441,
               normalized=0, zero_dc=0, chunk=352800, step=None, complement=0,
-              sample_first=0, sample_count=0, threads=1, num_overlap=2):
+              sample_first=0, sample_count=0, threads=1, num_overlap=2, shifts=0, seed=0,
+              sample_rate=44100):
     keep = _Bands(band_sizes, band_freqs)
     p = RfParams(n_channels, n_stems, n_fft, hop, normalized, zero_dc, chunk,
                  chunk // num_overlap if step is None else step, keep.sizes.size,
                  keep.sizes.ctypes.data_as(_I32P), keep.freqs.ctypes.data_as(_I32P),
-                 complement, sample_first, sample_count, threads)
+                 complement, sample_first, sample_count, threads, shifts, seed, sample_rate)
     p._keep = keep
     return p
 

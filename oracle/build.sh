@@ -1,6 +1,6 @@
 #!/usr/bin/env bash
 # Builds the CPU checker (test infrastructure only):
-#   oracle/liboracle.so            the C restatement (oracle.c), always
+#   oracle/liboracle.so            the C restatement (oracle.c, shifts.cpp), always
 #   oracle/_ref/libstems_ref.so    the reference's own stft.h / vr_dsp.h behind ref_shim.cpp,
 #   oracle/_ref/dsp_test           the reference's own known-answer tests, compiled from its
 #   oracle/_ref/vr_dsp_test        sources where they lie,
@@ -11,7 +11,11 @@ HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 REF_ROOT="${REF_ROOT:-$HERE/../../reference}"
 REF_SRC="${REF_SRC:-$REF_ROOT/src}"
 
-gcc -O2 -std=c11 -fPIC -shared -Wall -Wno-unused-result "$HERE/oracle.c" -o "$HERE/liboracle.so" -lm -lpthread -ldl
+OBJ="$(mktemp -d)"
+trap 'rm -rf "$OBJ"' EXIT
+gcc -O2 -std=c11 -fPIC -Wall -Wno-unused-result -c "$HERE/oracle.c" -o "$OBJ/oracle.o"
+g++ -O2 -std=c++17 -fPIC -Wall -c "$HERE/shifts.cpp" -o "$OBJ/shifts.o"
+g++ -shared "$OBJ/oracle.o" "$OBJ/shifts.o" -o "$HERE/liboracle.so" -lm -lpthread -ldl
 
 if [ -f "$REF_SRC/stft.h" ] && [ -f "$REF_SRC/vr_dsp.h" ]; then
     mkdir -p "$HERE/_ref"

@@ -385,10 +385,24 @@ static int ht_stride(const or_ht_params* p) {                            /* htde
     return (int)((1.0 - overlap) * p->segment);
 }
 
-int or_ht_n_segments(const or_ht_params* p, int len) {
+static int ht_view_segments(const or_ht_params* p, int view_len) {
     const int stride = ht_stride(p);
-    if (stride <= 0 || len <= 0) return 0;
-    return (len + stride - 1) / stride;                                   /* :576 */
+    if (stride <= 0 || view_len <= 0) return 0;
+    return (view_len + stride - 1) / stride;                              /* :576, 592 */
+}
+
+static int max_shift_of(int sample_rate);
+
+/* All segments the separation runs, every shift's view included (:575-577). */
+int or_ht_n_segments(const or_ht_params* p, int len) {
+    if (p->shifts <= 0) return ht_view_segments(p, len);
+    const int ms = max_shift_of(p->sample_rate);
+    int* off = (int*)malloc(sizeof(int) * p->shifts);
+    or_shift_offsets(p->seed, p->shifts, ms, off);                          /* :617-619 */
+    int n = 0;
+    for (int k = 0; k < p->shifts; k++) n += ht_view_segments(p, len + ms - off[k]);
+    free(off);
+    return n;
 }
 
 static double mean_of(const float* x, size_t n) {                        /* htdemucs.cpp:293-297 */
@@ -404,9 +418,11 @@ static double std_of(const float* x, size_t n, double mean) {            /* :298
 
 typedef struct {
     const or_ht_params* p;
-    const float* mix;      /* normalised mix [C][len] */
-    int len, stride, seg, T;
-    const float* mask;
+    const float* buf;      /* the buffer the view looks into [C][total] */
+    int total;
+    int view0, view_len;   /* the view: buffer samples [view0, view0 + view_len) */
+    int stride, seg, T;
+    const float* mask;     /* the view's first segment's mask */
     float* seg_out;        /* [G][S][C][seg] */
 } ht_job;
 
@@ -417,13 +433,13 @@ static int ht_segment(void* vctx, int g) {
     const or_ht_params* p = J->p;
     const int C = p->n_channels, S = p->n_sources, L = J->seg, T = J->T, F = HT_NFFT / 2;
     const int off = g * J->stride;
-    const int length = J->len - off < L ? J->len - off : L;
-    const int start = off - (L - length) / 2;
+    const int length = J->view_len - off < L ? J->view_len - off : L;
+    const int start = J->view0 + off - (L - length) / 2;
     float* seg_in = (float*)calloc((size_t)C * L, sizeof(float));
     for (int c = 0; c < C; c++)
         for (int i = 0; i < L; i++) {
             const int j = start + i;
-            if (j >= 0 && j < J->len) seg_in[(size_t)c * L + i] = J->mix[(size_t)c * J->len + j];
+            if (j >= 0 && j < J->total) seg_in[(size_t)c * L + i] = J->buf[(size_t)c * J->total + j];
         }
     const size_t FT = (size_t)F * T;
     float* mag = (float*)malloc(sizeof(float) * 2 * C * FT);
@@ -468,6 +484,38 @@ static int ht_segment(void* vctx, int g) {
     return rc;
 }
 
+/* split() over one view (htdemucs.cpp:588-606): the view's segments, weighted overlap-add,
+ * centre trim, divided by the summed weight. out [S][C][view_len]. sampled: honour the
+ * params' sample window (timing only). */
+static int ht_split(const or_ht_params* p, const float* buf, int total, int view0, int view_len,
+                    const float* mask, const float* weight, int sampled, float* out) {
+    const int S = p->n_sources, C = p->n_channels, seg = p->segment, stride = ht_stride(p);
+    const int G = ht_view_segments(p, view_len);
+    int lo = 0, hi = G;
+    if (sampled) sample_window(G, p->sample_first, p->sample_count, &lo, &hi);
+    ht_job J = {p, buf, total, view0, view_len, stride, seg, or_ht_n_frames(p), mask, NULL};
+    J.seg_out = (float*)malloc(sizeof(float) * (size_t)G * S * C * seg);
+    if (!J.seg_out) return ERR_MEM;
+    int rc = parallel_for(lo, hi, p->threads, ht_segment, &J);
+    float* sum_w = (float*)calloc((size_t)view_len, sizeof(float));
+    memset(out, 0, sizeof(float) * (size_t)S * C * view_len);
+    for (int g = lo; g < hi && !rc; g++) {
+        const int off = g * stride;
+        const int length = view_len - off < seg ? view_len - off : seg;
+        const int trim = (seg - length) / 2;                              /* center_trim */
+        for (int sc = 0; sc < S * C; sc++) {
+            const float* so = J.seg_out + ((size_t)g * S * C + sc) * seg;
+            for (int i = 0; i < length; i++)
+                out[(size_t)sc * view_len + off + i] += weight[i] * so[trim + i];
+        }
+        for (int i = 0; i < length; i++) sum_w[off + i] += weight[i];
+    }
+    for (int sc = 0; sc < S * C && !rc; sc++)
+        for (int i = 0; i < view_len; i++) out[(size_t)sc * view_len + i] /= sum_w[i];
+    free(sum_w); free(J.seg_out);
+    return rc;
+}
+
 int or_ht_separate(const or_ht_params* p, const float* mix_in, int len, const float* mask,
                    float* est) {
     if (!p || !mix_in || !mask || !est || len <= 0 || p->n_channels < 1 || p->n_sources < 1 ||
@@ -504,33 +552,36 @@ int or_ht_separate(const or_ht_params* p, const float* mix_in, int len, const fl
         for (int i = 1; i < seg; i++) if (weight[i] > mx) mx = weight[i];
         for (int i = 0; i < seg; i++) weight[i] /= mx;
     }
-    const int G = or_ht_n_segments(p, len);
-    int lo, hi;
-    sample_window(G, p->sample_first, p->sample_count, &lo, &hi);
-    ht_job J = {p, mix, len, stride, seg, or_ht_n_frames(p), mask, NULL};
-    J.seg_out = (float*)malloc(sizeof(float) * (size_t)G * S * C * seg);
-    if (!J.seg_out) { free(weight); free(mix); return ERR_MEM; }
-    int rc = parallel_for(lo, hi, p->threads, ht_segment, &J);
-    /* split(): weighted overlap-add, centre trim, divide by the summed weight (:589-606) */
-    float* sum_w = (float*)calloc((size_t)len, sizeof(float));
-    memset(est, 0, sizeof(float) * (size_t)S * C * len);
-    for (int g = lo; g < hi && !rc; g++) {
-        const int off = g * stride;
-        const int length = len - off < seg ? len - off : seg;
-        const int trim = (seg - length) / 2;
-        for (int sc = 0; sc < S * C; sc++) {
-            const float* so = J.seg_out + ((size_t)g * S * C + sc) * seg;
-            for (int i = 0; i < length; i++)
-                est[(size_t)sc * len + off + i] += weight[i] * so[trim + i];
+    int rc = 0;
+    if (p->shifts <= 0) {
+        rc = ht_split(p, mix, len, 0, len, mask, weight, 1, est);         /* :610-611 */
+    } else {
+        /* views of the mix padded by max_shift zeros per side; offset uniform in
+         * [0, max_shift], the views' estimates summed then divided (:612-626) */
+        const int ms = max_shift_of(p->sample_rate), total = len + 2 * ms;
+        float* pm = (float*)calloc((size_t)C * total, sizeof(float));
+        for (int c = 0; c < C; c++) memcpy(pm + (size_t)c * total + ms, mix + (size_t)c * len, sizeof(float) * len);
+        int* off = (int*)malloc(sizeof(int) * p->shifts);
+        or_shift_offsets(p->seed, p->shifts, ms, off);
+        memset(est, 0, sizeof(float) * (size_t)S * C * len);
+        const size_t mask_per_seg = (size_t)S * 2 * C * (HT_NFFT / 2) * or_ht_n_frames(p);
+        const float* m = mask;
+        for (int k = 0; k < p->shifts && !rc; k++) {
+            const int vl = len + ms - off[k];
+            float* o = (float*)malloc(sizeof(float) * (size_t)S * C * vl);
+            rc = ht_split(p, pm, total, off[k], vl, m, weight, 0, o);
+            for (int sc = 0; sc < S * C && !rc; sc++)
+                for (int i = 0; i < len; i++) est[(size_t)sc * len + i] += o[(size_t)sc * vl + ms - off[k] + i];
+            m += (size_t)ht_view_segments(p, vl) * mask_per_seg;
+            free(o);
         }
-        for (int i = 0; i < length; i++) sum_w[off + i] += weight[i];
+        for (size_t i = 0; i < (size_t)S * C * len && !rc; i++) est[i] /= p->shifts;
+        free(off); free(pm);
     }
-    for (int sc = 0; sc < S * C && !rc; sc++)
-        for (int i = 0; i < len; i++) est[(size_t)sc * len + i] /= sum_w[i];
     /* one model, weight 1: v / 1 * ref_std + ref_mean (:629-642) */
     if (p->mono_norm && !rc)
         for (size_t i = 0; i < (size_t)S * C * len; i++) est[i] = (float)(est[i] * ref_std + ref_mean);
-    free(sum_w); free(J.seg_out); free(weight); free(mix);
+    free(weight); free(mix);
     return rc;
 }
 
@@ -550,10 +601,23 @@ static int rf_check(const or_rf_params* p) {
     return 0;
 }
 
-int or_rf_n_chunks(const or_rf_params* p, int len) {                    /* roformer.cpp:353-357 */
+static int rf_demix_chunks(const or_rf_params* p, int len) {            /* roformer.cpp:353-357 */
     const int border = p->chunk - p->step;
     const int Lp = (len > 2 * border && border > 0) ? len + 2 * border : len;
     return (Lp + p->step - 1) / p->step;
+}
+
+static int max_shift_of(int sample_rate) { return (sample_rate > 0 ? sample_rate : 44100) / 2; }
+
+int or_rf_n_chunks(const or_rf_params* p, int len) {
+    if (p->shifts <= 0) return rf_demix_chunks(p, len);
+    const int ms = max_shift_of(p->sample_rate);                           /* :460 */
+    int* off = (int*)malloc(sizeof(int) * p->shifts);
+    or_shift_offsets(p->seed, p->shifts, ms - 1, off);                      /* :461-465 */
+    int n = 0;
+    for (int k = 0; k < p->shifts; k++) n += rf_demix_chunks(p, len + ms - off[k]);
+    free(off);
+    return n;
 }
 
 int or_rf_band_gather(const or_rf_params* p, const double* zd, int T, float* feat) {
@@ -661,8 +725,8 @@ static int rf_chunk(void* vctx, int g) {
     return rc;
 }
 
-int or_rf_separate(const or_rf_params* p, const float* mix, int len, const float* mask, float* out) {
-    if (rf_check(p) || !mix || !mask || !out || len <= 0) return ERR_ARG;
+/* demix() of one track (roformer.cpp:286-351): out [S][C][len]. */
+static int rf_demix(const or_rf_params* p, const float* mix, int len, const float* mask, float* out) {
     const int C = p->n_channels, S = p->n_stems, Cc = p->chunk, step = p->step, F = p->n_fft / 2 + 1;
     const int T = Cc / p->hop + 1;
     const int fade = Cc / 10, border = Cc - step;                         /* :288-291 */
@@ -721,9 +785,47 @@ int or_rf_separate(const or_rf_params* p, const float* mix, int len, const float
             const double v = result[(size_t)k * Lp + off + t] / counter[off + t];
             out[(size_t)k * len + t] = isfinite(v) ? (float)v : 0.0f;
         }
+    free(w); free(counter); free(result); free(J.y); free(bpf); free(window); free(fade_in); free(x);
+    return rc;
+}
+
+/* separate() (roformer.cpp:436-486): one demix, or the average over random shifts, then the
+ * complement. */
+int or_rf_separate(const or_rf_params* p, const float* mix, int len, const float* mask, float* out) {
+    if (rf_check(p) || !mix || !mask || !out || len <= 0) return ERR_ARG;
+    const int C = p->n_channels, S = p->n_stems;
+    int rc = 0;
+    if (p->shifts <= 0) {
+        rc = rf_demix(p, mix, len, mask, out);                            /* :456-457 */
+    } else {
+        const int ms = max_shift_of(p->sample_rate), T = p->chunk / p->hop + 1;
+        size_t din_total = 0;
+        for (int b = 0; b < p->n_bands; b++) din_total += (size_t)p->band_sizes[b] * C * 2;
+        const size_t mask_per_chunk = (size_t)S * din_total * T;
+        int* off = (int*)malloc(sizeof(int) * p->shifts);
+        or_shift_offsets(p->seed, p->shifts, ms - 1, off);                  /* :461-465 */
+        memset(out, 0, sizeof(float) * (size_t)S * C * len);
+        const float* m = mask;
+        for (int k = 0; k < p->shifts && !rc; k++) {
+            const int n = len + ms - off[k];                              /* :466 */
+            float* shifted = (float*)calloc((size_t)C * n, sizeof(float));
+            float* y = (float*)malloc(sizeof(float) * (size_t)S * C * n);
+            for (int c = 0; c < C; c++)                                   /* :467-472 */
+                for (int t = 0; t < n; t++) {
+                    const int src = t + off[k] - ms;
+                    if (src >= 0 && src < len) shifted[(size_t)c * n + t] = mix[(size_t)c * len + src];
+                }
+            rc = rf_demix(p, shifted, n, m, y);
+            for (int i = 0; i < S * C && !rc; i++)                        /* :474-477 */
+                for (int t = 0; t < len; t++)
+                    out[(size_t)i * len + t] += y[(size_t)i * n + ms - off[k] + t] / p->shifts;
+            m += (size_t)rf_demix_chunks(p, n) * mask_per_chunk;
+            free(y); free(shifted);
+        }
+        free(off);
+    }
     if (p->complement && !rc)                                             /* :481-485 */
         for (size_t i = 0; i < (size_t)C * len; i++) out[(size_t)S * C * len + i] = mix[i] - out[i];
-    free(w); free(counter); free(result); free(J.y); free(bpf); free(window); free(fade_in); free(x);
     return rc;
 }
 

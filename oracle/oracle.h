@@ -37,6 +37,12 @@ int or_torch_istft(int n_fft, const double* spec, int n_frames, int hop, int nor
 int or_htdemucs_spec(int n_fft, const float* x, int len, double* out, int* n_frames);  /* stft.h:79-103 */
 int or_htdemucs_ispec(int n_fft, const double* spec, int n_frames, int length, float* out); /* stft.h:106-140 */
 
+/* The random-shift offsets the separators draw: std::mt19937(seed), then `shifts` draws of
+ * std::uniform_int_distribution<int>(0, hi) (src/htdemucs.cpp:578, 617-619, hi = max_shift;
+ * src/roformer.cpp:461-465, hi = max_shift - 1). oracle/shifts.cpp, C++ for the same
+ * standard-library sequence. */
+int or_shift_offsets(unsigned seed, int shifts, int hi, int* out);
+
 /* Swap the primitives above (as used by the glue below) for the reference's own compiled
  * code. path = NULL restores the restatement. Returns 0 on success. */
 int or_use_reference(const char* path);
@@ -51,11 +57,14 @@ typedef struct {
     int cac_norm;        /* 1: mean/std normalise the CaC spectrogram around the stand-in */
     int mono_norm;       /* 1: demucs' mono-mix normalisation around the whole separation */
     int sample_first;    /* timing only: process segments [first, first+count) */
-    int sample_count;    /* <= 0: all segments */
+    int sample_count;    /* <= 0: all segments (the window applies without shifts only) */
     int threads;         /* worker threads for the per-segment work (<= 1: serial) */
+    int shifts;          /* random shifts averaged (:610-626); 0 = one pass */
+    unsigned seed;       /* std::mt19937 seed of the shift offsets */
+    int sample_rate;     /* max shift = sample_rate / 2; 0 = 44100 */
 } or_ht_params;
 /* mask: per segment [S][2C][F = n_fft/2][T] float (re plane 2c, im plane 2c+1), segments
- * back to back. out: [S][C][len]. */
+ * back to back (with shifts: every shift's segments, shift by shift). out: [S][C][len]. */
 int or_ht_n_segments(const or_ht_params* p, int len);
 int or_ht_n_frames(const or_ht_params* p);
 int or_ht_separate(const or_ht_params* p, const float* mix, int len, const float* mask, float* out);
@@ -70,6 +79,9 @@ typedef struct {
     const int* band_freqs;  /* [sum band_sizes] */
     int complement;         /* append mix - est as one more stem */
     int sample_first, sample_count, threads;
+    int shifts;             /* random shifts averaged (:456-478); 0 = one pass */
+    unsigned seed;          /* std::mt19937 seed of the shift offsets */
+    int sample_rate;        /* max shift = sample_rate / 2; 0 = 44100 */
 } or_rf_params;
 /* mask: per chunk [S][sum_b din_b * T] band-major, block b = [T][din_b], din_b = size_b*C*2,
  * entries (j*C + c)*2 + {re, im}. out: [S(+1)][C][len]. */

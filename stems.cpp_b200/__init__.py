@@ -43,7 +43,8 @@ class Cancelled(StemsError):
 class HTDemucsConfig(C.Structure):
     _fields_ = [("size", C.c_uint32), ("n_channels", C.c_int32), ("n_sources", C.c_int32),
                 ("segment", C.c_int32), ("overlap", C.c_float), ("mono_norm", C.c_int32),
-                ("cac_norm", C.c_int32)]
+                ("cac_norm", C.c_int32), ("shifts", C.c_int32), ("seed", C.c_uint32),
+                ("sample_rate", C.c_int32)]
 
 
 class RoFormerConfig(C.Structure):
@@ -51,7 +52,8 @@ class RoFormerConfig(C.Structure):
                 ("n_fft", C.c_int32), ("hop", C.c_int32), ("normalized", C.c_int32),
                 ("zero_dc", C.c_int32), ("chunk", C.c_int32), ("num_overlap", C.c_int32),
                 ("overlap", C.c_float), ("n_bands", C.c_int32), ("band_sizes", _I32P),
-                ("band_freqs", _I32P), ("complement", C.c_int32)]
+                ("band_freqs", _I32P), ("complement", C.c_int32), ("shifts", C.c_int32),
+                ("seed", C.c_uint32), ("sample_rate", C.c_int32)]
 
 
 class TFCConfig(C.Structure):
@@ -255,23 +257,26 @@ class Engine:
 
     # -- plans ---------------------------------------------------------------------------
     def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0,
-                      mono_norm=True, cac_norm=True):
+                      mono_norm=True, cac_norm=True, shifts=0, seed=0, sample_rate=44100):
         """HTDemucs.separate (src/htdemucs.cpp:534-642). Both normalisations are on by default,
-        as in the reference; mono_norm / cac_norm False leave the mix / spectrogram raw."""
+        as in the reference; mono_norm / cac_norm False leave the mix / spectrogram raw.
+        shifts > 0 averages that many random shifts (offsets from std::mt19937(seed)); the
+        plan's chunks are then every shift's segments, shift by shift."""
         cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap,
-                             int(bool(mono_norm)), int(bool(cac_norm)))
+                             int(bool(mono_norm)), int(bool(cac_norm)), shifts, seed, sample_rate)
         h = C.c_void_p()
         self._check(lib().stg_plan_htdemucs(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_htdemucs")
         return Plan(self, h)
 
     def plan_roformer(self, n_samples, band_sizes, band_freqs, n_channels=2, n_stems=1, n_fft=2048,
                       hop=441, normalized=False, zero_dc=False, chunk=352800, num_overlap=2,
-                      overlap=-1.0, complement=False):
+                      overlap=-1.0, complement=False, shifts=0, seed=0, sample_rate=44100):
         sizes = np.ascontiguousarray(band_sizes, dtype=np.int32)
         freqs = np.ascontiguousarray(band_freqs, dtype=np.int32)
         cfg = RoFormerConfig(C.sizeof(RoFormerConfig), n_channels, n_stems, n_fft, hop, int(normalized),
                              int(zero_dc), chunk, num_overlap, overlap, sizes.size,
-                             sizes.ctypes.data_as(_I32P), freqs.ctypes.data_as(_I32P), int(complement))
+                             sizes.ctypes.data_as(_I32P), freqs.ctypes.data_as(_I32P), int(complement),
+                             shifts, seed, sample_rate)
         h = C.c_void_p()
         self._check(lib().stg_plan_roformer(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_roformer")
         return Plan(self, h)

@@ -78,7 +78,7 @@ struct stg_plan {
     stg_engine* engine = nullptr;
     HostPlan H;
     PlanDevice D;
-    DevBuf d_chunks, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
+    DevBuf d_chunks, d_groups, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
     DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
     DevBuf d_mask_t;                                  // t-major masks (HTDemucs, TFC-TDF)
@@ -96,6 +96,7 @@ struct stg_plan {
     void upload_all() {
         const FftTables& t = engine->fft_tables_for(H.g.n_fft);
         upload(d_chunks, H.chunks, "chunk table");
+        upload(d_groups, H.groups, "chunk groups");
         upload(d_w, H.W, "weight table");
         upload(d_env, H.env, "envelope table");
         upload(d_btab, H.btab, "band table");
@@ -121,6 +122,7 @@ struct stg_plan {
             D.cac_stats = reinterpret_cast<double2*>(d_cac_stats.p);
         }
         D.chunks = d_chunks.as<ChunkDesc>();
+        D.groups = d_groups.as<ChunkGroup>();
         D.W = d_w.as<float>();
         D.env = d_env.as<float>();
         D.btab = d_btab.as<int2>();

@@ -67,8 +67,10 @@ __device__ __forceinline__ float chunk_sample(const Params& p, const ChunkDesc& 
         pl = 2 * (int64_t)(cd.valid - 1) - pl;
     }
     int64_t x = cd.src0 + pl;
-    if (p.reflect_global) x = reflect1(x, p.len);
-    else if (x < 0 || x >= p.len) return 0.0f;
+    if (cd.reflect) x = reflect1(x, cd.vlen);
+    else if (x < 0 || x >= cd.vlen) return 0.0f;
+    x += cd.vshift;
+    if (x < 0 || x >= p.len) return 0.0f;
     return ld_stream(chan + x);
 }
 

@@ -305,55 +305,69 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 }
 
 // ---- combine ------------------------------------------------------------------------------
-// One thread per output sample and SC = stems x channels rows: sum the chunks covering the
-// sample in ascending chunk order (src/roformer.cpp:337-340, src/tfc_tdf.cpp:420-422,
-// src/htdemucs.cpp:598-601), each value the chunk output Y plus, on a tile boundary, the
-// previous tile's trailing partial Tr; divide by the summed weight; epilogue.
+// One thread per output sample and SC = stems x channels rows. Per group (a pass of the shift
+// average; one group without shifts): sum the chunks covering the sample in ascending chunk
+// order (src/roformer.cpp:337-340, src/tfc_tdf.cpp:420-422, src/htdemucs.cpp:598-601), each
+// value the chunk output Y plus, on a tile boundary, the previous tile's trailing partial Tr,
+// and divide by the summed weight; then average the groups and finish (epilogue).
 template <int SC>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= p.len) return;
     const FrameGeom& G = p.g;
-    const int P = i + (int)p.out_shift;
-    const int out00 = (int)p.chunks[0].out0;
     const int step = (int)p.step_out;
-    int ghi = (P - out00) / step;
-    ghi = min(ghi, p.n_chunks - 1);
-    int glo = (P - out00 - (int)p.max_out_len) / step;
-    glo = max(glo, 0);
     const int span = p.K * G.hop, ov = G.n_fft - G.hop;
-    float acc[SC];
+    float res[SC];
 #pragma unroll
-    for (int k = 0; k < SC; k++) acc[k] = 0.0f;
-    float wsum = 0.0f;
-    for (int g = glo; g <= ghi + 1 && g < p.n_chunks; g++) {
-        const ChunkDesc& d = p.chunks[g];
-        const int u = P - (int)d.out0;
-        if (u < 0 || u >= d.out_len) continue;
-        const float w = __ldg(p.W + d.w_off + u);
-        wsum += w;
-        const int j = d.y_off + u;
-        const float* y = p.Y + (int64_t)g * p.y_chunk_stride + j;
-        // the tile boundary region j falls in, if any
-        const int q = j + G.out_offset - G.first_pos;
-        const int tau = q / span;
-        const int uu = q - tau * span;
-        const float* tr = nullptr;
-        if (tau >= 1 && tau < p.n_tiles && uu < ov)
-            tr = p.Tr + (int64_t)g * p.tr_chunk_stride + (int64_t)(tau - 1) * SC * ov + uu;
+    for (int k = 0; k < SC; k++) res[k] = 0.0f;
+    for (int gi = 0; gi < p.n_groups; gi++) {
+        const ChunkGroup grp = p.groups[gi];
+        const int P = i + grp.out_shift;
+        const int out00 = (int)p.chunks[grp.c0].out0;
+        const int n = grp.c1 - grp.c0;
+        int ghi = (P - out00) / step;
+        ghi = min(ghi, n - 1);
+        int glo = (P - out00 - (int)p.max_out_len) / step;
+        glo = max(glo, 0);
+        float acc[SC];
+#pragma unroll
+        for (int k = 0; k < SC; k++) acc[k] = 0.0f;
+        float wsum = 0.0f;
+        for (int gl = glo; gl <= ghi + 1 && gl < n; gl++) {
+            const int g = grp.c0 + gl;
+            const ChunkDesc& d = p.chunks[g];
+            const int u = P - (int)d.out0;
+            if (u < 0 || u >= d.out_len) continue;
+            const float w = __ldg(p.W + d.w_off + u);
+            wsum += w;
+            const int j = d.y_off + u;
+            const float* y = p.Y + (int64_t)g * p.y_chunk_stride + j;
+            // the tile boundary region j falls in, if any
+            const int q = j + G.out_offset - G.first_pos;
+            const int tau = q / span;
+            const int uu = q - tau * span;
+            const float* tr = nullptr;
+            if (tau >= 1 && tau < p.n_tiles && uu < ov)
+                tr = p.Tr + (int64_t)g * p.tr_chunk_stride + (int64_t)(tau - 1) * SC * ov + uu;
+#pragma unroll
+            for (int k = 0; k < SC; k++) {
+                float v = __ldg(y + (int64_t)k * G.Lout);
+                if (tr) v += __ldg(tr + k * ov);
+                acc[k] = fmaf(w, v, acc[k]);
+            }
+        }
+        const float inv = 1.0f / wsum;
 #pragma unroll
         for (int k = 0; k < SC; k++) {
-            float v = __ldg(y + (int64_t)k * G.Lout);
-            if (tr) v += __ldg(tr + k * ov);
-            acc[k] = fmaf(w, v, acc[k]);
+            float v = acc[k] * inv;
+            if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
+            res[k] += p.shift_mean == 2 ? v / (float)p.n_groups : v;
         }
     }
-    const float inv = 1.0f / wsum;
     float outv[SC];
 #pragma unroll
     for (int k = 0; k < SC; k++) {
-        float v = acc[k] * inv;
-        if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
+        float v = p.shift_mean == 1 ? res[k] / (float)p.n_groups : res[k];
         v *= p.compensate;
         if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
         outv[k] = v;

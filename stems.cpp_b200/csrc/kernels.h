@@ -14,19 +14,34 @@ enum Arch : int { ARCH_ROFORMER = 0, ARCH_HTDEMUCS = 1, ARCH_TFC = 2 };
 
 // One chunk (RoFormer/TFC-TDF) or segment (HTDemucs) of a track.
 //
-// Input side: chunk-local sample p in [0, Lc) reads the track at src0 + p when p < valid;
-// past valid it reads the mirror 2*(valid-1) - p (tail_reflect) or zero. Track coordinates
-// outside [0, len) are reflected (FusedParams::reflect_global) or read as zero.
-// Output side: the chunk contributes out_len samples starting at global output coordinate
-// out0; sample u of them is the chunk's own output at y_off + u, weighted by W[w_off + u].
+// Input side: chunk-local sample p in [0, Lc) reads the chunk's virtual track at src0 + p
+// when p < valid; past valid it reads the mirror 2*(valid-1) - p (tail_reflect) or zero.
+// Virtual-track coordinates outside [0, vlen) are reflected (reflect) or read as zero; the
+// virtual track's sample x is the mix's sample x + vshift, zero outside the mix. (The
+// virtual track is the mix itself, or one pass of the random-shift average: the mix behind
+// max_shift - offset zeros, src/roformer.cpp:464-472.)
+// Output side: the chunk contributes out_len samples starting at output coordinate out0 of
+// its group; sample u of them is the chunk's own output at y_off + u, weighted by
+// W[w_off + u].
 struct ChunkDesc {
     int64_t src0;
     int64_t out0;
+    int64_t vlen;
+    int64_t vshift;
     int32_t valid;
     int32_t tail_reflect;
+    int32_t reflect;
     int32_t out_len;
     int32_t y_off;
     int32_t w_off;
+    int32_t _pad[2];
+};
+
+// Chunks [c0, c1) overlap-added into one normalised estimate (a pass of the shift average);
+// output sample i of the track is the group's output coordinate i + out_shift.
+struct ChunkGroup {
+    int32_t c0, c1;
+    int32_t out_shift;
     int32_t _pad;
 };
 
@@ -49,7 +64,6 @@ struct FusedParams {
     const float* mix;          // planar [C][len]
     int64_t len;
     int n_channels;            // 1 or 2
-    int reflect_global;
     const ChunkDesc* chunks;
     int n_chunks;
     FrameGeom g;
@@ -93,6 +107,10 @@ struct CombineParams {
     int64_t tr_chunk_stride;
     const ChunkDesc* chunks;
     int n_chunks;
+    const ChunkGroup* groups;  // the passes of the shift average (one group without shifts)
+    int n_groups;
+    int shift_mean;            // 1: sum the groups, then divide (src/htdemucs.cpp:618-626);
+                               // 2: add each group divided by n_groups (src/roformer.cpp:474-477)
     int64_t step_out;          // regular chunk step in output coordinates
     int64_t max_out_len;       // longest out_len of any chunk
     FrameGeom g;
@@ -100,7 +118,6 @@ struct CombineParams {
     const float* W;            // weight tables
     int S, C;
     int64_t len;               // output samples per row
-    int64_t out_shift;         // global output coordinate of output sample 0
     int mode;                  // ARCH_*
     int nan_to_zero;
     float compensate;          // multiplies the stems (1 = off)
@@ -131,7 +148,6 @@ struct SplitParams {
     const float* mix;          // front: the track
     int64_t len;
     int n_channels;
-    int reflect_global;
     const ChunkDesc* chunks;
     int n_chunks;
     FrameGeom g;

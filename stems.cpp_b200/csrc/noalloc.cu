@@ -96,6 +96,7 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
 
         Carver c;
         const size_t o_chunks = c.take(H.chunks.size() * sizeof(ChunkDesc));
+        const size_t o_groups = c.take(H.groups.size() * sizeof(ChunkGroup));
         const size_t o_w = c.take(H.W.size() * sizeof(float));
         const size_t o_env = c.take(H.env.size() * sizeof(float));
         const size_t o_btab = c.take(H.btab.size() * sizeof(int2));
@@ -116,6 +117,7 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
 
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         put(arena, o_chunks, H.chunks, st);
+        put(arena, o_groups, H.groups, st);
         put(arena, o_w, H.W, st);
         put(arena, o_env, H.env, st);
         put(arena, o_btab, H.btab, st);
@@ -129,6 +131,7 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
         // call, so the arena needs no clearing between calls.
         PlanDevice D;
         D.chunks = reinterpret_cast<const ChunkDesc*>(arena + o_chunks);
+        D.groups = reinterpret_cast<const ChunkGroup*>(arena + o_groups);
         D.W = reinterpret_cast<const float*>(arena + o_w);
         D.env = reinterpret_cast<const float*>(arena + o_env);
         D.btab = reinterpret_cast<const int2*>(arena + o_btab);

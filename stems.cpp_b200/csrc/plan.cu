@@ -2,6 +2,8 @@
 // library's cos/sin and rounded once to float.
 #include "plan.h"
 
+#include <random>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -78,6 +80,17 @@ void finish_plan(HostPlan& P, int env_frames) {
         if (cost < best) { best = cost; P.K = K; }
     }
     P.n_tiles = (P.g.T + P.K - 1) / P.K;
+    // chunks of the plain track (no shift pass): the mix itself, reflected as the plan says
+    for (ChunkDesc& d : P.chunks)
+        if (d.vlen == 0) {
+            d.vlen = P.len;
+            d.vshift = 0;
+            d.reflect = P.reflect_global;
+        }
+    if (P.groups.empty()) {
+        if (P.out_shift > INT32_MAX) fail(STG_INVALID_ARGUMENT, "input is too long");
+        P.groups.push_back(ChunkGroup{0, (int32_t)P.chunks.size(), (int32_t)P.out_shift, 0});
+    }
     P.y_chunk_stride = (int64_t)P.S * P.C * P.g.Lout;
     P.tr_chunk_stride = (int64_t)P.n_tiles * P.S * P.C * (N - hop);
     P.max_out_len = 0;
@@ -105,7 +118,19 @@ void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
     if (ns != n) fail(STG_INTERNAL_ERROR, "radix plan does not multiply to n_fft");
 }
 
-// ---- HTDemucs: src/htdemucs.cpp:534-606 ---------------------------------------------------
+// The offsets of the random-shift passes: std::mt19937 seeded with `seed`, one draw of
+// std::uniform_int_distribution<int>(0, hi) per pass, as the separators draw them
+// (src/htdemucs.cpp:578, 617-619; src/roformer.cpp:461-465). The same standard library
+// produces the same sequence.
+static std::vector<int> shift_offsets(uint32_t seed, int shifts, int hi) {
+    std::mt19937 rng(seed);
+    std::uniform_int_distribution<int> dist(0, hi);
+    std::vector<int> v(shifts);
+    for (int& o : v) o = dist(rng);
+    return v;
+}
+
+// ---- HTDemucs: src/htdemucs.cpp:534-626 ---------------------------------------------------
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     const int N = 4096, hl = N / 4;                                   // htdemucs.cpp:35-36
     if (c.n_channels < 1 || c.n_channels > 2 || c.n_sources < 1 || c.n_sources > 8)
@@ -130,17 +155,39 @@ void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     P.mask_per_chunk = (int64_t)P.S * 2 * P.C * (N / 2) * T;
     P.mask_planes = 2 * P.C;
     P.mask_bins = N / 2;
-    for (int64_t off = 0; off < len; off += stride) {                 // :592
-        const int length = (int)std::min<int64_t>(seg, len - off);
-        ChunkDesc d{};
-        d.src0 = off - (seg - length) / 2;                            // :553-554
-        d.valid = seg;
-        d.tail_reflect = 0;
-        d.out0 = off;
-        d.out_len = length;
-        d.y_off = (seg - length) / 2;                                 // center_trim (:597)
-        d.w_off = 0;
-        P.chunks.push_back(d);
+    // split() over one view of the (zero-padded) mix: segments of the view, each read with
+    // real samples around it where the buffer has them (:552-561, 588-606). view0 is the mix
+    // coordinate of the view's sample 0; output sample i of the track is view sample
+    // i + out_shift.
+    auto split_view = [&](int64_t view0, int64_t view_len, int out_shift) {
+        const int c0 = (int)P.chunks.size();
+        for (int64_t off = 0; off < view_len; off += stride) {        // :592
+            const int length = (int)std::min<int64_t>(seg, view_len - off);
+            ChunkDesc d{};
+            d.src0 = view0 + off - (seg - length) / 2;                // :553-554
+            d.vlen = len;
+            d.vshift = 0;
+            d.reflect = 0;                                            // padded(): zeros outside
+            d.valid = seg;
+            d.tail_reflect = 0;
+            d.out0 = off;
+            d.out_len = length;
+            d.y_off = (seg - length) / 2;                             // center_trim (:597)
+            d.w_off = 0;
+            P.chunks.push_back(d);
+        }
+        P.groups.push_back(ChunkGroup{c0, (int32_t)P.chunks.size(), out_shift, 0});
+    };
+    const int shifts = std::max(0, c.shifts);                         // :575
+    if (shifts == 0) {
+        split_view(0, len, 0);                                        // :610-611
+    } else {
+        // views [offset, offset + len + max_shift - offset) of the mix padded by max_shift
+        // zeros per side; offset uniform in [0, max_shift] (:612-626)
+        const int max_shift = (c.sample_rate > 0 ? c.sample_rate : 44100) / 2;
+        for (int offset : shift_offsets(c.seed, shifts, max_shift))
+            split_view((int64_t)offset - max_shift, len + max_shift - offset, max_shift - offset);
+        P.shift_mean = 1;                                             // sum, then / shifts (:626)
     }
     std::vector<float>& weight = P.W;                                 // :566-573
     weight.assign(seg, 0.0f);
@@ -232,7 +279,6 @@ void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
     // chunking (:288-341)
     const int fade = Cc / 10, border = Cc - step;
     const bool pad = len > 2 * (int64_t)border && border > 0;
-    const int64_t Lp = pad ? len + 2 * (int64_t)border : len;
     std::vector<float> fade_in(std::max(fade, 0), 0.0f);
     if (fade > 1) {
         const float stp = 1.0f / (float)(fade - 1);
@@ -249,21 +295,42 @@ void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
         if (v == 1) std::fill(w, w + fade, 1.0f);                     // :335
         if (v == 2) std::fill(w + Cc - fade, w + Cc, 1.0f);           // :336
     }
-    for (int64_t i = 0; i < Lp; i += step) {                          // :317
-        const int length = (int)std::min<int64_t>(Cc, Lp - i);
-        ChunkDesc d{};
-        d.src0 = i - (pad ? border : 0);
-        d.valid = length;
-        d.tail_reflect = length < Cc && length > Cc / 2 + 1;          // :323-330
-        d.out0 = i;
-        d.out_len = length;
-        d.y_off = 0;
-        d.w_off = i == 0 ? Cc : (i + Cc >= Lp ? 2 * Cc : 0);
-        P.chunks.push_back(d);
+    // demix() of one track of n samples, the mix's sample x + vshift at its sample x (zero
+    // outside the mix); output sample i of the separation is the track's sample i + out_extra.
+    auto demix = [&](int64_t n, int64_t vshift, int out_extra) {
+        const bool pad_n = n > 2 * (int64_t)border && border > 0;      // :290-299
+        const int64_t Lp_n = pad_n ? n + 2 * (int64_t)border : n;
+        const int c0 = (int)P.chunks.size();
+        for (int64_t i = 0; i < Lp_n; i += step) {                    // :317
+            const int length = (int)std::min<int64_t>(Cc, Lp_n - i);
+            ChunkDesc d{};
+            d.src0 = i - (pad_n ? border : 0);
+            d.vlen = n;
+            d.vshift = vshift;
+            d.reflect = pad_n;
+            d.valid = length;
+            d.tail_reflect = length < Cc && length > Cc / 2 + 1;      // :323-330
+            d.out0 = i;
+            d.out_len = length;
+            d.y_off = 0;
+            d.w_off = i == 0 ? Cc : (i + Cc >= Lp_n ? 2 * Cc : 0);
+            P.chunks.push_back(d);
+        }
+        P.groups.push_back(ChunkGroup{c0, (int32_t)P.chunks.size(), (pad_n ? border : 0) + out_extra, 0});   // :344
+    };
+    if (c.shifts <= 0) {
+        demix(len, 0, 0);                                             // :456-457
+    } else {
+        // tracks of len + max_shift - offset samples, the mix behind max_shift - offset zeros;
+        // offset uniform in [0, max_shift - 1] (:458-478)
+        const int max_shift = (c.sample_rate > 0 ? c.sample_rate : 44100) / 2;
+        for (int offset : shift_offsets(c.seed, c.shifts, max_shift - 1))
+            demix(len + max_shift - offset, (int64_t)offset - max_shift, max_shift - offset);
+        P.shift_mean = 2;                                             // y / shifts, summed (:476)
     }
     P.reflect_global = pad;
     P.step_out = step;
-    P.out_shift = pad ? border : 0;                                   // :344
+    P.out_shift = pad ? border : 0;
     P.nan_to_zero = 1;                                                // :348
     P.complement = c.complement ? 1 : 0;                              // :481-485
     P.front_layout = FRONT_BANDS;                                     // feat (:226-241)
@@ -476,7 +543,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         if (timing) timing->launches += k;
     }
     FusedParams f{};
-    f.mix = d_mix; f.len = P.len; f.n_channels = P.C; f.reflect_global = P.reflect_global;
+    f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
     f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
     f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
     f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
@@ -518,10 +585,11 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
     c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
     c.chunks = D.chunks; c.n_chunks = G;
+    c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
     c.step_out = P.step_out; c.max_out_len = P.max_out_len;
     c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
     c.W = D.W;
-    c.S = P.S; c.C = P.C; c.len = P.len; c.out_shift = P.out_shift;
+    c.S = P.S; c.C = P.C; c.len = P.len;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
     c.mono_stats = P.mono_norm ? D.mono : nullptr;
@@ -538,7 +606,6 @@ SplitParams split_params(const HostPlan& P, const PlanDevice& D, const float* d_
     s.mix = d_mix;
     s.len = P.len;
     s.n_channels = P.C;
-    s.reflect_global = P.reflect_global;
     s.chunks = D.chunks + first;
     s.n_chunks = n;
     s.g = P.g;
@@ -592,7 +659,7 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
         // RoFormer: the network's masks are exactly the fused kernel's mask input
         if (reinterpret_cast<uintptr_t>(d_net_out) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
         FusedParams f{};
-        f.mix = d_mix; f.len = P.len; f.n_channels = P.C; f.reflect_global = P.reflect_global;
+        f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
         f.chunks = D.chunks + first; f.n_chunks = n;
         f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
         f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
@@ -622,11 +689,11 @@ void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, f
     c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
     c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
     c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
+    c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
     c.step_out = P.step_out; c.max_out_len = P.max_out_len;
     c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
     c.W = D.W;
     c.S = P.S; c.C = P.C; c.len = P.arch_out_len();
-    c.out_shift = P.out_shift;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
     c.mono_stats = P.mono_norm ? D.mono : nullptr;

@@ -33,11 +33,13 @@ struct HostPlan {
     int C = 2, S = 1, S_out = 1;
     int64_t mask_per_chunk = 0;
     std::vector<ChunkDesc> chunks;
+    std::vector<ChunkGroup> groups;   // the passes of the shift average (finish_plan: one)
+    int shift_mean = 0;               // CombineParams::shift_mean
     FrameGeom g{};
     int K = 16, n_tiles = 0;
     float fwd_scale = 1.0f, inv_scale = 1.0f;
-    int reflect_global = 0;
-    int64_t step_out = 1, out_shift = 0, max_out_len = 0;
+    int reflect_global = 0;        // the default of ChunkDesc::reflect
+    int64_t step_out = 1, out_shift = 0, max_out_len = 0;   // out_shift: the default group's
     int nan_to_zero = 0, complement = 0;
     float compensate = 1.0f;
     int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
@@ -78,6 +80,7 @@ struct HostPlan {
 // Where the device copies of a plan's tables and scratch live.
 struct PlanDevice {
     const ChunkDesc* chunks = nullptr;
+    const ChunkGroup* groups = nullptr;
     const float* W = nullptr;
     const float* env = nullptr;
     const int2* btab = nullptr;

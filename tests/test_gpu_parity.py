@@ -89,6 +89,33 @@ def test_htdemucs_matches_oracle(case, pkg, engine, oracle_mod):
     check(got, want, name)
 
 
+# ---- random shifts (src/htdemucs.cpp:610-626, src/roformer.cpp:456-478) -----------------------
+@pytest.mark.parametrize("shifts,seed", [(1, 0), (3, 17)])
+def test_htdemucs_shifts_match_oracle(engine, oracle_mod, shifts, seed):
+    seg, length, S = 1024 * 24, 60000, 4
+    plan = engine.plan_htdemucs(length, n_sources=S, segment=seg, shifts=shifts, seed=seed)
+    p = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=1, cac_norm=1, shifts=shifts, seed=seed,
+                             threads=8)
+    assert plan.n_chunks == oracle_mod.ht_n_segments(p, length)
+    mix = synth_audio(31, length)
+    mask = synth_mask(32, plan.mask_floats, 1.0)
+    check(run_gpu(plan, mix, mask), oracle_mod.ht_separate(p, mix, mask), f"ht shifts={shifts}")
+
+
+@pytest.mark.parametrize("length", [441 * 100 + 33, 15000])   # 15000: only the shifted tracks are padded
+def test_roformer_shifts_match_oracle(pkg, engine, oracle_mod, length):
+    sizes, freqs = pkg.bands.bs_bands()
+    chunk = 441 * 40
+    plan = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=2, zero_dc=True, complement=True,
+                                shifts=2, seed=9)
+    p = oracle_mod.rf_params(sizes, freqs, chunk=chunk, num_overlap=2, zero_dc=1, complement=1, shifts=2, seed=9,
+                             threads=8)
+    assert plan.n_chunks == oracle_mod.rf_n_chunks(p, length)
+    mix = synth_audio(33, length)
+    mask = synth_mask(34, plan.mask_floats, 0.5)
+    check(run_gpu(plan, mix, mask), oracle_mod.rf_separate(p, mix, mask), f"rf shifts, length {length}")
+
+
 # ---- TFC-TDF -------------------------------------------------------------------------------
 TFC_CASES = [
     # name, dim_t, chunking, overlap, length, compensate, complement

@@ -96,6 +96,67 @@ def test_identity_mask_gives_back_the_mix(oracle_mod, pkg):
         assert np.abs(y[0] - x).max() < 1e-6
 
 
+# ---- random shifts (src/htdemucs.cpp:610-626, src/roformer.cpp:456-478) ----------------------
+def _mt19937_raw(seed, n):
+    """Raw 32-bit outputs of std::mt19937(seed): numpy's legacy RandomState seeds MT19937 by
+    the same init_genrand, and a full-range 32-bit draw is one raw output."""
+    return np.random.RandomState(seed).randint(0, 2**32, size=n, dtype=np.uint64)
+
+
+def _bounded(raw, hi, count):
+    """uniform_int_distribution<int>(0, hi) over 32-bit raw draws: Lemire's multiply-shift
+    with rejection of the biased low products."""
+    out, it, span = [], iter(raw), hi + 1
+    while len(out) < count:
+        prod = int(next(it)) * span
+        if (prod & 0xFFFFFFFF) < span:
+            threshold = (2**32 - span) % span
+            while (prod & 0xFFFFFFFF) < threshold:
+                prod = int(next(it)) * span
+        out.append(prod >> 32)
+    return out
+
+
+@pytest.mark.parametrize("seed,shifts,hi", [(0, 5, 22050), (42, 3, 22049), (7, 10, 3999)])
+def test_shift_offsets_are_the_standard_library_sequence(oracle_mod, seed, shifts, hi):
+    got = oracle_mod.shift_offsets(seed, shifts, hi)
+    assert list(got) == _bounded(_mt19937_raw(seed, 4 * shifts + 8), hi, shifts)
+    assert all(0 <= o <= hi for o in got)
+
+
+def _sines(length, channels=2, seed=5):
+    rng = np.random.default_rng(seed)
+    t = np.arange(length) / 44100.0
+    return np.stack([(rng.uniform(0.05, 0.2, 6)[:, None] *
+                      np.sin(2 * np.pi * rng.uniform(60, 4000, 6)[:, None] * t)).sum(0)
+                     for _ in range(channels)]).astype(np.float32)
+
+
+def test_htdemucs_shift_schedule(oracle_mod):
+    """Every shift runs split() over a view of len + max_shift - offset samples, offset in
+    [0, max_shift] (src/htdemucs.cpp:612-621): the segment count is the views' sum."""
+    length, seg = 30000, 1024 * 12
+    p = oracle_mod.ht_params(n_sources=2, segment=seg, shifts=4, seed=3, sample_rate=8000)
+    stride = int(0.75 * seg)
+    offs = oracle_mod.shift_offsets(3, 4, 4000)
+    want = sum(-(-(length + 4000 - int(o)) // stride) for o in offs)
+    assert oracle_mod.ht_n_segments(p, length) == want
+
+
+def test_roformer_shift_average_of_identity_is_the_mix(oracle_mod, pkg):
+    sizes, freqs = pkg.bands.mel_bands()
+    chunk = 441 * 20
+    p = oracle_mod.rf_params(sizes, freqs, chunk=chunk, num_overlap=4, shifts=3, seed=11, sample_rate=8000,
+                             complement=1)
+    length = 441 * 50 + 7
+    T = chunk // 441 + 1
+    m = np.zeros((oracle_mod.rf_n_chunks(p, length), int(sizes.sum()) * 4 * T), np.float32)
+    m[:, 0::2] = 1.0
+    x = synth_audio(4, length)
+    y = oracle_mod.rf_separate(p, x, m)
+    assert np.abs(y[0] - x).max() < 1e-5 and np.abs(y[1]).max() < 1e-5
+
+
 # ---- 2. golden vectors from the reference ----------------------------------------------------
 def test_primitives_match_golden(oracle_mod, golden):
     g = golden
