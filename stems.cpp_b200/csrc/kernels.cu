@@ -522,12 +522,19 @@ __global__ void __launch_bounds__(256) mask_transpose(const float* __restrict__ 
     for (int cs = blockIdx.z; cs < n_cs; cs += gridDim.z) {
         const int ci = cs / S, s = cs - ci * S;
         const float* src = in + ci * in_chunk_stride + (int64_t)s * P * F * T;
+        // all 16 loads of a thread in flight before the first shared-memory store
+        float v[4][kTile / 8];
 #pragma unroll
         for (int p = 0; p < 4; p++)
-            for (int r = ly; r < kTile; r += 8) {
-                const int f = f0 + r, t = t0 + lx;
-                tile[p][r][lx] = (p < P && f < F && t < T) ? ld_stream(src + ((int64_t)p * F + f) * T + t) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < kTile / 8; k++) {
+                const int f = f0 + ly + 8 * k, t = t0 + lx;
+                v[p][k] = (p < P && f < F && t < T) ? ld_stream(src + ((int64_t)p * F + f) * T + t) : 0.0f;
             }
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+#pragma unroll
+            for (int k = 0; k < kTile / 8; k++) tile[p][ly + 8 * k][lx] = v[p][k];
         __syncthreads();
         float4* dst = out + ci * out_chunk_stride + (int64_t)s * T * F;
         for (int r = ly; r < kTile; r += 8) {
