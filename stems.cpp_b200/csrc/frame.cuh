@@ -27,12 +27,15 @@ template <> struct FftCfg<4096> {
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;
     using Plan = RadixList<16, 16, 16>;
 };
+// 7680: radix 15 last, because a first radix-15 pass stores at stride 15, which the padding
+// of pad_idx cancels into 16-way bank conflicts; 256 threads let a thread keep its ~200 live
+// values in registers (at 512 threads the 128-register cap spilled).
 template <> struct FftCfg<7680> {
-    static constexpr int T = 512, MINB = 1, HOPMAX = 1024;
+    static constexpr int T = 256, MINB = 1, HOPMAX = 1024;
     static constexpr int PF_GROUPS = 1;
     static constexpr bool AHEAD = false;
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;
-    using Plan = RadixList<15, 8, 8, 8>;
+    using Plan = RadixList<8, 8, 8, 15>;
 };
 
 __device__ __forceinline__ int64_t reflect1(int64_t j, int64_t n) {
