@@ -257,6 +257,31 @@ STG_API stg_status stg_separate_network(stg_plan* plan, const float* d_mix, floa
                                         int32_t chunks_per_batch, stg_network_fn network, void* user,
                                         const stg_run_options* options, void* stream);
 
+/* ---- the request's audio in and the stems out (src/libstems.cpp:160-199) ------------------ */
+
+/* Samples per channel after resampling n samples from src_rate to dst_rate:
+ * llround(n * dst_rate / src_rate), or n at the same rate (src/audio.h:20-21). */
+STG_API int64_t stg_resampled_length(int64_t n_samples, int32_t src_rate, int32_t dst_rate);
+
+/* The request's audio in the model's format, as libstems.cpp:160-169 makes it: d_in holds
+ * n_samples frames of n_channels channels, interleaved (interleaved = 1) or planar; d_out
+ * receives planar [model_channels][stg_resampled_length(n_samples, sample_rate, model_rate)]:
+ * channels converted by to_channels (mono duplicated, extra channels dropped,
+ * src/audio.h:59-68), then resampled to model_rate by the Kaiser-windowed sinc of
+ * resample_planar (src/audio.h:17-56) when the rates differ. Sample for sample the floats
+ * the reference computes. Asynchronous on `stream`. */
+STG_API stg_status stg_prepare_input(stg_engine* engine, const float* d_in, int32_t interleaved,
+                                     int64_t n_samples, int32_t n_channels, int32_t sample_rate,
+                                     int32_t model_channels, int32_t model_rate, float* d_out,
+                                     void* stream);
+
+/* The stems back at the request's rate (libstems.cpp:189-199): d_stems planar [rows][len] at
+ * model_rate -> d_out planar [rows][n_samples] at sample_rate, resampled when the rates
+ * differ and then pinned to n_samples (cut, or zero-filled past the resampled end). */
+STG_API stg_status stg_restore_output(stg_engine* engine, const float* d_stems, int32_t rows,
+                                      int64_t len, int32_t model_rate, int32_t sample_rate,
+                                      int64_t n_samples, float* d_out, void* stream);
+
 /* ---- the DSP primitives of src/stft.h on the device -------------------------------------- */
 
 /* torch.stft (src/stft.h:146-164) of each channel: periodic Hann, centre reflect pad,

@@ -72,6 +72,9 @@ def lib():
         L.or_htdemucs_ispec.argtypes = [C.c_int, _F64, C.c_int, C.c_int, _F32]
         L.or_use_reference.argtypes = [C.c_char_p]
         L.or_shift_offsets.argtypes = [C.c_uint, C.c_int, C.c_int, _I32P]
+        L.or_resampled_length.restype = C.c_longlong
+        L.or_resampled_length.argtypes = [C.c_longlong, C.c_int, C.c_int]
+        L.or_resample_planar.argtypes = [_F32, C.c_int, C.c_int, C.c_int, C.c_int, _F32, _I32P]
         L.or_ht_n_segments.argtypes = [C.POINTER(HtParams), C.c_int]
         L.or_ht_n_frames.argtypes = [C.POINTER(HtParams)]
         L.or_ht_separate.argtypes = [C.POINTER(HtParams), _F32, C.c_int, _F32, _F32]
@@ -110,6 +113,7 @@ def ref_lib():
         R.ref_torch_istft.argtypes = [C.c_int, _F64, C.c_int, C.c_int, C.c_int, _F32]
         R.ref_htdemucs_spec.argtypes = [C.c_int, _F32, C.c_int, _F64, _I32P]
         R.ref_htdemucs_ispec.argtypes = [C.c_int, _F64, C.c_int, C.c_int, _F32]
+        R.ref_resample_planar.argtypes = [_F32, C.c_int, C.c_int, C.c_int, C.c_int, _F32, _I32P]
         _ref = R
     return _ref
 
@@ -167,6 +171,49 @@ def htdemucs_ispec(spec, length, n_fft=4096, impl=None):
     out = np.zeros(length, np.float32)
     f = impl.ref_htdemucs_ispec if impl is not None else lib().or_htdemucs_ispec
     _check(f(n_fft, spec.reshape(-1).view(np.float64), spec.shape[1], length, out), "htdemucs_ispec")
+    return out
+
+
+# ---- the request's audio in and the stems out ----------------------------------------------
+def resampled_length(n, src_rate, dst_rate):
+    return int(lib().or_resampled_length(n, src_rate, dst_rate))
+
+
+def resample_planar(x, src_rate, dst_rate, impl=None):
+    """audio.h resample_planar of planar x [ch][n] -> [ch][out_n]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ch, n = x.shape
+    m = resampled_length(n, src_rate, dst_rate)
+    out = np.zeros(ch * m, np.float32)
+    got = C.c_int(0)
+    f = impl.ref_resample_planar if impl is not None else lib().or_resample_planar
+    _check(f(x.reshape(-1), n, ch, src_rate, dst_rate, out, C.byref(got)), "resample_planar")
+    assert got.value == m
+    return out.reshape(ch, m)
+
+
+def to_channels(x, want):
+    """audio.h to_channels: mono duplicated, extra channels dropped (planar [ch][n])."""
+    ch = x.shape[0]
+    return np.stack([x[0 if ch == 1 else min(c, ch - 1)] for c in range(want)])
+
+
+def prepare_input(samples, interleaved, n_channels, sample_rate, model_channels, model_rate, impl=None):
+    """libstems.cpp:160-169: interleaved/planar -> planar, to_channels, resample."""
+    s = np.asarray(samples, np.float32).reshape(-1)
+    n = s.size // n_channels
+    planar = s.reshape(n, n_channels).T.copy() if interleaved else s.reshape(n_channels, n)
+    return resample_planar(to_channels(planar, model_channels), sample_rate, model_rate, impl=impl)
+
+
+def restore_output(stems, model_rate, sample_rate, n_samples, impl=None):
+    """libstems.cpp:189-199: stems [rows][len] back to the request's rate, pinned to n_samples."""
+    if model_rate == sample_rate:
+        return np.asarray(stems, np.float32)
+    y = resample_planar(stems, model_rate, sample_rate, impl=impl)
+    out = np.zeros((y.shape[0], n_samples), np.float32)
+    k = min(n_samples, y.shape[1])
+    out[:, :k] = y[:, :k]
     return out
 
 

@@ -1026,3 +1026,63 @@ int or_tfc_separate(const or_tfc_params* p, const float* mix, int len, const flo
     free(window); free(w); free(divider); free(result); free(J.y); free(x);
     return rc;
 }
+
+/* ===================================================================================== */
+/* Input conversion: resample_planar (audio.h:17-56)                                      */
+/* ===================================================================================== */
+long long or_resampled_length(long long n, int src_rate, int dst_rate) {
+    if (src_rate == dst_rate) return n;
+    return llround((double)n * ((double)dst_rate / src_rate));           /* :20-21 */
+}
+
+static double kaiser_i0(double x) {                                       /* :27-31 */
+    double s = 1, t = 1;
+    for (int k = 1; k < 30; k++) { t *= (x / (2 * k)) * (x / (2 * k)); s += t; }
+    return s;
+}
+
+int or_resample_planar(const float* in, int n, int ch, int src_rate, int dst_rate, float* out, int* out_n) {
+    if (!in || !out || !out_n || n <= 0 || ch < 1 || src_rate <= 0 || dst_rate <= 0) return ERR_ARG;
+    if (src_rate == dst_rate) {
+        memcpy(out, in, sizeof(float) * (size_t)n * ch);
+        *out_n = n;
+        return 0;
+    }
+    const double ratio = (double)dst_rate / src_rate;
+    const int m = (int)llround(n * ratio);
+    const double cutoff = 0.95 * (ratio < 1.0 ? ratio : 1.0);             /* :22 */
+    const int zc = 32;
+    const double half = zc / cutoff;
+    const double beta = 8.6;
+    const double i0b = kaiser_i0(beta);
+    const int table_n = 1 << 15;                                          /* :33-42 */
+    double* table = (double*)malloc(sizeof(double) * (table_n + 2));
+    double* acc = (double*)malloc(sizeof(double) * ch);
+    if (!table || !acc) { free(table); free(acc); return ERR_MEM; }
+    for (int t = 0; t <= table_n + 1; t++) {
+        const double q = (double)t / table_n;
+        const double x = (q < 1.0 ? q : 1.0) * half;
+        const double r = x / half;
+        const double arg = M_PI * x * cutoff;
+        const double sinc = arg < 1e-12 ? 1.0 : sin(arg) / arg;
+        table[t] = r >= 1 ? 0.0 : sinc * kaiser_i0(beta * sqrt(1 - r * r)) / i0b * cutoff;
+    }
+    for (int i = 0; i < m; i++) {                                         /* :45-54 */
+        const double c = i / ratio;
+        const int lo0 = (int)ceil(c - half), hi0 = (int)floor(c + half);
+        const int lo = lo0 > 0 ? lo0 : 0, hi = hi0 < n - 1 ? hi0 : n - 1;
+        for (int k = 0; k < ch; k++) acc[k] = 0.0;
+        for (int j = lo; j <= hi; j++) {
+            const double pos = fabs(j - c) / half * table_n;
+            const int t = (int)pos;
+            if (t >= table_n) continue;
+            const double fr = pos - t;
+            const double w = table[t] + (table[t + 1] - table[t]) * fr;
+            for (int k = 0; k < ch; k++) acc[k] += w * in[(size_t)k * n + j];
+        }
+        for (int k = 0; k < ch; k++) out[(size_t)k * m + i] = (float)acc[k];
+    }
+    *out_n = m;
+    free(acc); free(table);
+    return 0;
+}

@@ -43,6 +43,13 @@ int or_htdemucs_ispec(int n_fft, const double* spec, int n_frames, int length, f
  * standard-library sequence. */
 int or_shift_offsets(unsigned seed, int shifts, int hi, int* out);
 
+/* ---- the request's audio in and the stems out (src/audio.h:17-56) ---------------------- */
+/* resample_planar: Kaiser-windowed sinc (32 zero crossings, cutoff 0.95 of the lower Nyquist,
+ * beta 8.6, 2^15-entry table interpolated linearly), planar in [ch][n] -> out [ch][out_n],
+ * out_n = llround(n * dst / src). out must hold ch * or_resampled_length(...) floats. */
+long long or_resampled_length(long long n, int src_rate, int dst_rate);
+int or_resample_planar(const float* in, int n, int ch, int src_rate, int dst_rate, float* out, int* out_n);
+
 /* Swap the primitives above (as used by the glue below) for the reference's own compiled
  * code. path = NULL restores the restatement. Returns 0 on success. */
 int or_use_reference(const char* path);

@@ -5,7 +5,9 @@
 // from the reference is copied here: this file only forwards to st::FFT, st::VRFFT,
 // st::torch_stft/istft and st::htdemucs_spec/ispec (src/stft.h, src/vr_dsp.h) so the C
 // restatement in oracle.c can be pinned against them, golden vectors can be generated from
-// them, and the CPU baseline can time them.
+// them, and the CPU baseline can time them. ref_resample_planar forwards to
+// st::resample_planar (src/audio.h).
+#include "audio.h"
 #include "stft.h"
 #include "vr_dsp.h"
 
@@ -99,6 +101,17 @@ int ref_htdemucs_ispec(int n_fft, const double* spec, int n_frames, int length, 
         const std::vector<st::cplx> s = get(spec, (size_t)(n_fft / 2) * n_frames);
         const std::vector<float> y = st::htdemucs_ispec(fft_for(n_fft), s, n_frames, length);
         std::memcpy(out, y.data(), y.size() * sizeof(float));
+        return 0;
+    } catch (...) { return -3; }
+}
+
+int ref_resample_planar(const float* in, int n, int ch, int src_rate, int dst_rate, float* out, int* out_n) {
+    try {
+        const std::vector<float> x(in, in + (size_t)n * ch);
+        int m = 0;
+        const std::vector<float> y = st::resample_planar(x, n, ch, src_rate, dst_rate, m);
+        std::memcpy(out, y.data(), y.size() * sizeof(float));
+        *out_n = m;
         return 0;
     } catch (...) { return -3; }
 }

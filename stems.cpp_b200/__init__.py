@@ -114,6 +114,11 @@ _SIGNATURES = {
     "stg_finish": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_network": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, NETWORK_FN, C.c_void_p,
                                          C.POINTER(RunOptions), C.c_void_p]),
+    "stg_resampled_length": (C.c_int64, [C.c_int64, C.c_int32, C.c_int32]),
+    "stg_prepare_input": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                                      C.c_int32, C.c_void_p, C.c_void_p]),
+    "stg_restore_output": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int64,
+                                       C.c_void_p, C.c_void_p]),
     "stg_torch_stft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int64,
                                    C.c_void_p, C.c_void_p]),
     "stg_torch_istft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32,
@@ -153,6 +158,11 @@ def version() -> str:
 
 def device_count() -> int:
     return lib().stg_device_count()
+
+
+def resampled_length(n_samples: int, src_rate: int, dst_rate: int) -> int:
+    """Samples per channel after resampling (src/audio.h:20-21)."""
+    return int(lib().stg_resampled_length(n_samples, src_rate, dst_rate))
 
 
 def _ptr(x):
@@ -235,6 +245,32 @@ class Engine:
         self._check(lib().stg_torch_istft(self._h, n_fft, hop, int(normalized), spec.data_ptr(), C_, T, _ptr(y),
                                           _stream_of(stream, spec)), "torch_istft")
         return y
+
+    # -- the request's audio in and the stems out (src/libstems.cpp:160-199) -----------------
+    def prepare_input(self, samples, n_channels, sample_rate, interleaved=True, model_channels=2,
+                      model_rate=44100, out=None, stream=None):
+        """Request audio (a flat CUDA tensor of n frames x n_channels, interleaved or planar)
+        -> planar float32 [model_channels][resampled length] at model_rate."""
+        import torch
+        n = samples.numel() // n_channels
+        m = resampled_length(n, sample_rate, model_rate)
+        if out is None:
+            out = torch.empty((model_channels, m), dtype=torch.float32, device=samples.device)
+        self._check(lib().stg_prepare_input(self._h, _ptr(samples), int(bool(interleaved)), n, n_channels,
+                                            sample_rate, model_channels, model_rate, _ptr(out),
+                                            _stream_of(stream, samples)), "prepare_input")
+        return out
+
+    def restore_output(self, stems, model_rate, sample_rate, n_samples, out=None, stream=None):
+        """Stems [rows][len] at model_rate -> [rows][n_samples] at sample_rate."""
+        import torch
+        stems = stems.reshape(-1, stems.shape[-1])
+        rows, length = stems.shape
+        if out is None:
+            out = torch.empty((rows, n_samples), dtype=torch.float32, device=stems.device)
+        self._check(lib().stg_restore_output(self._h, _ptr(stems), rows, length, model_rate, sample_rate, n_samples,
+                                             _ptr(out), _stream_of(stream, stems)), "restore_output")
+        return out
 
     def htdemucs_spec(self, x, stream=None):
         """HTDemucs _spec of x [C][n]: complex64 [C][2048][ceil(n/1024)]."""

@@ -58,6 +58,24 @@ struct stg_engine {
     std::map<int, std::unique_ptr<FftTables>> tables;
     // single-chunk plans of the DSP primitives, by (kind, n_fft, hop, normalized, C, length)
     std::map<std::tuple<int, int, int, int, int, int64_t>, std::unique_ptr<stg_plan>> primitives;
+    // Kaiser kernel tables of the resampler, by (source rate, destination rate)
+    struct Kaiser {
+        DevBuf table;
+        double half = 0, ratio = 1;
+    };
+    std::map<std::pair<int, int>, std::unique_ptr<Kaiser>> kaiser;
+
+    const Kaiser& kaiser_for(int src, int dst) {
+        auto& k = kaiser[{src, dst}];
+        if (!k) {
+            auto nk = std::make_unique<Kaiser>();
+            std::vector<double> t;
+            kaiser_table(src, dst, t, nk->half, nk->ratio);
+            upload(nk->table, t, "resampling table");
+            k = std::move(nk);
+        }
+        return *k;
+    }
 
     const FftTables& fft_tables_for(int n) {
         auto& t = tables[n];
@@ -419,6 +437,62 @@ STG_API stg_status stg_separate_network(stg_plan* p, const float* d_mix, float* 
             }
         }
         launch_finish(H, p->D, d_mix, d_out, st);
+    });
+}
+
+// ---- the request's audio in and the stems out ------------------------------------------------
+namespace {
+void resample_rows(stg_engine* e, const float* d_in, int interleaved, int64_t n, int in_ch, int to_channels,
+                   int rows, int src_rate, int dst_rate, int64_t out_pin, float* d_out, cudaStream_t st) {
+    if (!d_in || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+    if (n <= 0 || n > (int64_t)INT32_MAX) fail(STG_INVALID_ARGUMENT, "bad length");
+    if (in_ch < 1 || rows < 1 || rows > 4096) fail(STG_INVALID_ARGUMENT, "bad channel count");
+    if (src_rate <= 0 || dst_rate <= 0) fail(STG_INVALID_ARGUMENT, "sample rates must be positive");
+    cuda_check(cudaSetDevice(e->device), "cudaSetDevice");
+    ResampleParams p{};
+    p.in = d_in;
+    p.in_n = n;
+    p.in_ch = in_ch;
+    p.interleaved = interleaved;
+    p.to_channels = to_channels;
+    p.rows = rows;
+    p.out_n = resampled_length(n, src_rate, dst_rate);
+    p.out_pin = out_pin < 0 ? p.out_n : out_pin;
+    p.out_n = std::min(p.out_n, p.out_pin);
+    if (src_rate != dst_rate) {
+        const auto& k = e->kaiser_for(src_rate, dst_rate);
+        p.table = k.table.as<double>();
+        p.half = k.half;
+        p.ratio = k.ratio;
+    }
+    p.out = d_out;
+    cuda_check(launch_resample(p, st), "resampling kernel launch");
+}
+} // namespace
+
+STG_API int64_t stg_resampled_length(int64_t n, int32_t src_rate, int32_t dst_rate) {
+    if (n < 0 || src_rate <= 0 || dst_rate <= 0) return -1;
+    return resampled_length(n, src_rate, dst_rate);
+}
+
+STG_API stg_status stg_prepare_input(stg_engine* e, const float* d_in, int32_t interleaved, int64_t n,
+                                     int32_t n_channels, int32_t sample_rate, int32_t model_channels,
+                                     int32_t model_rate, float* d_out, void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        resample_rows(e, d_in, interleaved != 0, n, n_channels, 1, model_channels, sample_rate, model_rate, -1,
+                      d_out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+STG_API stg_status stg_restore_output(stg_engine* e, const float* d_stems, int32_t rows, int64_t len,
+                                      int32_t model_rate, int32_t sample_rate, int64_t n_samples, float* d_out,
+                                      void* stream) {
+    if (!e) return STG_INVALID_ARGUMENT;
+    return guard(e, [&] {
+        if (n_samples <= 0) fail(STG_INVALID_ARGUMENT, "bad length");
+        resample_rows(e, d_stems, 0, len, rows, 0, rows, model_rate, sample_rate, n_samples, d_out,
+                      static_cast<cudaStream_t>(stream));
     });
 }
 

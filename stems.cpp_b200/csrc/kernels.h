@@ -192,6 +192,27 @@ int fused_resident_ctas(int arch, int n_fft);
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
 
+// convert.cu. Resampling (and layout / channel conversion) of planar or interleaved audio:
+// output row k, sample i < out_n, is the resampled input channel src(k) (to_channels: 0 for
+// a mono input, else min(k, in_ch - 1); otherwise k); samples [out_n, out_pin) are zero.
+// table == nullptr copies instead of resampling (same rate).
+struct ResampleParams {
+    const float* in;
+    int64_t in_n;              // samples per input channel
+    int in_ch;
+    int interleaved;           // 1: in[i * in_ch + c]; 0: in[c * in_n + i]
+    int to_channels;
+    int rows;
+    const double* table;       // kaiser_table, or null
+    double half, ratio;
+    int64_t out_n;             // resampled length
+    int64_t out_pin;           // row stride of the output (pinned length)
+    float* out;                // [rows][out_pin]
+};
+int64_t resampled_length(int64_t n, int src_rate, int dst_rate);
+void kaiser_table(int src_rate, int dst_rate, std::vector<double>& table, double& half, double& ratio);
+cudaError_t launch_resample(const ResampleParams& p, cudaStream_t st);
+
 // norm.cu. Mono-mix normalisation of mix [C][len] into out, with scratch of
 // mono_scratch_doubles() doubles (scratch[0] = mean, scratch[1] = std afterwards).
 size_t mono_scratch_doubles();

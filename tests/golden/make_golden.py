@@ -8,7 +8,7 @@ oracle/build.sh compiles from the reference's src/stft.h and src/vr_dsp.h):
 
 What it stores:
   * primitives computed by the reference itself (st::FFT, st::VRFFT, st::torch_stft/istft,
-    st::htdemucs_spec/ispec) on small seeded inputs;
+    st::htdemucs_spec/ispec, st::resample_planar) on small seeded inputs;
   * whole separations (RoFormer, HTDemucs, TFC-TDF host loops as restated in oracle.c, with
     the network replaced by a seeded mask) whose DSP primitives are the reference's own.
 Inputs are regenerated from their seeds by the tests; a checksum of each input is stored so
@@ -27,7 +27,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(HERE))
 
 import oracle  # noqa: E402
-from golden_cases import CASES, inputs_for  # noqa: E402
+from golden_cases import CASES, RESAMPLE_RATES, inputs_for  # noqa: E402
 
 
 def main():
@@ -56,6 +56,11 @@ def main():
     h = oracle.htdemucs_spec(b, impl=R)
     out["prim_hspec_4096"] = h
     out["prim_hispec_4096"] = oracle.htdemucs_ispec(h, b.size, impl=R)
+    # -- the input resampler, straight from the reference (src/audio.h resample_planar) -----
+    io = np.random.default_rng(77).uniform(-1, 1, (3, 3001)).astype(np.float32)
+    out["io_resample_in"] = io
+    for src, dst in RESAMPLE_RATES:
+        out[f"io_resample_{src}_{dst}"] = oracle.resample_planar(io, src, dst, impl=R)
     # -- whole separations with the reference's primitives ----------------------------------
     assert oracle.use_reference(True)
     for name, case in CASES.items():

@@ -60,6 +60,9 @@ def _tfc(dim_t, chunking, overlap, length, compensate, complement):
                          complement=bool(complement)))
 
 
+# (source rate, destination rate) pairs of the resampler's golden vectors
+RESAMPLE_RATES = [(48000, 44100), (44100, 48000), (22050, 44100), (44100, 32000), (8000, 44100)]
+
 CASES = {
     "rf_mel": _rf("mel", 441 * 20, 4, 441 * 45 + 7, 0, 0),
     "rf_bs": _rf("bs", 441 * 20, 2, 441 * 33 + 100, 1, 1),

@@ -71,3 +71,16 @@ def test_missing_library_raises_instead_of_falling_back(pkg, monkeypatch, tmp_pa
     monkeypatch.setattr(pkg, "LIB_PATH", str(tmp_path / "absent.so"))
     with pytest.raises(pkg.StemsError):
         pkg.lib()
+
+
+def test_resampled_length_without_a_gpu(pkg, oracle_mod):
+    for n, src, dst in [(44100, 48000, 44100), (1, 48000, 44100), (123457, 22050, 44100), (99, 44100, 44100)]:
+        assert pkg.resampled_length(n, src, dst) == oracle_mod.resampled_length(n, src, dst)
+    assert pkg.lib().stg_resampled_length(10, 0, 44100) == -1
+
+
+def test_conversion_entry_points_reject_a_null_engine(pkg):
+    L = pkg.lib()
+    assert L.stg_prepare_input(None, None, 1, 10, 2, 48000, 2, 44100, None, None) == 1
+    assert L.stg_restore_output(None, None, 2, 10, 44100, 48000, 10, None, None) == 1
+
