@@ -282,6 +282,54 @@ STG_API stg_status stg_restore_output(stg_engine* engine, const float* d_stems, 
                                       int64_t len, int32_t model_rate, int32_t sample_rate,
                                       int64_t n_samples, float* d_out, void* stream);
 
+/* ---- VR (src/vr.cpp:215-269, 349-377; src/vr_dsp.h:43-125) -------------------------------- */
+
+/* One band of a VR model (vr.band.<i>.* of the GGUF, src/vr.cpp:306-318), lowest rate first.
+ * -1 in hpf_start / lpf_start: no filter. */
+typedef struct {
+    int32_t sample_rate, hop, n_fft, crop_start, crop_stop;
+    int32_t hpf_start, hpf_stop, lpf_start, lpf_stop;
+} stg_vr_band;
+/* A resampling FIR of the model (resample.<src>.<dst>, src/vr.cpp:320-327). */
+typedef struct {
+    int32_t src_rate, dst_rate, n_taps;
+    const float* taps;
+} stg_vr_fir;
+typedef struct {
+    uint32_t size;
+    int32_t sample_rate;        /* stems.samplerate: the last band's rate */
+    int32_t bins;               /* vr.bins */
+    int32_t pre_filter_start;   /* vr.pre_filter_start / stop */
+    int32_t pre_filter_stop;
+    int32_t n_bands;            /* 1..16 */
+    const stg_vr_band* bands;
+    int32_t n_firs;             /* every rate pair the chain crosses, both directions */
+    const stg_vr_fir* firs;
+} stg_vr_config;
+typedef struct stg_vr_plan stg_vr_plan;
+
+/* A VR separation of n_samples stereo samples at sample_rate, checked as src/vr.cpp:296-327
+ * checks a model (STG_MODEL_ERROR) and as synthesize() checks the band lengths. Band n_fft
+ * 320, 512, 640, 960, 1024 or 2048 with hop <= n_fft / 2 (else STG_UNSUPPORTED). */
+STG_API stg_status stg_plan_vr(stg_engine* engine, const stg_vr_config* config, int64_t n_samples,
+                               stg_vr_plan** out_plan);
+STG_API void stg_vr_plan_destroy(stg_vr_plan* plan);
+/* T, the frames of the spectrum; the network's input and mask are [2][bins + 1][T]. */
+STG_API stg_status stg_vr_plan_frames(const stg_vr_plan* plan, int64_t* n_frames);
+/* spectrum() (src/vr.cpp:215-239) of d_mix [2][n_samples]: kept in the plan for stg_vr_back;
+ * |spec| into d_mag [2][bins+1][T] and its peak into d_peak (one float) when not NULL, the
+ * network's input before the patching (vr.cpp:357-366). */
+STG_API stg_status stg_vr_front(stg_vr_plan* plan, const float* d_mix, float* d_mag, float* d_peak,
+                                void* stream);
+/* The two stems from the last front's spectrum and the network's mask [2][bins+1][T]:
+ * spec x mask and spec x (1 - mask), each synthesised (vr.cpp:241-269, 368-377) into
+ * d_out [2 stems][2][n_samples]. */
+STG_API stg_status stg_vr_back(stg_vr_plan* plan, const float* d_mask, float* d_out, void* stream);
+/* stg_vr_front without outputs, then stg_vr_back: the whole separation with the mask as the
+ * stand-in for the network. */
+STG_API stg_status stg_separate_vr(stg_vr_plan* plan, const float* d_mix, const float* d_mask,
+                                   float* d_out, void* stream);
+
 /* ---- the DSP primitives of src/stft.h on the device -------------------------------------- */
 
 /* torch.stft (src/stft.h:146-164) of each channel: periodic Hann, centre reflect pad,

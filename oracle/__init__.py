@@ -52,6 +52,21 @@ class TfcParams(C.Structure):
                 ("threads", C.c_int)]
 
 
+class VrBand(C.Structure):
+    _fields_ = [(k, C.c_int) for k in ("sr", "hop", "nfft", "start", "stop", "hp_start", "hp_stop",
+                                      "lp_start", "lp_stop")]
+
+
+class VrFir(C.Structure):
+    _fields_ = [("src", C.c_int), ("dst", C.c_int), ("n_taps", C.c_int), ("taps", C.POINTER(C.c_float))]
+
+
+class VrParams(C.Structure):
+    _fields_ = [("sample_rate", C.c_int), ("bins", C.c_int), ("pre_start", C.c_int), ("pre_stop", C.c_int),
+                ("n_bands", C.c_int), ("bands", C.POINTER(VrBand)), ("n_firs", C.c_int),
+                ("firs", C.POINTER(VrFir))]
+
+
 def build(force: bool = False) -> None:
     """Compile oracle.c (and the reference shim when the reference sources exist)."""
     if force or not os.path.exists(LIB_PATH):
@@ -72,6 +87,16 @@ def lib():
         L.or_htdemucs_ispec.argtypes = [C.c_int, _F64, C.c_int, C.c_int, _F32]
         L.or_use_reference.argtypes = [C.c_char_p]
         L.or_shift_offsets.argtypes = [C.c_uint, C.c_int, C.c_int, _I32P]
+        L.or_vr_stft.argtypes = [_F32, C.c_int, C.c_int, C.c_int, _F64, _I32P]
+        L.or_vr_istft.argtypes = [_F64, C.c_int, C.c_int, C.c_int, _F32]
+        L.or_vr_resampled_length.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.or_vr_resample.argtypes = [_F32, C.c_int, C.c_int, C.c_int, _F32, C.c_int, _F32]
+        L.or_vr_lowpass.restype = C.c_float
+        L.or_vr_lowpass.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.or_vr_highpass.restype = C.c_float
+        L.or_vr_highpass.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.or_vr_n_frames.argtypes = [C.POINTER(VrParams), C.c_int]
+        L.or_vr_separate.argtypes = [C.POINTER(VrParams), _F32, C.c_int, _F32, _F32]
         L.or_resampled_length.restype = C.c_longlong
         L.or_resampled_length.argtypes = [C.c_longlong, C.c_int, C.c_int]
         L.or_resample_planar.argtypes = [_F32, C.c_int, C.c_int, C.c_int, C.c_int, _F32, _I32P]
@@ -114,6 +139,9 @@ def ref_lib():
         R.ref_htdemucs_spec.argtypes = [C.c_int, _F32, C.c_int, _F64, _I32P]
         R.ref_htdemucs_ispec.argtypes = [C.c_int, _F64, C.c_int, C.c_int, _F32]
         R.ref_resample_planar.argtypes = [_F32, C.c_int, C.c_int, C.c_int, C.c_int, _F32, _I32P]
+        R.ref_vr_stft.argtypes = [_F32, C.c_int, C.c_int, C.c_int, _F64, _I32P]
+        R.ref_vr_istft.argtypes = [_F64, C.c_int, C.c_int, C.c_int, _F32]
+        R.ref_vr_resample.argtypes = [_F32, C.c_int, C.c_int, C.c_int, _F32, C.c_int, _F32]
         _ref = R
     return _ref
 
@@ -215,6 +243,86 @@ def restore_output(stems, model_rate, sample_rate, n_samples, impl=None):
     k = min(n_samples, y.shape[1])
     out[:, :k] = y[:, :k]
     return out
+
+
+# ---- VR (src/vr_dsp.h, src/vr.cpp) ------------------------------------------------------------
+def vr_stft(wave, nfft, hop, impl=None):
+    """vr_stft of stereo wave [2][n]: complex128 [2][nfft/2+1][n/hop+1] (complex64 values)."""
+    wave = np.ascontiguousarray(wave, np.float32)
+    n = wave.shape[1]
+    frames = n // hop + 1
+    out = np.zeros(2 * (nfft // 2 + 1) * frames, np.complex128)
+    got = C.c_int(0)
+    f = impl.ref_vr_stft if impl is not None else lib().or_vr_stft
+    _check(f(wave.reshape(-1), n, nfft, hop, out.view(np.float64), C.byref(got)), "vr_stft")
+    return out.reshape(2, nfft // 2 + 1, frames)
+
+
+def vr_istft(spec, nfft, hop, impl=None):
+    spec = np.ascontiguousarray(spec, np.complex128)
+    frames = spec.shape[2]
+    out = np.zeros(2 * hop * (frames - 1), np.float32)
+    f = impl.ref_vr_istft if impl is not None else lib().or_vr_istft
+    _check(f(spec.reshape(-1).view(np.float64), frames, nfft, hop, out), "vr_istft")
+    return out.reshape(2, -1)
+
+
+def vr_resample(x, src, dst, fir, impl=None):
+    x = np.ascontiguousarray(x, np.float32)
+    fir = np.ascontiguousarray(fir, np.float32)
+    n = x.shape[1]
+    m = lib().or_vr_resampled_length(n, src, dst)
+    out = np.zeros(2 * m, np.float32)
+    f = impl.ref_vr_resample if impl is not None else lib().or_vr_resample
+    _check(f(x.reshape(-1), n, src, dst, fir, fir.size, out), "vr_resample")
+    return out.reshape(2, m)
+
+
+def vr_fir(src, dst):
+    """The model's resampling FIR as the reference's converter designs it (tools/convert_vr.py:
+    199-211): scipy.signal.firwin(20*m + 1, 1/m, kaiser 5.0) * up, float32."""
+    from math import gcd
+    from scipy.signal import firwin
+    g = gcd(src, dst)
+    up, down = dst // g, src // g
+    m = max(up, down)
+    return (firwin(20 * m + 1, 1.0 / m, window=("kaiser", 5.0)).astype(np.float32) * up).astype(np.float32)
+
+
+def vr_params(bands, sample_rate=44100, bins=None, pre_start=0, pre_stop=0):
+    """bands: dicts with sr, hop, nfft, start, stop and optional hp_start/hp_stop/lp_start/lp_stop
+    (-1 when absent), lowest rate first. The FIRs of every rate pair come from vr_fir."""
+    bl = (VrBand * len(bands))()
+    for i, b in enumerate(bands):
+        bl[i] = VrBand(b["sr"], b["hop"], b["nfft"], b["start"], b["stop"], b.get("hp_start", -1),
+                       b.get("hp_stop", -1), b.get("lp_start", -1), b.get("lp_stop", -1))
+    rates = sorted({b["sr"] for b in bands} | {sample_rate})
+    keep, firs = [], []
+    for s in rates:
+        for d in rates:
+            if s != d:
+                h = vr_fir(s, d)
+                keep.append(h)
+                firs.append(VrFir(s, d, h.size, h.ctypes.data_as(C.POINTER(C.c_float))))
+    fl = (VrFir * max(1, len(firs)))(*firs)
+    if bins is None:
+        bins = sum(b["stop"] - b["start"] for b in bands)
+    p = VrParams(sample_rate, bins, pre_start, pre_stop, len(bands), bl, len(firs), fl)
+    p._keep = (bl, fl, keep, bands)
+    return p
+
+
+def vr_n_frames(p, length):
+    return lib().or_vr_n_frames(C.byref(p), length)
+
+
+def vr_separate(p, mix, mask):
+    mix = np.ascontiguousarray(mix, np.float32)
+    n = mix.shape[1]
+    out = np.zeros(4 * n, np.float32)
+    _check(lib().or_vr_separate(C.byref(p), mix.reshape(-1), n, np.ascontiguousarray(mask, np.float32).reshape(-1),
+                                out), "vr_separate")
+    return out.reshape(2, 2, n)
 
 
 # ---- glue --------------------------------------------------------------------------------

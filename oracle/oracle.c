@@ -1086,3 +1086,235 @@ int or_resample_planar(const float* in, int n, int ch, int src_rate, int dst_rat
     free(acc); free(table);
     return 0;
 }
+
+/* ===================================================================================== */
+/* VR: vr_stft / vr_istft / vr_resample / band filters (vr_dsp.h:43-125), spectrum and     */
+/* synthesize (vr.cpp:215-269), separate with the network replaced by a given mask          */
+/* (vr.cpp:349-377)                                                                         */
+/* ===================================================================================== */
+int or_vr_stft(const float* wave, int n, int nfft, int hop, double* outd, int* n_frames) {
+    if (!wave || !outd || !n_frames || n < 1 || nfft < 2 || hop < 1) return ERR_ARG;
+    const int frames = n / hop + 1, F = nfft / 2 + 1;                     /* :44-45 */
+    cplx* out = (cplx*)outd;
+    double* win = hann_periodic(nfft);
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    int rc = 0;
+    for (int c = 0; c < 2 && !rc; c++)
+        for (int t = 0; t < frames && !rc; t++) {
+            for (int j = 0; j < nfft; j++) {                              /* :50-53 */
+                const int k = t * hop + j - nfft / 2;
+                buf[j] = k >= 0 && k < n ? wave[(size_t)c * n + k] * win[j] : 0.0;
+            }
+            rc = or_vrfft(nfft, (double*)buf, 0);
+            for (int f = 0; f < F; f++)                                   /* :55-59: complex64 */
+                out[((size_t)c * F + f) * frames + t] = (double)(float)creal(buf[f]) + I * (double)(float)cimag(buf[f]);
+        }
+    *n_frames = frames;
+    free(buf); free(win);
+    return rc;
+}
+
+int or_vr_istft(const double* specd, int frames, int nfft, int hop, float* out) {
+    if (!specd || !out || frames < 1 || nfft < 2 || hop < 1) return ERR_ARG;
+    const cplx* spec = (const cplx*)specd;
+    const int F = nfft / 2 + 1, n = hop * (frames - 1);                    /* :65 */
+    const size_t full = (size_t)nfft + n;
+    double* win = hann_periodic(nfft);
+    double* env = (double*)calloc(full, sizeof(double));
+    double* y = (double*)malloc(sizeof(double) * full);
+    cplx* buf = (cplx*)malloc(sizeof(cplx) * nfft);
+    for (int t = 0; t < frames; t++)                                      /* :69-70 */
+        for (int j = 0; j < nfft; j++) env[(size_t)t * hop + j] += win[j] * win[j];
+    int rc = 0;
+    for (int c = 0; c < 2 && !rc; c++) {
+        memset(y, 0, sizeof(double) * full);
+        for (int t = 0; t < frames && !rc; t++) {
+            for (int f = 0; f < F; f++) buf[f] = spec[((size_t)c * F + f) * frames + t];
+            buf[0] = creal(buf[0]);                                       /* :77-79 */
+            buf[F - 1] = creal(buf[F - 1]);
+            for (int f = 1; f < F - 1; f++) buf[nfft - f] = conj(buf[f]);
+            rc = or_vrfft(nfft, (double*)buf, 1);
+            for (int j = 0; j < nfft; j++) y[(size_t)t * hop + j] += creal(buf[j]) / nfft * win[j];
+        }
+        for (int j = 0; j < n; j++) {                                     /* :83-86 */
+            const size_t k = (size_t)j + nfft / 2;
+            out[(size_t)c * n + j] = env[k] > 1e-11 ? (float)(y[k] / env[k]) : 0.0f;
+        }
+    }
+    free(buf); free(y); free(env); free(win);
+    return rc;
+}
+
+static int gcd_int(int a, int b) { while (b) { const int t = a % b; a = b; b = t; } return a; }
+
+int or_vr_resampled_length(int n, int src, int dst) {
+    if (src == dst) return n;
+    const int g = gcd_int(src, dst), up = dst / g, down = src / g;
+    return (int)(((int64_t)n * up + down - 1) / down);                    /* :96 */
+}
+
+int or_vr_resample(const float* x, int n, int src, int dst, const float* fir, int n_taps, float* y) {
+    if (!x || !y || n < 1 || src <= 0 || dst <= 0) return ERR_ARG;
+    if (src == dst) { memcpy(y, x, sizeof(float) * 2 * (size_t)n); return 0; }
+    if (!fir || n_taps < 1) return ERR_ARG;
+    const int g = gcd_int(src, dst), up = dst / g, down = src / g;
+    const int out_n = or_vr_resampled_length(n, src, dst);
+    const int half = n_taps / 2;
+    for (int c = 0; c < 2; c++)                                           /* :99-108 */
+        for (int j = 0; j < out_n; j++) {
+            const int64_t pos = (int64_t)j * down + half;
+            const int64_t lo0 = (pos - n_taps + up) / up;
+            const int lo = (int)(lo0 > 0 ? lo0 : 0);
+            const int64_t hi0 = pos / up;
+            const int hi = (int)(hi0 < n - 1 ? hi0 : n - 1);
+            double sum = 0;
+            for (int i = lo; i <= hi; i++) sum += (double)x[(size_t)c * n + i] * fir[(size_t)(pos - (int64_t)i * up)];
+            y[(size_t)c * out_n + j] = (float)sum;
+        }
+    return 0;
+}
+
+float or_vr_lowpass(int f, int start, int stop) {                       /* :113-118 */
+    if (start < 0) return 1;
+    if (f < start - 1) return 1;
+    if (f >= stop) return 0;
+    return 1.0f - (float)(f - start + 1) / (stop - start);
+}
+float or_vr_highpass(int f, int start, int stop) {                      /* :119-125 */
+    if (start <= 0) return 1;
+    if (f <= stop + 1) return 0;
+    if (f >= start + 1) return 1;
+    return (float)(f - stop - 1) / (start - stop);
+}
+
+static const or_vr_fir* vr_fir(const or_vr_params* p, int src, int dst) {
+    for (int k = 0; k < p->n_firs; k++)
+        if (p->firs[k].src == src && p->firs[k].dst == dst) return &p->firs[k];
+    return NULL;
+}
+
+/* Resample [2][n] from src to dst with the model's FIR (vr.cpp:211-214); *out is malloc'd. */
+static int vr_resample_model(const or_vr_params* p, const float* x, int n, int src, int dst, float** out, int* out_n) {
+    const int m = or_vr_resampled_length(n, src, dst);
+    *out = (float*)malloc(sizeof(float) * 2 * (size_t)m);
+    *out_n = m;
+    if (src == dst) { memcpy(*out, x, sizeof(float) * 2 * (size_t)n); return 0; }
+    const or_vr_fir* f = vr_fir(p, src, dst);
+    if (!f) return ERR_ARG;
+    return or_vr_resample(x, n, src, dst, f->taps, f->n_taps, *out);
+}
+
+int or_vr_n_frames(const or_vr_params* p, int len) {                     /* vr.cpp:219-225 */
+    int n = len, rate = p->sample_rate, T = INT32_MAX;
+    for (int i = p->n_bands - 1; i >= 0; i--) {
+        n = or_vr_resampled_length(n, rate, p->bands[i].sr);
+        rate = p->bands[i].sr;
+        const int frames = n / p->bands[i].hop + 1;
+        if (frames < T) T = frames;
+    }
+    return T;
+}
+
+/* spectrum() (vr.cpp:215-236): spec [2][bins+1][T] complex. */
+static int vr_spectrum(const or_vr_params* p, const float* mix, int len, cplx* spec, int T) {
+    const int B = p->n_bands, F1 = p->bins + 1;
+    cplx** specs = (cplx**)calloc(B, sizeof(cplx*));
+    int* frames = (int*)calloc(B, sizeof(int));
+    float* wave = (float*)malloc(sizeof(float) * 2 * (size_t)len);
+    memcpy(wave, mix, sizeof(float) * 2 * (size_t)len);
+    int n = len, rate = p->sample_rate, rc = 0;
+    for (int i = B - 1; i >= 0 && !rc; i--) {
+        float* w2 = NULL;
+        int n2 = 0;
+        rc = vr_resample_model(p, wave, n, rate, p->bands[i].sr, &w2, &n2);
+        free(wave);
+        wave = w2; n = n2; rate = p->bands[i].sr;
+        const int F = p->bands[i].nfft / 2 + 1;
+        specs[i] = (cplx*)malloc(sizeof(cplx) * 2 * (size_t)F * (n / p->bands[i].hop + 1));
+        if (!rc) rc = or_vr_stft(wave, n, p->bands[i].nfft, p->bands[i].hop, (double*)specs[i], &frames[i]);
+    }
+    memset(spec, 0, sizeof(cplx) * 2 * (size_t)F1 * T);
+    int off = 0;
+    for (int i = 0; i < B && !rc; i++) {                                  /* :228-235 */
+        const or_vr_band* b = &p->bands[i];
+        const int F = b->nfft / 2 + 1;
+        for (int c = 0; c < 2; c++)
+            for (int f = b->start; f < b->stop; f++)
+                for (int t = 0; t < T; t++)
+                    spec[((size_t)c * F1 + off + f - b->start) * T + t] = specs[i][((size_t)c * F + f) * frames[i] + t];
+        off += b->stop - b->start;
+    }
+    if (p->pre_start > 0 && !rc)                                          /* :236-239 */
+        for (int c = 0; c < 2; c++)
+            for (int f = 0; f <= p->bins; f++)
+                for (int t = 0; t < T; t++) spec[((size_t)c * F1 + f) * T + t] *= or_vr_lowpass(f, p->pre_start, p->pre_stop);
+    for (int i = 0; i < B; i++) free(specs[i]);
+    free(specs); free(frames); free(wave);
+    return rc;
+}
+
+/* synthesize() (vr.cpp:241-269): out [2][len]. */
+static int vr_synthesize(const or_vr_params* p, const cplx* spec, int T, int len, float* out) {
+    const int B = p->n_bands, F1 = p->bins + 1;
+    float* wave = NULL;
+    int off = 0, n = 0, rc = 0;
+    for (int i = 0; i < B && !rc; i++) {
+        const or_vr_band* b = &p->bands[i];
+        const int F = b->nfft / 2 + 1;
+        cplx* part = (cplx*)calloc((size_t)2 * F * T, sizeof(cplx));
+        for (int c = 0; c < 2; c++)
+            for (int f = b->start; f < b->stop; f++) {
+                const float gain = or_vr_highpass(f, b->hp_start, b->hp_stop - 1) *
+                                   (i + 1 == B ? 1 : or_vr_lowpass(f, b->lp_start, b->lp_stop));
+                for (int t = 0; t < T; t++)
+                    part[((size_t)c * F + f) * T + t] = spec[((size_t)c * F1 + off + f - b->start) * T + t] * (double)gain;
+            }
+        off += b->stop - b->start;
+        const int bn = b->hop * (T - 1);
+        float* add = (float*)malloc(sizeof(float) * 2 * (size_t)bn);
+        rc = or_vr_istft((const double*)part, T, b->nfft, b->hop, add);
+        free(part);
+        if (!wave) { wave = add; n = bn; }
+        else {
+            if (n != bn) rc = ERR_ARG;                                    /* "bands do not align" */
+            for (size_t k = 0; k < 2 * (size_t)n && !rc; k++) wave[k] += add[k];
+            free(add);
+        }
+        if (i + 1 < B && !rc) {
+            float* w2 = NULL;
+            int n2 = 0;
+            rc = vr_resample_model(p, wave, n, b->sr, p->bands[i + 1].sr, &w2, &n2);
+            free(wave);
+            wave = w2; n = n2;
+        }
+    }
+    for (int c = 0; c < 2 && !rc; c++)
+        for (int j = 0; j < len; j++) out[(size_t)c * len + j] = j < n ? wave[(size_t)c * n + j] : 0.0f;
+    free(wave);
+    return rc;
+}
+
+int or_vr_separate(const or_vr_params* p, const float* mix, int len, const float* mask, float* out) {
+    if (!p || !mix || !mask || !out || len <= 0 || p->n_bands < 1) return ERR_ARG;
+    const int T = or_vr_n_frames(p, len), F1 = p->bins + 1;
+    const size_t K = (size_t)2 * F1 * T;
+    cplx* spec = (cplx*)malloc(sizeof(cplx) * K);
+    cplx* z = (cplx*)malloc(sizeof(cplx) * K);
+    int rc = vr_spectrum(p, mix, len, spec, T);
+    float peak = 0;                                                       /* :357-360 */
+    for (size_t k = 0; k < K && !rc; k++) {
+        const float m = (float)cabs(spec[k]);
+        if (m > peak) peak = m;
+    }
+    if (!rc && peak == 0) {
+        memset(out, 0, sizeof(float) * 4 * (size_t)len);
+    } else {
+        for (int s = 0; s < 2 && !rc; s++) {                              /* :370-376 */
+            for (size_t k = 0; k < K; k++) z[k] = spec[k] * (s == 0 ? mask[k] : 1 - mask[k]);
+            rc = vr_synthesize(p, z, T, len, out + (size_t)s * 2 * len);
+        }
+    }
+    free(z); free(spec);
+    return rc;
+}
+

@@ -50,6 +50,29 @@ int or_shift_offsets(unsigned seed, int shifts, int hi, int* out);
 long long or_resampled_length(long long n, int src_rate, int dst_rate);
 int or_resample_planar(const float* in, int n, int ch, int src_rate, int dst_rate, float* out, int* out_n);
 
+/* ---- VR (src/vr_dsp.h:43-125, src/vr.cpp:215-269, 349-377) ----------------------------- */
+/* Stereo only, as the reference. Spectra are [2][nfft/2+1][frames] complex (interleaved
+ * double pairs holding complex64 values). */
+int or_vr_stft(const float* wave, int n, int nfft, int hop, double* out, int* n_frames);
+int or_vr_istft(const double* spec, int frames, int nfft, int hop, float* out);   /* out [2][hop*(frames-1)] */
+int or_vr_resampled_length(int n, int src_rate, int dst_rate);
+int or_vr_resample(const float* x, int n, int src_rate, int dst_rate, const float* fir, int n_taps, float* y);
+float or_vr_lowpass(int f, int start, int stop);
+float or_vr_highpass(int f, int start, int stop);
+typedef struct { int sr, hop, nfft, start, stop, hp_start, hp_stop, lp_start, lp_stop; } or_vr_band;
+typedef struct { int src, dst, n_taps; const float* taps; } or_vr_fir;
+typedef struct {
+    int sample_rate, bins, pre_start, pre_stop;
+    int n_bands;
+    const or_vr_band* bands;   /* lowest rate first, as vr.band.0 .. */
+    int n_firs;
+    const or_vr_fir* firs;     /* the model's resample.<src>.<dst> FIRs */
+} or_vr_params;
+int or_vr_n_frames(const or_vr_params* p, int len);
+/* mask [2][bins+1][T] (the network's output, the stand-in); out [2 stems][2][len]:
+ * spectrum x mask, spectrum x (1 - mask), each synthesised. */
+int or_vr_separate(const or_vr_params* p, const float* mix, int len, const float* mask, float* out);
+
 /* Swap the primitives above (as used by the glue below) for the reference's own compiled
  * code. path = NULL restores the restatement. Returns 0 on success. */
 int or_use_reference(const char* path);

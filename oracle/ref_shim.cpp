@@ -116,4 +116,34 @@ int ref_resample_planar(const float* in, int n, int ch, int src_rate, int dst_ra
     } catch (...) { return -3; }
 }
 
+int ref_vr_stft(const float* wave, int n, int nfft, int hop, double* out, int* n_frames) {
+    try {
+        const std::vector<float> w(wave, wave + 2 * (size_t)n);
+        const st::VRBand b = {0, hop, nfft, 0, nfft / 2 + 1, -1, -1, -1, -1};
+        int frames = 0;
+        put(st::vr_stft(w, n, b, frames), out);
+        *n_frames = frames;
+        return 0;
+    } catch (...) { return -3; }
+}
+
+int ref_vr_istft(const double* spec, int frames, int nfft, int hop, float* out) {
+    try {
+        const st::VRBand b = {0, hop, nfft, 0, nfft / 2 + 1, -1, -1, -1, -1};
+        const std::vector<float> y = st::vr_istft(get(spec, (size_t)2 * (nfft / 2 + 1) * frames), frames, b);
+        std::memcpy(out, y.data(), y.size() * sizeof(float));
+        return 0;
+    } catch (...) { return -3; }
+}
+
+int ref_vr_resample(const float* x, int n, int src, int dst, const float* fir, int n_taps, float* y) {
+    try {
+        const std::vector<float> in(x, x + 2 * (size_t)n), h(fir, fir + n_taps);
+        int m = 0;
+        const std::vector<float> out = st::vr_resample(in, n, src, dst, h, m);
+        std::memcpy(y, out.data(), out.size() * sizeof(float));
+        return 0;
+    } catch (...) { return -3; }
+}
+
 } // extern "C"

@@ -70,6 +70,22 @@ class PlanInfo(C.Structure):
                 ("out_floats", C.c_int64), ("scratch_bytes", C.c_int64)]
 
 
+class VrBandC(C.Structure):
+    _fields_ = [(k, C.c_int32) for k in ("sample_rate", "hop", "n_fft", "crop_start", "crop_stop", "hpf_start",
+                                        "hpf_stop", "lpf_start", "lpf_stop")]
+
+
+class VrFirC(C.Structure):
+    _fields_ = [("src_rate", C.c_int32), ("dst_rate", C.c_int32), ("n_taps", C.c_int32),
+                ("taps", C.POINTER(C.c_float))]
+
+
+class VrConfig(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("sample_rate", C.c_int32), ("bins", C.c_int32),
+                ("pre_filter_start", C.c_int32), ("pre_filter_stop", C.c_int32), ("n_bands", C.c_int32),
+                ("bands", C.POINTER(VrBandC)), ("n_firs", C.c_int32), ("firs", C.POINTER(VrFirC))]
+
+
 PROGRESS_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int32, C.c_int32)
 CANCEL_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p)
 
@@ -119,6 +135,12 @@ _SIGNATURES = {
                                       C.c_int32, C.c_void_p, C.c_void_p]),
     "stg_restore_output": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_int64,
                                        C.c_void_p, C.c_void_p]),
+    "stg_plan_vr": (C.c_int32, [C.c_void_p, C.POINTER(VrConfig), C.c_int64, C.POINTER(C.c_void_p)]),
+    "stg_vr_plan_destroy": (None, [C.c_void_p]),
+    "stg_vr_plan_frames": (C.c_int32, [C.c_void_p, C.POINTER(C.c_int64)]),
+    "stg_vr_front": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_vr_back": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_vr": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_torch_stft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int64,
                                    C.c_void_p, C.c_void_p]),
     "stg_torch_istft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32,
@@ -245,6 +267,27 @@ class Engine:
         self._check(lib().stg_torch_istft(self._h, n_fft, hop, int(normalized), spec.data_ptr(), C_, T, _ptr(y),
                                           _stream_of(stream, spec)), "torch_istft")
         return y
+
+    def plan_vr(self, n_samples, bands, firs, sample_rate=44100, bins=None, pre_filter_start=0,
+                pre_filter_stop=0):
+        """A VR separation (src/vr.cpp). bands: dicts with sample_rate, hop, n_fft, crop_start,
+        crop_stop and optional hpf_start/hpf_stop/lpf_start/lpf_stop (-1 = none), lowest rate
+        first; firs: {(src_rate, dst_rate): float32 taps}, the model's resampling filters."""
+        bl = (VrBandC * len(bands))()
+        for i, b in enumerate(bands):
+            bl[i] = VrBandC(b["sample_rate"], b["hop"], b["n_fft"], b["crop_start"], b["crop_stop"],
+                            b.get("hpf_start", -1), b.get("hpf_stop", -1), b.get("lpf_start", -1),
+                            b.get("lpf_stop", -1))
+        taps = {k: np.ascontiguousarray(v, dtype=np.float32) for k, v in firs.items()}
+        fl = (VrFirC * max(1, len(taps)))(*[VrFirC(s, d, t.size, t.ctypes.data_as(C.POINTER(C.c_float)))
+                                             for (s, d), t in taps.items()])
+        if bins is None:
+            bins = sum(b["crop_stop"] - b["crop_start"] for b in bands)
+        cfg = VrConfig(C.sizeof(VrConfig), sample_rate, bins, pre_filter_start, pre_filter_stop, len(bands), bl,
+                       len(taps), fl)
+        h = C.c_void_p()
+        self._check(lib().stg_plan_vr(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_vr")
+        return VrPlan(self, h, n_samples, bins)
 
     # -- the request's audio in and the stems out (src/libstems.cpp:160-199) -----------------
     def prepare_input(self, samples, n_channels, sample_rate, interleaved=True, model_channels=2,
@@ -447,3 +490,41 @@ class Plan:
         rc = lib().stg_separate_host(self._h, mix.ctypes.data, mask.ctypes.data, out.ctypes.data, st)
         self.engine._check(rc, "separate_host")
         return out
+
+
+class VrPlan:
+    """A VR model's spectral path bound to one track length (stg_plan_vr)."""
+
+    def __init__(self, engine: Engine, handle, n_samples, bins):
+        self.engine = engine
+        self._h = handle
+        self.n_samples = n_samples
+        self.bins = bins
+        t = C.c_int64()
+        engine._check(lib().stg_vr_plan_frames(self._h, C.byref(t)), "vr_plan_frames")
+        self.n_frames = t.value
+        self.mask_shape = (2, bins + 1, self.n_frames)
+        self.out_shape = (2, 2, n_samples)
+
+    def front(self, mix, mag=None, peak=None, stream=None):
+        self.engine._check(lib().stg_vr_front(self._h, _ptr(mix), _ptr(mag), _ptr(peak), _stream_of(stream, mix)),
+                           "vr_front")
+
+    def back(self, mask, out, stream=None):
+        self.engine._check(lib().stg_vr_back(self._h, _ptr(mask), _ptr(out), _stream_of(stream, mask)), "vr_back")
+
+    def separate(self, mix, mask, out, stream=None):
+        self.engine._check(lib().stg_separate_vr(self._h, _ptr(mix), _ptr(mask), _ptr(out),
+                                                 _stream_of(stream, mix, out)), "separate_vr")
+
+    def close(self):
+        if self._h:
+            lib().stg_vr_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

@@ -37,6 +37,23 @@ template <> struct FftCfg<7680> {
     static constexpr bool SMEM_TW = false, SMEM_WIN = false;
     using Plan = RadixList<8, 8, 8, 15>;
 };
+// The VR bands' sizes (src/vr_dsp.h, 320 to 2048 points): front and back kernels only.
+template <int N, int TT, class P> struct SmallFft {
+    static constexpr int T = TT, MINB = 1, HOPMAX = N / 2;
+    static constexpr int PF_GROUPS = 1;
+    static constexpr bool AHEAD = false;
+    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    using Plan = P;
+};
+template <> struct FftCfg<320> : SmallFft<320, 64, RadixList<8, 8, 5>> {};
+template <> struct FftCfg<512> : SmallFft<512, 64, RadixList<8, 8, 8>> {};
+template <> struct FftCfg<640> : SmallFft<640, 64, RadixList<8, 8, 10>> {};
+template <> struct FftCfg<960> : SmallFft<960, 64, RadixList<8, 8, 15>> {};
+template <> struct FftCfg<1024> : SmallFft<1024, 64, RadixList<8, 8, 16>> {};
+
+// The largest hop of the front kernel's input prefetch: half the frame, which covers every
+// STFT the reference runs (the fused kernel's own limit is FftCfg::HOPMAX).
+template <int N> __host__ __device__ constexpr int split_hopmax() { return N / 2; }
 
 __device__ __forceinline__ int64_t reflect1(int64_t j, int64_t n) {
     if (j < 0) j = -j;
@@ -86,8 +103,14 @@ template <int T, int HOPMAX> struct InPrefetch {
 template <class Params>
 __device__ __forceinline__ float2 frame_sample(const Params& p, const ChunkDesc& cd, const float* chL,
                                                const float* chR, int lxf, int q) {
-    int r = (int)reflect1((int64_t)q - p.g.n_fft / 2, lxf);
-    if (p.g.ht_pad) r = (int)reflect1(r - p.g.ht_pad, p.g.Lc);
+    int r;
+    if (p.g.zero_pad) {   // zeros around the signal instead of its mirror (src/vr_dsp.h:50-53)
+        r = q - p.g.n_fft / 2;
+        if (r < 0 || r >= p.g.Lc) return make_float2(0.0f, 0.0f);
+    } else {
+        r = (int)reflect1((int64_t)q - p.g.n_fft / 2, lxf);
+        if (p.g.ht_pad) r = (int)reflect1(r - p.g.ht_pad, p.g.Lc);
+    }
     const float a = chunk_sample(p, cd, chL, r);
     const float b = p.n_channels > 1 ? chunk_sample(p, cd, chR, r) : 0.0f;
     return make_float2(a, b);

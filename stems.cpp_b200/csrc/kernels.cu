@@ -419,6 +419,11 @@ template <int... Rs> static std::vector<int> radix_vec(RadixList<Rs...>) { retur
 
 std::vector<int> fused_radices(int n) {
     switch (n) {
+        case 320: return radix_vec(FftCfg<320>::Plan{});
+        case 512: return radix_vec(FftCfg<512>::Plan{});
+        case 640: return radix_vec(FftCfg<640>::Plan{});
+        case 960: return radix_vec(FftCfg<960>::Plan{});
+        case 1024: return radix_vec(FftCfg<1024>::Plan{});
         case 2048: return radix_vec(FftCfg<2048>::Plan{});
         case 4096: return radix_vec(FftCfg<4096>::Plan{});
         case 7680: return radix_vec(FftCfg<7680>::Plan{});

@@ -49,6 +49,7 @@ struct ChunkGroup {
 // A padded position q maps to chunk-local sample reflect(q - n_fft/2, Lc) (torch.stft's
 // centre pad), or, for HTDemucs' _spec, reflect(reflect(q - n_fft/2, ht_lxf) - ht_pad, Lc).
 // The chunk's output sample j (iSTFT with window-sum normalisation) sits at q = j + out_offset.
+// zero_pad: chunk-local sample q - n_fft/2, zero outside [0, Lc) (VR's zero-centred STFT).
 struct FrameGeom {
     int n_fft, hop;
     int Lc;
@@ -58,6 +59,7 @@ struct FrameGeom {
     int ht_lxf;
     int out_offset;
     int Lout;
+    int zero_pad;
 };
 
 struct FusedParams {
@@ -191,6 +193,8 @@ int fused_resident_ctas(int arch, int n_fft);
 // The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
+bool split_supported(int n_fft);   // n_fft the front and back kernels take
+int split_max_hop(int n_fft);
 
 // convert.cu. Resampling (and layout / channel conversion) of planar or interleaved audio:
 // output row k, sample i < out_n, is the resampled input channel src(k) (to_channels: 0 for

@@ -62,8 +62,10 @@ std::vector<float> torch_linspace(float a, float b, int n) {
 // Sizes shared by every arch, and the window-sum envelope of a chunk's output.
 void finish_plan(HostPlan& P, int env_frames) {
     const int N = P.g.n_fft, hop = P.g.hop;
-    if (!fused_supported(N)) fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
-    if (hop > fused_max_hop(N) || hop > N)
+    // single-chunk primitives run the front and back kernels only; plans also the fused one
+    if (P.primitive ? !split_supported(N) : !fused_supported(N))
+        fail(STG_UNSUPPORTED, "n_fft " + std::to_string(N) + " is not implemented");
+    if (hop > (P.primitive ? split_max_hop(N) : fused_max_hop(N)) || hop > N)
         fail(STG_UNSUPPORTED, "hop " + std::to_string(hop) + " is too large for n_fft " + std::to_string(N));
     // Frames per tile. The persistent CTAs take work items (chunk, tile) round-robin, so a
     // launch lasts ceil(items / resident CTAs) rounds of one tile each; a tile costs its K
@@ -463,16 +465,16 @@ void single_chunk(HostPlan& P, int64_t len) {
 } // namespace
 
 void build_torch_stft(HostPlan& P, int n_fft, int hop, bool normalized, int n_channels, int64_t len,
-                      bool inverse) {
+                      bool inverse, bool zero_pad) {
     if (n_channels < 1 || n_channels > 2) fail(STG_INVALID_ARGUMENT, "n_channels must be 1 or 2");
     if (hop < 1 || len < 1 || len > INT32_MAX / 4) fail(STG_INVALID_ARGUMENT, "bad hop or length");
-    if (!inverse && len <= n_fft / 2)
+    if (!inverse && !zero_pad && len <= n_fft / 2)
         fail(STG_INVALID_ARGUMENT, "reflect pad larger than the signal");   // stft.h:59
     P.arch = ARCH_TFC;                                                // plain CaC-free spectra
     P.len = len;
     P.C = n_channels;
     const int T = (int)(len / hop) + 1;                               // stft.h:153
-    P.g = FrameGeom{n_fft, hop, (int)len, T, 0, 0, 0, n_fft / 2, hop * (T - 1)};
+    P.g = FrameGeom{n_fft, hop, (int)len, T, 0, 0, 0, n_fft / 2, hop * (T - 1), zero_pad ? 1 : 0};
     P.fwd_scale = normalized ? (float)(1.0 / std::sqrt((double)n_fft)) : 1.0f;
     P.inv_scale = (float)((normalized ? std::sqrt((double)n_fft) : 1.0) / n_fft);
     single_chunk(P, len);

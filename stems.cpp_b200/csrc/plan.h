@@ -101,9 +101,11 @@ struct PlanDevice {
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
 // Single-chunk plans of the DSP primitives: torch.stft / torch.istft (src/stft.h:146-197) of
 // `len` samples (the istft's output length), HTDemucs _spec/_ispec (src/stft.h:79-140).
-// For the inverse, len = hop * (frames - 1), the istft's output length.
+// For the inverse, len = hop * (frames - 1), the istft's output length. zero_pad: VR's
+// zero-centred forward STFT (src/vr_dsp.h:43-62) instead of torch's reflect padding; VR's
+// inverse (src/vr_dsp.h:64-88) is torch's.
 void build_torch_stft(HostPlan& P, int n_fft, int hop, bool normalized, int n_channels, int64_t len,
-                      bool inverse);
+                      bool inverse, bool zero_pad = false);
 void build_htdemucs_spec(HostPlan& P, int n_channels, int64_t len);
 void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len);
 void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len);

@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
     const float half_fwd = 0.5f * p.fwd_scale;
     if (p.layout == FRONT_BANDS)
         for (int i = tid; i < p.n_bins; i += T) btab[i] = __ldg(p.bin_tab + i);
-    InPrefetch<T, FftCfg<N>::HOPMAX> nx;
+    InPrefetch<T, split_hopmax<N>()> nx;
     __shared__ double red[2 * (T / 32)];
 
     for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
@@ -317,9 +317,24 @@ template <int N> cudaError_t back_t(const SplitParams& p, cudaStream_t st) {
 
 } // namespace
 
+bool split_supported(int n) {
+    switch (n) {
+        case 320: case 512: case 640: case 960: case 1024: case 2048: case 4096: case 7680: return true;
+    }
+    return false;
+}
+
+int split_max_hop(int n) { return split_supported(n) ? n / 2 : 0; }
+
 cudaError_t launch_front(const SplitParams& p, cudaStream_t st) {
     if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
+    if (p.g.hop > split_max_hop(p.g.n_fft)) return cudaErrorInvalidValue;
     switch (p.g.n_fft) {
+        case 320: return front_t<320>(p, st);
+        case 512: return front_t<512>(p, st);
+        case 640: return front_t<640>(p, st);
+        case 960: return front_t<960>(p, st);
+        case 1024: return front_t<1024>(p, st);
         case 2048: return front_t<2048>(p, st);
         case 4096: return front_t<4096>(p, st);
         case 7680: return front_t<7680>(p, st);
@@ -330,6 +345,11 @@ cudaError_t launch_front(const SplitParams& p, cudaStream_t st) {
 cudaError_t launch_back(const SplitParams& p, cudaStream_t st) {
     if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
     switch (p.g.n_fft) {
+        case 320: return back_t<320>(p, st);
+        case 512: return back_t<512>(p, st);
+        case 640: return back_t<640>(p, st);
+        case 960: return back_t<960>(p, st);
+        case 1024: return back_t<1024>(p, st);
         case 2048: return back_t<2048>(p, st);
         case 4096: return back_t<4096>(p, st);
         case 7680: return back_t<7680>(p, st);

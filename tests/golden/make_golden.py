@@ -8,7 +8,8 @@ oracle/build.sh compiles from the reference's src/stft.h and src/vr_dsp.h):
 
 What it stores:
   * primitives computed by the reference itself (st::FFT, st::VRFFT, st::torch_stft/istft,
-    st::htdemucs_spec/ispec, st::resample_planar) on small seeded inputs;
+    st::htdemucs_spec/ispec, st::resample_planar, st::vr_stft/vr_istft/vr_resample) on small
+    seeded inputs;
   * whole separations (RoFormer, HTDemucs, TFC-TDF host loops as restated in oracle.c, with
     the network replaced by a seeded mask) whose DSP primitives are the reference's own.
 Inputs are regenerated from their seeds by the tests; a checksum of each input is stored so
@@ -27,7 +28,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(HERE))
 
 import oracle  # noqa: E402
-from golden_cases import CASES, RESAMPLE_RATES, inputs_for  # noqa: E402
+from golden_cases import CASES, RESAMPLE_RATES, VR_RESAMPLES, VR_STFTS, inputs_for  # noqa: E402
 
 
 def main():
@@ -61,6 +62,16 @@ def main():
     out["io_resample_in"] = io
     for src, dst in RESAMPLE_RATES:
         out[f"io_resample_{src}_{dst}"] = oracle.resample_planar(io, src, dst, impl=R)
+    # -- VR primitives, straight from the reference (src/vr_dsp.h) --------------------------
+    vw = np.random.default_rng(78).uniform(-0.5, 0.5, (2, 2000)).astype(np.float32)
+    out["vr_wave_in"] = vw
+    for nfft, hop in VR_STFTS:
+        spec = oracle.vr_stft(vw, nfft, hop, impl=R)
+        out[f"vr_stft_{nfft}_{hop}"] = spec
+        out[f"vr_istft_{nfft}_{hop}"] = oracle.vr_istft(spec, nfft, hop, impl=R)
+    for src, dst in VR_RESAMPLES:
+        out[f"vr_fir_{src}_{dst}"] = oracle.vr_fir(src, dst)
+        out[f"vr_resample_{src}_{dst}"] = oracle.vr_resample(vw, src, dst, out[f"vr_fir_{src}_{dst}"], impl=R)
     # -- whole separations with the reference's primitives ----------------------------------
     assert oracle.use_reference(True)
     for name, case in CASES.items():

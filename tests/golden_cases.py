@@ -63,6 +63,10 @@ def _tfc(dim_t, chunking, overlap, length, compensate, complement):
 # (source rate, destination rate) pairs of the resampler's golden vectors
 RESAMPLE_RATES = [(48000, 44100), (44100, 48000), (22050, 44100), (44100, 32000), (8000, 44100)]
 
+# VR primitives' golden vectors: (n_fft, hop) of vr_stft / vr_istft and resampler rate pairs
+VR_STFTS = [(320, 80), (640, 160), (960, 480), (512, 128), (2048, 1024)]
+VR_RESAMPLES = [(44100, 22050), (22050, 44100), (44100, 7350), (7350, 44100)]
+
 CASES = {
     "rf_mel": _rf("mel", 441 * 20, 4, 441 * 45 + 7, 0, 0),
     "rf_bs": _rf("bs", 441 * 20, 2, 441 * 33 + 100, 1, 1),

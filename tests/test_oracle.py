@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 
 from common import synth_audio
-from golden_cases import CASES, RESAMPLE_RATES, inputs_for
+from golden_cases import CASES, RESAMPLE_RATES, VR_RESAMPLES, VR_STFTS, inputs_for
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
@@ -119,6 +119,67 @@ def test_resampler_passes_a_low_tone(oracle_mod):
     y = oracle_mod.resample_planar(x, 48000, 44100)[0]
     want = np.sin(2 * np.pi * 440 * np.arange(y.size) / 44100)
     assert y.size == 44100 and np.abs(y[200:-200] - want[200:-200]).max() < 1e-3
+
+
+# ---- VR (src/vr_dsp.h) ----------------------------------------------------------------------
+@pytest.mark.parametrize("n", [320, 512, 640, 960, 2048])
+def test_vr_stft_round_trip(oracle_mod, n):                     # vr_dsp_test.cpp:17-24
+    samples = 3 * n
+    k = np.arange(2 * samples)
+    wave = (0.2 * np.sin(0.017 * k)).astype(np.float32).reshape(2, samples)
+    spec = oracle_mod.vr_stft(wave, n, n // 2)
+    back = oracle_mod.vr_istft(spec, n, n // 2)
+    assert back.shape == wave.shape and np.abs(back - wave).max() < 1e-6
+
+
+def test_vr_band_filter_edges(oracle_mod):                       # vr_dsp_test.cpp:26-27
+    L = oracle_mod.lib()
+    assert L.or_vr_lowpass(24, 25, 53) == 1 and L.or_vr_lowpass(52, 25, 53) == 0
+    assert L.or_vr_highpass(85, 130, 85) == 0 and L.or_vr_highpass(86, 130, 85) == 0
+    assert L.or_vr_highpass(131, 130, 85) == 1
+
+
+def test_vr_polyphase_alignment(oracle_mod):                     # vr_dsp_test.cpp:28-33
+    x = np.array([[0, 1, 0, 0], [0, 1, 0, 0]], np.float32)
+    y = oracle_mod.vr_resample(x, 1, 2, np.array([0.5, 1, 0.5], np.float32))
+    assert y.shape == (2, 8)
+    assert np.array_equal(y.reshape(-1), np.array([0, .5, 1, .5, 0, 0, 0, 0, 0, .5, 1, .5, 0, 0, 0, 0], np.float32))
+
+
+@pytest.mark.parametrize("nfft,hop", VR_STFTS)
+def test_vr_primitives_match_golden(oracle_mod, golden, nfft, hop):
+    spec = oracle_mod.vr_stft(golden["vr_wave_in"], nfft, hop)
+    assert np.array_equal(spec, golden[f"vr_stft_{nfft}_{hop}"])
+    assert np.array_equal(oracle_mod.vr_istft(spec, nfft, hop), golden[f"vr_istft_{nfft}_{hop}"])
+
+
+@pytest.mark.parametrize("src,dst", VR_RESAMPLES)
+def test_vr_resampler_matches_golden(oracle_mod, golden, src, dst):
+    got = oracle_mod.vr_resample(golden["vr_wave_in"], src, dst, golden[f"vr_fir_{src}_{dst}"])
+    assert np.array_equal(got, golden[f"vr_resample_{src}_{dst}"])
+
+
+def test_vr_primitives_bit_exact_vs_reference(oracle_mod):
+    R = oracle_mod.ref_lib()
+    if R is None:
+        pytest.skip("reference not compiled on this machine")
+    w = np.random.default_rng(4).uniform(-1, 1, (2, 7001)).astype(np.float32)
+    for nfft, hop in [(640, 80), (1024, 256), (960, 320)]:
+        s = oracle_mod.vr_stft(w, nfft, hop)
+        assert np.array_equal(s, oracle_mod.vr_stft(w, nfft, hop, impl=R))
+        assert np.array_equal(oracle_mod.vr_istft(s, nfft, hop), oracle_mod.vr_istft(s, nfft, hop, impl=R))
+    h = oracle_mod.vr_fir(14700, 44100)
+    assert np.array_equal(oracle_mod.vr_resample(w, 14700, 44100, h), oracle_mod.vr_resample(w, 14700, 44100, h, impl=R))
+
+
+def test_vr_separation_of_silence_is_silence(oracle_mod):
+    """A zero peak returns zeros (src/vr.cpp:361)."""
+    p = oracle_mod.vr_params([dict(sr=44100, hop=512, nfft=1024, start=0, stop=480)], bins=480, pre_start=0,
+                             pre_stop=1)
+    n = 20000
+    T = oracle_mod.vr_n_frames(p, n)
+    y = oracle_mod.vr_separate(p, np.zeros((2, n), np.float32), np.full((2, 481, T), 0.5, np.float32))
+    assert not y.any()
 
 
 # ---- random shifts (src/htdemucs.cpp:610-626, src/roformer.cpp:456-478) ----------------------
