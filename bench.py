@@ -51,6 +51,13 @@ WORKLOADS = {
                  desc="MDX TFC-TDF (Kim_Vocal_2) framing, 180 s stereo, n_fft 7680, UVR 50% overlap"),
     "cfg4": dict(arch="htdemucs", seconds=240, segment=343980, sources=4, sigma=1.0, seed=4, tracks=64,
                  desc="batch of 64 tracks of 240 s through the HTDemucs spectral path, round-robin over GPUs"),
+    # VR (src/vr.cpp): no BASELINE config; a three-band layout of the reference's kind (bands at
+    # 7.35 / 14.7 / 44.1 kHz, n_fft 320 / 512 / 960, equal frame durations), 180 s
+    "vr3band": dict(arch="vr", seconds=180, seed=10, bins=608, pre=(500, 600), bands=[
+        dict(sr=7350, hop=80, nfft=320, start=0, stop=100, lp_start=80, lp_stop=100),
+        dict(sr=14700, hop=160, nfft=512, start=50, stop=200, hp_start=60, hp_stop=50, lp_start=180, lp_stop=200),
+        dict(sr=44100, hop=480, nfft=960, start=150, stop=481, hp_start=170, hp_stop=150)],
+        desc="VR spectral path, 3 bands (7.35/14.7/44.1 kHz, n_fft 320/512/960), 180 s stereo, 2 stems"),
     # the request-side conversions around separate() (src/libstems.cpp:160-199): not a
     # BASELINE config; measured so the row that feeds the path has its own number
     "io48k": dict(arch="io", seconds=180, rate=48000, stems=4, seed=9,
@@ -213,11 +220,12 @@ def cpu_run(w, length, mix, mask_host, n_sample, threads):
 def run_reference(args, w, rank):
     if rank != 0:
         return 0
-    if w["arch"] == "io":
+    if w["arch"] in ("io", "vr"):
         sample_s = 5.0
         times, kind = [], "port"
+        fn = cpu_io if w["arch"] == "io" else cpu_vr
         for k in range(args.warmup + args.steps):
-            dt, kind = cpu_io(w, sample_s)
+            dt, kind = fn(w, sample_s)
             if k >= args.warmup:
                 times.append(dt)
         value = sample_s / statistics.mean(times)
@@ -376,6 +384,114 @@ def run_ours_io(args, w, rank, world, local_rank):
         "e2e": {"value": audio_s / (e2e_ms / 1e3), "unit": "audio-s/s",
                 "h2d_bytes_per_step": 4 * (2 * n + rows * m), "d2h_bytes_per_step": 4 * rows * n},
         "gpu_launches": 2 * args.steps,
+    }
+
+
+def _vr_setup(w):
+    import oracle
+    p = oracle.vr_params(w["bands"], bins=w["bins"], pre_start=w["pre"][0], pre_stop=w["pre"][1])
+    rates = sorted({x["sr"] for x in w["bands"]})
+    firs = {(s, d): oracle.vr_fir(s, d) for s in rates for d in rates if s != d}
+    bands = [dict(sample_rate=x["sr"], hop=x["hop"], n_fft=x["nfft"], crop_start=x["start"], crop_stop=x["stop"],
+                  hpf_start=x.get("hp_start", -1), hpf_stop=x.get("hp_stop", -1), lpf_start=x.get("lp_start", -1),
+                  lpf_stop=x.get("lp_stop", -1)) for x in w["bands"]]
+    return p, firs, bands
+
+
+def cpu_vr(w, seconds):
+    """The VR path restated in C (oracle, one thread, as the reference runs it) on a sample."""
+    import oracle
+    p, _, _ = _vr_setup(w)
+    n = int(seconds * SR)
+    T = oracle.vr_n_frames(p, n)
+    mask = np.random.default_rng(11).uniform(0, 1, (2, w["bins"] + 1, T)).astype(np.float32)
+    mix = synth_audio(w["seed"], n)
+    t0 = time.perf_counter()
+    oracle.vr_separate(p, mix, mask)
+    return time.perf_counter() - t0, "port"
+
+
+def run_ours_vr(args, w, rank, world, local_rank):
+    import torch
+    pkg = load_pkg()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    eng = pkg.Engine(local_rank)
+    _, firs, bands = _vr_setup(w)
+    n = w["seconds"] * SR
+    plan = eng.plan_vr(n, bands, firs, bins=w["bins"], pre_filter_start=w["pre"][0], pre_filter_stop=w["pre"][1])
+    mix_h = synth_audio(w["seed"] + 7 * rank, n)
+    d_mix = torch.from_numpy(mix_h).to(dev)
+    d_mask = torch.rand(plan.mask_shape, device=dev, generator=torch.Generator(device=dev).manual_seed(12))
+    d_out = torch.empty(plan.out_shape, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        plan.separate(d_mix, d_mask, d_out, stream=stream)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local_rank])
+
+    def timed(fn, k):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clk:
+            e0.record(stream)
+            for _ in range(k):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        return e0.elapsed_time(e1) / k, clk
+
+    ms, clk = timed(step, args.steps)
+    remeasured = False
+    if clk.rejected():
+        ms, clk = timed(step, args.steps)
+        remeasured = True
+    ms = pkg.sharding.max_over_ranks(ms, device=dev)
+    h_mix = torch.from_numpy(mix_h).pin_memory()
+    h_mask = d_mask.cpu().pin_memory()
+    h_out = torch.empty(plan.out_shape).pin_memory()
+
+    def e2e_step():
+        d_mix.copy_(h_mix, non_blocking=True)
+        d_mask.copy_(h_mask, non_blocking=True)
+        step()
+        h_out.copy_(d_out, non_blocking=True)
+    e2e_ms, _ = timed(e2e_step, max(1, min(args.steps, 10)))
+    e2e_ms = pkg.sharding.max_over_ranks(e2e_ms, device=dev)
+    mask_b = 4 * d_mask.numel()
+    bytes_step = 4 * 2 * n + mask_b + 4 * 4 * n
+    peak, peak_kind = measured_peak()
+    achieved = bytes_step / (ms / 1e3) / 1e9
+    # front: resamples between the B distinct rates, B STFTs, the assembly; each stem: B band
+    # parts, B iSTFT back + combine, B - 1 sums, B - 1 resamples, the crop
+    launches = 2 * len(bands) + 2 * (5 * len(bands) - 1)
+    plan.close()
+    eng.close()
+    if rank != 0:
+        return None
+    return {
+        "metric": "audio_seconds_per_second", "value": w["seconds"] * world / (ms / 1e3), "unit": "audio-s/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded sines + noise; U(0, 1) masks standing in for the network)",
+        "config": {"workload": args.workload, "desc": w["desc"], "frames": plan.n_frames,
+                   "mask_bytes_per_track": mask_b, "l2": "inputs larger than L2 (no flush needed)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "kernel": "the VR path (all its kernels)", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                     "algorithmic_bytes_per_step": bytes_step},
+        "clocks": dict(clk.summary(), remeasured=remeasured),
+        "e2e": {"value": w["seconds"] * world / (e2e_ms / 1e3), "unit": "audio-s/s",
+                "h2d_bytes_per_step": 4 * 2 * n + mask_b, "d2h_bytes_per_step": 4 * 4 * n},
+        "gpu_launches": launches * args.steps,
     }
 
 
@@ -543,16 +659,16 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = (run_ours_io if w["arch"] == "io" else run_ours)(args, w, rank, world, local_rank)
+        line = {"io": run_ours_io, "vr": run_ours_vr}.get(w["arch"], run_ours)(args, w, rank, world, local_rank)
     finally:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
             dist.destroy_process_group()
-    if rank == 0 and w["arch"] == "io":
+    if rank == 0 and w["arch"] in ("io", "vr"):
         if world == 1 and not args.no_cpu_baseline:
-            dt, kind = cpu_io(w, 5.0)
+            dt, kind = (cpu_io if w["arch"] == "io" else cpu_vr)(w, 5.0)
             line["cpu_baseline"] = {"value": 5.0 / dt, "unit": "audio-s/s", "cores": 1, "kind": kind,
-                                    "sample": f"5 s of the {w['seconds']} s request (one thread, as libstems runs it)"}
+                                    "sample": f"5 s of the {w['seconds']} s input (one thread, as the reference runs it)"}
         print(json.dumps(line))
         return 0
     if rank == 0:
