@@ -106,7 +106,8 @@ STG_API stg_status stg_plan_get_info(const stg_plan* p, stg_plan_info* info) {
     info->mask_floats_per_chunk = H.mask_per_chunk;
     info->out_floats = H.out_floats();
     info->scratch_bytes = (int64_t)(p->d_y.bytes + p->d_tr.bytes + p->d_mixn.bytes + p->d_mono.bytes +
-                                    p->d_cac_part.bytes + p->d_cac_stats.bytes + p->d_mask_t.bytes);
+                                    p->d_cac_part.bytes + p->d_cac_stats.bytes + p->d_mask_t.bytes +
+                                    p->d_zspec.bytes);
     return STG_OK;
 }
 

@@ -101,6 +101,7 @@ struct stg_plan {
     DevBuf d_y, d_tr;
     DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
     DevBuf d_mask_t;                                  // t-major masks (HTDemucs, TFC-TDF)
+    DevBuf d_zspec;                                   // HTDemucs spectra
     const float* mono_src = nullptr;                  // the track d_mixn was normalised from
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
@@ -129,6 +130,10 @@ struct stg_plan {
             d_mono.reserve(H.mono_bytes(), "mono statistics");
             D.mixn = d_mixn.as<float>();
             D.mono = reinterpret_cast<double*>(d_mono.p);
+        }
+        if (H.z_per_chunk()) {
+            d_zspec.reserve(H.z_bytes(), "segment spectra");
+            D.zspec = reinterpret_cast<float4*>(d_zspec.p);
         }
         if (H.mask_planes) {
             d_mask_t.reserve(H.mask_t_bytes(), "t-major masks");

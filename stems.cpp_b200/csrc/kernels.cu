@@ -6,13 +6,15 @@
 //      real channels as one complex frame L + iR;
 //   2. forward FFT in shared memory (fft.cuh);
 //   3. split the two channels' spectra, apply the architecture's spectral op (the stand-in
-//      for the network: complex mask, band-averaged mask, or CaC real mask), drop what the
-//      reference's c2r drops, and repack the two masked spectra as one Hermitian pair;
+//      for the network: RoFormer's band-averaged mask or TFC-TDF's CaC real mask), drop what
+//      the reference's c2r drops, and repack the two masked spectra as one Hermitian pair;
 //   4. inverse FFT, window, and overlap-add into a ring buffer of n_fft samples per channel;
 //   5. flush the hop of samples that no later frame of the tile touches, scaled by the
 //      inverse window-sum envelope, to the chunk output Y. The last frame of a tile sends
 //      its n_fft - hop trailing samples to Tr instead; the combine adds them to the next
 //      tile's leading samples, so every sum is formed in a fixed order (no atomics).
+// (HTDemucs, whose four or six stems share one spectrum, runs the front kernel once per frame
+// and the back kernel per stem instead: split.cu, FRONT_ZSPEC / BACK_ZMASK.)
 // Combine kernel: one thread per output sample; it sums the chunks that cover the sample
 // with their crossfade weights (reading Y and the tile-boundary partials Tr), divides by the
 // summed weight, and applies the architecture's epilogue (nan_to_num, compensation,
@@ -74,11 +76,11 @@ template <int ARCH, int N, int T> struct MaskOp {
                 }
             }
         } else {
-            // HTDemucs ox planes [S][2C][F][T] (src/htdemucs.cpp:463-469) and TFC-TDF y planes
-            // [4S][dim_f][T] (src/tfc_tdf.cpp:370-387), rewritten t-major by mask_transpose:
-            // [S][T][F] float4 (L re, L im, R re, R im), so frame t's bins are contiguous.
-            const int F = ARCH == ARCH_HTDEMUCS ? N / 2 : p.dim_f;
-            const int f_lo = ARCH == ARCH_HTDEMUCS ? 0 : p.zero_bins;
+            // TFC-TDF y planes [4S][dim_f][T] (src/tfc_tdf.cpp:370-387), rewritten t-major by
+            // mask_transpose: [S][T][dim_f] float4 (L re, L im, R re, R im), so frame t's bins
+            // are contiguous.
+            const int F = p.dim_f;
+            const int f_lo = p.zero_bins;
             const float* ms = m + ((int64_t)s * p.g.T + t) * F * 4;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
@@ -112,25 +114,6 @@ template <int ARCH, int N, int T> struct MaskOp {
             yl = cmul(zl, cscale(al, w));
             yr = cmul(zr, cscale(ar, w));
             if (p.zero_dc && f == 0) { yl = make_float2(0.f, 0.f); yr = yl; }      // :278
-        } else if constexpr (ARCH == ARCH_HTDEMUCS) {
-            // network output ox = Z * M; the Nyquist bin is dropped (src/stft.h:126). With the
-            // CaC normalisation the stand-in sees (Z - mean) / (1e-5 + std) and its output is
-            // mapped back by ox * std + mean on both parts (src/htdemucs.cpp:434-436, 469).
-            if (p.cac_stats) {
-                const double2 st = p.cac_stats[ci];
-                const float mean = (float)st.x, sd = (float)st.y, inv = (float)(1.0 / (1e-5 + st.y));
-                zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
-                zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
-                yl = cmul(zl, make_float2(a[i].x, a[i].y));
-                yr = cmul(zr, make_float2(a[i].z, a[i].w));
-                yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
-                yr = p.n_channels == 2 ? make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean))
-                                       : make_float2(0.f, 0.f);
-            } else {
-                yl = cmul(zl, make_float2(a[i].x, a[i].y));
-                yr = cmul(zr, make_float2(a[i].z, a[i].w));
-            }
-            if (f >= N / 2) { yl = make_float2(0.f, 0.f); yr = yl; }
         } else {
             // y = in * mask per CaC plane; zero below zero_bins and from dim_f up (the loads
             // left a[i] at zero there)
@@ -451,9 +434,6 @@ int fused_resident_ctas(int arch, int n) {
             if (n == 2048) return resident_t<ARCH_ROFORMER, 2048>();
             if (n == 4096) return resident_t<ARCH_ROFORMER, 4096>();
             break;
-        case ARCH_HTDEMUCS:
-            if (n == 4096) return resident_t<ARCH_HTDEMUCS, 4096>();
-            break;
         case ARCH_TFC:
             if (n == 7680) return resident_t<ARCH_TFC, 7680>();
             if (n == 4096) return resident_t<ARCH_TFC, 4096>();
@@ -499,9 +479,6 @@ cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st) {
         case ARCH_ROFORMER:
             if (p.g.n_fft == 2048) return launch_fused_t<ARCH_ROFORMER, 2048>(p, st);
             if (p.g.n_fft == 4096) return launch_fused_t<ARCH_ROFORMER, 4096>(p, st);
-            break;
-        case ARCH_HTDEMUCS:
-            if (p.g.n_fft == 4096) return launch_fused_t<ARCH_HTDEMUCS, 4096>(p, st);
             break;
         case ARCH_TFC:
             if (p.g.n_fft == 7680) return launch_fused_t<ARCH_TFC, 7680>(p, st);

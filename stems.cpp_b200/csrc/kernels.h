@@ -76,8 +76,8 @@ struct FusedParams {
     const float2* tw;          // the FFT plan's per-pass twiddles (fft.cuh: twiddle_index)
     const float* inv_env;      // [Lout]: 1 / sum of squared windows, 0 where it vanishes
     float fwd_scale, inv_scale;
-    // mask (the stand-in for the network's output), one block per chunk; HTDemucs and TFC-TDF
-    // masks in the t-major layout of launch_mask_transpose
+    // mask (the stand-in for the network's output), one block per chunk; TFC-TDF masks in the
+    // t-major layout of launch_mask_transpose
     const float* mask;
     int64_t mask_chunk_stride;
     // RoFormer: bin -> (band entry) inverse table. bin_tab[f] holds the first two bands holding
@@ -93,8 +93,6 @@ struct FusedParams {
     int64_t stem_stride;       // floats per stem within a chunk's mask block
     // TFC-TDF
     int dim_f, zero_bins;
-    // HTDemucs CaC normalisation: (mean, std) of every chunk's spectrogram, or null
-    const double2* cac_stats;
     // outputs
     float* Y;                  // [chunk][S*C][Lout]
     int64_t y_chunk_stride;
@@ -138,12 +136,15 @@ enum FrontLayout : int {
     FRONT_CAC = 1,       // float planes [2C][F][T]: re = 2c, im = 2c + 1 (HTDemucs input)
     FRONT_BANDS = 2,     // RoFormer band-major features [sum_b din_b * T]
     FRONT_TFC = 3,       // float planes [4][dim_f][T], bins below zero_bins 0 (TFC-TDF input)
-    FRONT_STATS = 4      // no output: (sum, sum of squares) of the CaC values per (chunk, tile)
+    FRONT_STATS = 4,     // no output: (sum, sum of squares) of the CaC values per (chunk, tile)
+    FRONT_ZSPEC = 5      // the spectra t-major, zspec [chunk][T][n_bins] float4 (L re, L im, R re, R im)
 };
 enum BackLayout : int {
     BACK_COMPLEX = 0,    // complex [C][F][T] (torch_istft, htdemucs_ispec)
     BACK_CAC = 1,        // float planes [S][2C][F][T] (HTDemucs output)
-    BACK_TFC = 2         // float planes [4S][dim_f][T] (TFC-TDF output)
+    BACK_TFC = 2,        // float planes [4S][dim_f][T] (TFC-TDF output)
+    BACK_ZMASK = 3       // HTDemucs with the stand-in network: zspec times the t-major masks
+                         // [S][T][n_bins] float4 in net (launch_mask_transpose), CaC-normalised
 };
 
 struct SplitParams {
@@ -168,8 +169,10 @@ struct SplitParams {
     const int2* bin_ent;
     float* net;                // front: written; back: read
     int64_t net_chunk_stride;
-    const double2* cac_stats;  // FRONT_CAC / BACK_CAC: per-chunk (mean, std), or null
-    double2* stats_out;        // FRONT_STATS: [chunk][tile] partial sums
+    const double2* cac_stats;  // FRONT_CAC / BACK_CAC / BACK_ZMASK: per-chunk (mean, std), or null
+    double2* stats_out;        // front: [chunk][tile] partial sums of the CaC values, or null
+    float4* zspec;             // FRONT_ZSPEC: written; BACK_ZMASK: read
+    int64_t z_chunk_stride;    // float4 per chunk
     float* Y;                  // back
     int64_t y_chunk_stride;
     float* Tr;
@@ -194,6 +197,7 @@ int fused_resident_ctas(int arch, int n_fft);
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
 bool split_supported(int n_fft);   // n_fft the front and back kernels take
+int back_resident_ctas(int n_fft); // CTAs of the back kernel resident at once (0 when unknown)
 int split_max_hop(int n_fft);
 
 // convert.cu. Resampling (and layout / channel conversion) of planar or interleaved audio:

@@ -72,7 +72,9 @@ void finish_plan(HostPlan& P, int env_frames) {
     // frames plus about one frame of prologue (the first window) and flush. K is the one in
     // [K_min, 16] with the shortest critical path, the larger on ties. K_min keeps every
     // sample within one tile boundary (K * hop >= n_fft - hop).
-    const int64_t slots = std::max(1, fused_resident_ctas(P.arch, N));
+    // (HTDemucs separations run the back kernel over the chunks, the others the fused one)
+    const int64_t slots = std::max(1, P.arch == ARCH_HTDEMUCS && !P.primitive ? back_resident_ctas(N)
+                                                                              : fused_resident_ctas(P.arch, N));
     const int k_min = std::max(1, (N - hop + hop - 1) / hop);
     P.K = std::max(16, k_min);
     int64_t best = INT64_MAX;
@@ -540,7 +542,26 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     const float* d_mix = normalise_mix(P, D, d_mix_in, st);
     if (timing && P.mono_norm) timing->launches += 5;
     const int G = (int)P.chunks.size();
-    if (P.cac_norm) {
+    const bool zpath = P.z_per_chunk() > 0;   // HTDemucs: spectra once, then the back kernel per stem
+    if (zpath) {
+        if (!D.zspec || !D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the segment spectra");
+        SplitParams z = split_params(P, D, d_mix, 0, G);
+        z.layout = FRONT_ZSPEC;
+        z.n_bins = P.front_bins;
+        z.zspec = D.zspec;
+        z.z_chunk_stride = P.z_per_chunk();
+        if (P.cac_norm) {
+            if (!D.cac_part || !D.cac_stats) fail(STG_INTERNAL_ERROR, "no scratch for the CaC normalisation");
+            z.stats_out = D.cac_part;
+        }
+        cuda_check(stg::launch_front(z, st), "segment spectra launch");
+        if (timing) timing->launches++;
+        if (P.cac_norm) {
+            const double count = 2.0 * P.C * P.front_bins * P.g.T;
+            cuda_check(launch_cac_finish(D.cac_part, G, P.n_tiles, count, D.cac_stats, st), "CaC statistics launch");
+            if (timing) timing->launches++;
+        }
+    } else if (P.cac_norm) {
         const int k = cac_statistics(P, D, d_mix, 0, G, st);
         if (timing) timing->launches += k;
     }
@@ -565,7 +586,6 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
         f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
         f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
-        f.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
         if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
             if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
             cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins, P.g.T,
@@ -576,7 +596,19 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
         }
         if (timed && b0 == 0) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
-        cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+        if (zpath) {   // every stem's ox = Z * M (CaC-normalised), iSTFT and overlap-add
+            SplitParams b = split_params(P, D, d_mix, b0, nb);
+            b.layout = BACK_ZMASK;
+            b.n_bins = P.back_bins;
+            b.net = const_cast<float*>(f.mask);
+            b.net_chunk_stride = f.mask_chunk_stride;
+            b.zspec = D.zspec + (int64_t)b0 * P.z_per_chunk();
+            b.z_chunk_stride = P.z_per_chunk();
+            b.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
+            cuda_check(stg::launch_back(b, st), "back kernel launch");
+        } else {
+            cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+        }
         if (timing) timing->launches++;
         if (opt && opt->on_progress) {
             cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");

@@ -74,6 +74,9 @@ struct HostPlan {
     size_t cac_part_bytes() const { return cac_norm ? sizeof(double2) * (size_t)n_tiles * chunks.size() : 0; }
     size_t cac_stats_bytes() const { return cac_norm ? sizeof(double2) * chunks.size() : 0; }
     int64_t mask_t_per_chunk() const { return mask_planes ? (int64_t)S * g.T * mask_bins : 0; }   // float4
+    // HTDemucs: each segment's spectra once, t-major (FRONT_ZSPEC), for the back kernel
+    int64_t z_per_chunk() const { return arch == ARCH_HTDEMUCS && !primitive ? (int64_t)g.T * (g.n_fft / 2) : 0; }
+    size_t z_bytes() const { return sizeof(float4) * (size_t)z_per_chunk() * chunks.size(); }
     size_t mask_t_bytes() const { return sizeof(float4) * (size_t)mask_t_per_chunk() * chunks.size(); }
 };
 
@@ -96,6 +99,7 @@ struct PlanDevice {
     double2* cac_part = nullptr;   // scratch: CaC partial sums (HostPlan::cac_norm)
     double2* cac_stats = nullptr;  // scratch: per-chunk CaC (mean, std)
     float4* mask_t = nullptr;      // scratch: t-major masks (HostPlan::mask_planes)
+    float4* zspec = nullptr;       // scratch: HTDemucs spectra (HostPlan::z_per_chunk)
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);

@@ -51,6 +51,10 @@ __device__ __forceinline__ void front_store(const SplitParams& p, const int2* bt
                 }
             }
             break;
+        case FRONT_ZSPEC:
+            if (f < p.n_bins)
+                p.zspec[(int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins + f] = make_float4(zl.x, zl.y, zr.x, zr.y);
+            break;
         case FRONT_TFC:
             if (f < p.n_bins) {
                 const bool z = f < p.zero_bins;
@@ -109,6 +113,26 @@ __device__ __forceinline__ void back_load(const SplitParams& p, int ci, int s, i
                 yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
                 yr = make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean));
                 if (C == 1) yr = make_float2(0.f, 0.f);
+            }
+            break;
+        }
+        case BACK_ZMASK: {
+            // ox = Z * M, with the CaC normalisation around it (src/htdemucs.cpp:434-436, 469)
+            float4 z = p.zspec[(int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins + f];
+            const float4 m = ld_stream4(in + 4 * (((int64_t)s * T + t) * p.n_bins + f));
+            float2 zl = make_float2(z.x, z.y), zr = make_float2(z.z, z.w);
+            if (p.cac_stats) {
+                const double2 st = p.cac_stats[ci];
+                const float mean = (float)st.x, sd = (float)st.y, inv = (float)(1.0 / (1e-5 + st.y));
+                zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
+                zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
+                yl = cmul(zl, make_float2(m.x, m.y));
+                yr = cmul(zr, make_float2(m.z, m.w));
+                yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
+                yr = C > 1 ? make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean)) : make_float2(0.f, 0.f);
+            } else {
+                yl = cmul(zl, make_float2(m.x, m.y));
+                yr = cmul(zr, make_float2(m.z, m.w));
             }
             break;
         }
@@ -190,20 +214,19 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
                 const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
                 const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
                 const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
-                if (p.layout == FRONT_STATS) {
+                if (p.stats_out && f < p.n_bins) {
                     acc_s += (double)zl.x + (double)zl.y;
                     acc_q += (double)zl.x * zl.x + (double)zl.y * zl.y;
                     if (C > 1) {
                         acc_s += (double)zr.x + (double)zr.y;
                         acc_q += (double)zr.x * zr.x + (double)zr.y * zr.y;
                     }
-                } else {
-                    front_store<N>(p, btab, ci, t, f, zl, zr);
                 }
+                if (p.layout != FRONT_STATS) front_store<N>(p, btab, ci, t, f, zl, zr);
             }
             __syncthreads();
         }
-        if (p.layout == FRONT_STATS) {   // block sums in a fixed order, one partial per item
+        if (p.stats_out) {   // block sums in a fixed order, one partial per item
             for (int o = 16; o > 0; o >>= 1) {
                 acc_s += __shfl_down_sync(0xffffffffu, acc_s, o);
                 acc_q += __shfl_down_sync(0xffffffffu, acc_q, o);
@@ -325,6 +348,24 @@ bool split_supported(int n) {
 }
 
 int split_max_hop(int n) { return split_supported(n) ? n / 2 : 0; }
+
+int back_resident_ctas(int n) {
+    int per_sm = 0, n_sm = 0, dev = 0;
+    auto query = [&](auto kernel, int threads, size_t smem) {
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return per_sm * n_sm;
+    };
+    switch (n) {
+        case 4096: return query(back_kernel<4096>, FftCfg<4096>::T, sizeof(float2) * ((size_t)padded_size(4096) + 4096));
+    }
+    return 0;
+}
 
 cudaError_t launch_front(const SplitParams& p, cudaStream_t st) {
     if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
