@@ -330,6 +330,34 @@ STG_API stg_status stg_vr_back(stg_vr_plan* plan, const float* d_mask, float* d_
 STG_API stg_status stg_separate_vr(stg_vr_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream);
 
+/* ---- model configurations from GGUF files ----------------------------------------------- */
+
+/* A model file's metadata, read without ggml and without its weights: what the separators'
+ * constructors read (src/htdemucs.cpp:478-500, src/roformer.cpp:360-412,
+ * src/tfc_tdf.cpp:498-553, src/vr.cpp:296-327) and VR's resampling FIRs. Host only; needs
+ * no GPU. `message` (optional) receives the reason for a failure: STG_IO_ERROR when the file
+ * cannot be opened, STG_MODEL_ERROR for a file that is not GGUF or lacks a key. */
+typedef struct stg_model stg_model;
+STG_API stg_status stg_model_open(const char* gguf_path, stg_model** out_model, char* message,
+                                  size_t message_size);
+STG_API void stg_model_close(stg_model* model);
+/* general.architecture: "htdemucs", "mel_band_roformer", "bs_roformer", "tfc_tdf" or
+ * "vr_cascaded". Borrowed until stg_model_close. */
+STG_API const char* stg_model_architecture(const stg_model* model);
+/* stems.samplerate, or 0 when absent. */
+STG_API int32_t stg_model_sample_rate(const stg_model* model);
+/* The configuration of the model's architecture, with the reference's defaults for the run
+ * options (overlap < 0, no shifts, HTDemucs' normalisations on); set config->size first.
+ * Arrays the configs point to (band tables, VR bands and FIRs) belong to the model. */
+STG_API stg_status stg_model_htdemucs_config(const stg_model* model, stg_htdemucs_config* config,
+                                             char* message, size_t message_size);
+STG_API stg_status stg_model_roformer_config(const stg_model* model, stg_roformer_config* config,
+                                             char* message, size_t message_size);
+STG_API stg_status stg_model_tfc_config(const stg_model* model, stg_tfc_config* config, char* message,
+                                        size_t message_size);
+STG_API stg_status stg_model_vr_config(const stg_model* model, stg_vr_config* config, char* message,
+                                       size_t message_size);
+
 /* ---- the DSP primitives of src/stft.h on the device -------------------------------------- */
 
 /* torch.stft (src/stft.h:146-164) of each channel: periodic Hann, centre reflect pad,

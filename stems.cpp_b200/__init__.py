@@ -141,6 +141,14 @@ _SIGNATURES = {
     "stg_vr_front": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_vr_back": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_vr": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_model_open": (C.c_int32, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
+    "stg_model_close": (None, [C.c_void_p]),
+    "stg_model_architecture": (C.c_char_p, [C.c_void_p]),
+    "stg_model_sample_rate": (C.c_int32, [C.c_void_p]),
+    "stg_model_htdemucs_config": (C.c_int32, [C.c_void_p, C.POINTER(HTDemucsConfig), C.c_char_p, C.c_size_t]),
+    "stg_model_roformer_config": (C.c_int32, [C.c_void_p, C.POINTER(RoFormerConfig), C.c_char_p, C.c_size_t]),
+    "stg_model_tfc_config": (C.c_int32, [C.c_void_p, C.POINTER(TFCConfig), C.c_char_p, C.c_size_t]),
+    "stg_model_vr_config": (C.c_int32, [C.c_void_p, C.POINTER(VrConfig), C.c_char_p, C.c_size_t]),
     "stg_torch_stft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int64,
                                    C.c_void_p, C.c_void_p]),
     "stg_torch_istft": (C.c_int32, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_int32,
@@ -288,6 +296,24 @@ class Engine:
         h = C.c_void_p()
         self._check(lib().stg_plan_vr(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_vr")
         return VrPlan(self, h, n_samples, bins)
+
+    def plan_from_model(self, model: "Model", n_samples, **run):
+        """A plan for a GGUF model (Model): the configuration its metadata gives, with the
+        run options (overlap, shifts, seed; HTDemucs' mono_norm / cac_norm) overriding the
+        reference's defaults. VR models give a VrPlan."""
+        cfg = model.config()
+        for k, v in run.items():
+            if not hasattr(cfg, k):
+                raise StemsError(1, f"{model.architecture} has no option {k}")
+            setattr(cfg, k, v)
+        h = C.c_void_p()
+        if model.architecture == "vr_cascaded":
+            self._check(lib().stg_plan_vr(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_vr")
+            return VrPlan(self, h, n_samples, cfg.bins)
+        fn = {"htdemucs": lib().stg_plan_htdemucs, "tfc_tdf": lib().stg_plan_tfc}.get(model.architecture,
+                                                                                    lib().stg_plan_roformer)
+        self._check(fn(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_from_model")
+        return Plan(self, h)
 
     # -- the request's audio in and the stems out (src/libstems.cpp:160-199) -----------------
     def prepare_input(self, samples, n_channels, sample_rate, interleaved=True, model_channels=2,
@@ -520,6 +546,52 @@ class VrPlan:
     def close(self):
         if self._h:
             lib().stg_vr_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Model:
+    """A model's spectral-path configuration read from its GGUF file (stg_model_open): no
+    weights are read and no GPU is needed."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        msg = C.create_string_buffer(512)
+        rc = lib().stg_model_open(os.fsencode(path), C.byref(h), msg, 512)
+        if rc != 0:
+            raise StemsError(rc, msg.value.decode(errors="replace"))
+        self._h = h
+        self.architecture = lib().stg_model_architecture(h).decode()
+        self.sample_rate = lib().stg_model_sample_rate(h)
+
+    def config(self):
+        """The architecture's configuration struct (HTDemucsConfig, RoFormerConfig, TFCConfig
+        or VrConfig); its arrays belong to this Model."""
+        kinds = {"htdemucs": (HTDemucsConfig, lib().stg_model_htdemucs_config),
+                 "mel_band_roformer": (RoFormerConfig, lib().stg_model_roformer_config),
+                 "bs_roformer": (RoFormerConfig, lib().stg_model_roformer_config),
+                 "tfc_tdf": (TFCConfig, lib().stg_model_tfc_config),
+                 "vr_cascaded": (VrConfig, lib().stg_model_vr_config)}
+        if self.architecture not in kinds:
+            raise StemsError(4, f"unknown architecture {self.architecture!r}")
+        T, fn = kinds[self.architecture]
+        cfg = T()
+        cfg.size = C.sizeof(T)
+        msg = C.create_string_buffer(512)
+        rc = fn(self._h, C.byref(cfg), msg, 512)
+        if rc != 0:
+            raise StemsError(rc, msg.value.decode(errors="replace"))
+        cfg._model = self
+        return cfg
+
+    def close(self):
+        if self._h:
+            lib().stg_model_close(self._h)
             self._h = None
 
     def __del__(self):
