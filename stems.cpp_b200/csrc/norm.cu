@@ -50,13 +50,20 @@ __global__ void __launch_bounds__(kThreads) mono_partials(const float* __restric
     if (threadIdx.x == 0) partial[blockIdx.x] = s;
 }
 
-// Sums the partials in block order: pass 0 writes the mean, pass 1 the std (at least 1e-8).
-__global__ void mono_finish(const double* __restrict__ partial, int n, int64_t len, int pass, double* stats) {
+// Sums the kBlocks partials by a fixed tree (one block of kBlocks threads): pass 0 writes the
+// mean, pass 1 the std (at least 1e-8).
+__global__ void __launch_bounds__(kBlocks) mono_finish(const double* __restrict__ partial, int64_t len, int pass,
+                                                       double* stats) {
+    __shared__ double s[kBlocks];
+    s[threadIdx.x] = partial[threadIdx.x];
+    __syncthreads();
+    for (int o = kBlocks / 2; o > 0; o >>= 1) {
+        if ((int)threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o];
+        __syncthreads();
+    }
     if (threadIdx.x != 0) return;
-    double s = 0.0;
-    for (int b = 0; b < n; b++) s += partial[b];
-    if (pass == 0) stats[0] = s / (double)len;
-    else stats[1] = fmax(sqrt(s / (double)(len - 1)), 1e-8);
+    if (pass == 0) stats[0] = s[0] / (double)len;
+    else stats[1] = fmax(sqrt(s[0] / (double)(len - 1)), 1e-8);
 }
 
 __global__ void __launch_bounds__(kThreads) mono_apply(const float* __restrict__ mix, int64_t n,
@@ -66,17 +73,23 @@ __global__ void __launch_bounds__(kThreads) mono_apply(const float* __restrict__
         out[i] = (float)(((double)mix[i] - mean) / sd);
 }
 
-// One thread per segment: the partial (sum, sum of squares) of its tiles, in tile order.
-__global__ void cac_finish(const double2* __restrict__ partial, int n_chunks, int n_tiles, double count,
-                           double2* __restrict__ stats) {
-    const int ci = blockIdx.x * blockDim.x + threadIdx.x;
+// One warp per segment: lane l adds tiles l, l + 32, ... in order, then the lanes' sums meet
+// in a fixed shuffle tree.
+__global__ void __launch_bounds__(128) cac_finish(const double2* __restrict__ partial, int n_chunks, int n_tiles,
+                                                  double count, double2* __restrict__ stats) {
+    const int ci = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (ci >= n_chunks) return;
     double s = 0.0, q = 0.0;
-    for (int t = 0; t < n_tiles; t++) {
+    for (int t = lane; t < n_tiles; t += 32) {
         const double2 v = partial[(int64_t)ci * n_tiles + t];
         s += v.x;
         q += v.y;
     }
+    for (int o = 16; o > 0; o >>= 1) {
+        s += __shfl_down_sync(0xffffffffu, s, o);
+        q += __shfl_down_sync(0xffffffffu, q, o);
+    }
+    if (lane != 0) return;
     const double mean = s / count;
     const double var = (q - s * mean) / (count - 1.0);
     stats[ci] = make_double2(mean, sqrt(fmax(var, 0.0)));
@@ -91,7 +104,7 @@ cudaError_t launch_mono_norm(const float* mix, int64_t len, int C, double* scrat
     double* stats = scratch;
     for (int pass = 0; pass < 2; pass++) {
         mono_partials<<<kBlocks, kThreads, 0, st>>>(mix, len, C, pass, stats, partial);
-        mono_finish<<<1, 32, 0, st>>>(partial, kBlocks, len, pass, stats);
+        mono_finish<<<1, kBlocks, 0, st>>>(partial, len, pass, stats);
     }
     mono_apply<<<kBlocks, kThreads, 0, st>>>(mix, (int64_t)C * len, stats, out);
     return cudaGetLastError();
@@ -99,7 +112,7 @@ cudaError_t launch_mono_norm(const float* mix, int64_t len, int C, double* scrat
 
 cudaError_t launch_cac_finish(const double2* partial, int n_chunks, int n_tiles, double count, double2* stats,
                               cudaStream_t st) {
-    cac_finish<<<(n_chunks + 127) / 128, 128, 0, st>>>(partial, n_chunks, n_tiles, count, stats);
+    cac_finish<<<(n_chunks + 3) / 4, 128, 0, st>>>(partial, n_chunks, n_tiles, count, stats);
     return cudaGetLastError();
 }
 

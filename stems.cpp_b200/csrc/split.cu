@@ -116,31 +116,31 @@ __device__ __forceinline__ void back_load(const SplitParams& p, int ci, int s, i
             }
             break;
         }
-        case BACK_ZMASK: {
-            // ox = Z * M, with the CaC normalisation around it (src/htdemucs.cpp:434-436, 469)
-            float4 z = p.zspec[(int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins + f];
-            const float4 m = ld_stream4(in + 4 * (((int64_t)s * T + t) * p.n_bins + f));
-            float2 zl = make_float2(z.x, z.y), zr = make_float2(z.z, z.w);
-            if (p.cac_stats) {
-                const double2 st = p.cac_stats[ci];
-                const float mean = (float)st.x, sd = (float)st.y, inv = (float)(1.0 / (1e-5 + st.y));
-                zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
-                zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
-                yl = cmul(zl, make_float2(m.x, m.y));
-                yr = cmul(zr, make_float2(m.z, m.w));
-                yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
-                yr = C > 1 ? make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean)) : make_float2(0.f, 0.f);
-            } else {
-                yl = cmul(zl, make_float2(m.x, m.y));
-                yr = cmul(zr, make_float2(m.z, m.w));
-            }
-            break;
-        }
-        default: {   // BACK_TFC
+        default: {   // BACK_TFC (BACK_ZMASK has its own batched path in back_kernel)
             const float* q = in + (int64_t)s * 4 * plane + idx;
             yl = make_float2(q[0], q[plane]);
             yr = make_float2(q[2 * plane], q[3 * plane]);
         }
+    }
+}
+
+// BACK_ZMASK: ox = Z * M for bin f, with the CaC normalisation around the stand-in
+// (src/htdemucs.cpp:434-436, 469); z and m were loaded by the caller (zero past n_bins).
+__device__ __forceinline__ void zmask_apply(const SplitParams& p, int ci, float4 z, float4 m, float2& yl,
+                                            float2& yr) {
+    float2 zl = make_float2(z.x, z.y), zr = make_float2(z.z, z.w);
+    if (p.cac_stats) {
+        const double2 st = p.cac_stats[ci];
+        const float mean = (float)st.x, sd = (float)st.y, inv = (float)(1.0 / (1e-5 + st.y));
+        zl = make_float2((zl.x - mean) * inv, (zl.y - mean) * inv);
+        zr = make_float2((zr.x - mean) * inv, (zr.y - mean) * inv);
+        yl = cmul(zl, make_float2(m.x, m.y));
+        yr = cmul(zr, make_float2(m.z, m.w));
+        yl = make_float2(fmaf(yl.x, sd, mean), fmaf(yl.y, sd, mean));
+        yr = p.n_channels > 1 ? make_float2(fmaf(yr.x, sd, mean), fmaf(yr.y, sd, mean)) : make_float2(0.f, 0.f);
+    } else {
+        yl = cmul(zl, make_float2(m.x, m.y));
+        yr = cmul(zr, make_float2(m.z, m.w));
     }
 }
 
@@ -267,13 +267,45 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
             float* Trs = p.Tr + (int64_t)ci * p.tr_chunk_stride + ((int64_t)tile * p.S + s) * C * (N - hop);
             for (int t = t_begin; t < t_end; t++) {
                 const int q0 = G.first_pos + t * hop;
-                for (int f = tid; f <= N / 2; f += T) {
-                    float2 yl, yr;
-                    back_load(p, ci, s, t, f, yl, yr);
+                auto pack = [&](int f, float2 yl, float2 yr) {
                     if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
                     const int fm = f == 0 ? 0 : N - f;
                     buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
                     if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
+                };
+                if (p.layout == BACK_ZMASK) {
+                    // the bins' Z and mask vectors in groups of GRP slots, every load of a group in
+                    // flight before the first is used
+                    constexpr int BPT = (N / 2 + T) / T, GRP = 5;
+                    const float4* zs = p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins;
+                    const float* ms = p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)s * G.T + t) * p.n_bins;
+#pragma unroll
+                    for (int g0 = 0; g0 < BPT; g0 += GRP) {
+                        float4 z[GRP], m[GRP];
+#pragma unroll
+                        for (int k = 0; k < GRP; k++) {
+                            const int f = tid + (g0 + k) * T;
+                            z[k] = m[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (g0 + k < BPT && f < p.n_bins) {
+                                z[k] = zs[f];
+                                m[k] = ld_stream4(ms + 4 * f);
+                            }
+                        }
+#pragma unroll
+                        for (int k = 0; k < GRP; k++) {
+                            const int f = tid + (g0 + k) * T;
+                            if (g0 + k >= BPT || f > N / 2) continue;
+                            float2 yl, yr;
+                            zmask_apply(p, ci, z[k], m[k], yl, yr);
+                            pack(f, yl, yr);
+                        }
+                    }
+                } else {
+                    for (int f = tid; f <= N / 2; f += T) {
+                        float2 yl, yr;
+                        back_load(p, ci, s, t, f, yl, yr);
+                        pack(f, yl, yr);
+                    }
                 }
                 __syncthreads();
                 passes<N, T, true, 1>(buf, tw, tid, InvInit{});
