@@ -97,18 +97,19 @@ def make_plan(pkg, eng, w, length):
                         zero_bins=w["zero_bins"], overlap=w["overlap"])
 
 
-def fused_algorithmic_bytes(plan, w):
-    """Bytes the fused kernel must move once: each chunk's audio window in, the masks in, and
-    each chunk's separated output out (4-byte floats)."""
-    if w["arch"] == "roformer":
-        lc = w["chunk"]
-    elif w["arch"] == "htdemucs":
+def kernel_algorithmic_bytes(plan, w):
+    """(the dominant kernel, the bytes it must move once per launch), 4-byte floats.
+    RoFormer / TFC-TDF, the fused kernel: each chunk's audio window in, the masks in, each
+    chunk's separated output out. HTDemucs, the back kernel: each segment's spectra
+    (2048 bins x T frames x 2 channels, complex) in, the masks in, the segment outputs out."""
+    if w["arch"] == "htdemucs":
         lc = w["segment"]
-    else:
-        lc = w["hop"] * (w["dim_t"] - 1)
+        z = plan.n_chunks * plan.n_frames * 2048 * 4
+        return "back_kernel", 4 * (z + plan.mask_floats + plan.n_chunks * plan.n_out_sources * plan.n_channels * lc)
+    lc = w["chunk"] if w["arch"] == "roformer" else w["hop"] * (w["dim_t"] - 1)
     n_src = plan.n_out_sources
-    return 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats
-                + plan.n_chunks * n_src * plan.n_channels * lc)
+    return "fused_kernel", 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats
+                                + plan.n_chunks * n_src * plan.n_channels * lc)
 
 
 def path_algorithmic_bytes(plan, w):
@@ -179,9 +180,9 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(workload):
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary, or None."""
-    path = os.path.join(ROOT, "profiles", f"fused_kernel_{workload}.txt")
+def profiled_traffic(kernel, workload):
+    """DRAM bytes per launch of the kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.txt")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):
@@ -602,9 +603,9 @@ def run_ours(args, w, rank, world, local_rank):
     audio_s = w["seconds"] * n_tracks
     value = audio_s / (ms / 1e3)
     peak, peak_kind = measured_peak()
-    fbytes = fused_algorithmic_bytes(plan, w)
+    kname, fbytes = kernel_algorithmic_bytes(plan, w)
     achieved = fbytes / (fused_ms / 1e3) / 1e9
-    traffic = profiled_traffic(args.workload)
+    traffic = profiled_traffic(kname, args.workload)
     line = None
     if rank == 0:
         line = {
@@ -616,7 +617,7 @@ def run_ours(args, w, rank, world, local_rank):
                        "chunks_per_track": plan.n_chunks, "frames_per_chunk": plan.n_frames,
                        "mask_bytes_per_track": 4 * plan.mask_floats,
                        "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "fused_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "algorithmic_bytes_per_launch": fbytes,
                          "fused_ms": fused_ms, "combine_ms": combine_ms, "prep_ms": prep_ms},
