@@ -97,7 +97,7 @@ struct stg_plan {
     stg_engine* engine = nullptr;
     HostPlan H;
     PlanDevice D;
-    DevBuf d_chunks, d_groups, d_w, d_env, d_btab, d_ebeg, d_ent, d_binv;
+    DevBuf d_chunks, d_groups, d_w, d_env, d_envp, d_btab, d_ebeg, d_ent, d_binv;
     DevBuf d_y, d_tr;
     DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
     DevBuf d_mask_t;                                  // t-major masks (HTDemucs, TFC-TDF)
@@ -119,6 +119,7 @@ struct stg_plan {
         upload(d_groups, H.groups, "chunk groups");
         upload(d_w, H.W, "weight table");
         upload(d_env, H.env, "envelope table");
+        upload(d_envp, H.env_period, "envelope period");
         upload(d_btab, H.btab, "band table");
         upload(d_ebeg, H.ebeg, "band table");
         upload(d_ent, H.ent, "band table");
@@ -149,6 +150,7 @@ struct stg_plan {
         D.groups = d_groups.as<ChunkGroup>();
         D.W = d_w.as<float>();
         D.env = d_env.as<float>();
+        D.env_period = H.env_period.empty() ? nullptr : d_envp.as<float>();
         D.btab = d_btab.as<int2>();
         D.ebeg = d_ebeg.as<int>();
         D.ent = d_ent.as<int2>();

@@ -55,7 +55,7 @@ template <> struct FftCfg<1024> : SmallFft<1024, 64, RadixList<8, 8, 16>> {};
 // STFT the reference runs (the fused kernel's own limit is FftCfg::HOPMAX).
 template <int N> __host__ __device__ constexpr int split_hopmax() { return N / 2; }
 
-__device__ __forceinline__ int64_t reflect1(int64_t j, int64_t n) {
+__device__ __forceinline__ int reflect1(int j, int n) {
     if (j < 0) j = -j;
     if (j >= n) j = 2 * (n - 1) - j;
     return j;
@@ -79,19 +79,20 @@ __device__ __forceinline__ float2 ld_stream2(const float* p) {
     return v;
 }
 
+// The track sample chunk-local sample pl reads, or -1 for a zero. 32-bit arithmetic: plans
+// are limited to INT32_MAX / 4 samples.
 template <class Params>
-__device__ __forceinline__ float chunk_sample(const Params& p, const ChunkDesc& cd,
-                                              const float* __restrict__ chan, int64_t pl) {
+__device__ __forceinline__ int chunk_index(const Params& p, const ChunkDesc& cd, int pl) {
     if (pl >= cd.valid) {
-        if (!cd.tail_reflect) return 0.0f;
-        pl = 2 * (int64_t)(cd.valid - 1) - pl;
+        if (!cd.tail_reflect) return -1;
+        pl = 2 * (cd.valid - 1) - pl;
     }
-    int64_t x = cd.src0 + pl;
-    if (cd.reflect) x = reflect1(x, cd.vlen);
-    else if (x < 0 || x >= cd.vlen) return 0.0f;
-    x += cd.vshift;
-    if (x < 0 || x >= p.len) return 0.0f;
-    return ld_stream(chan + x);
+    int x = (int)cd.src0 + pl;
+    if (cd.reflect) x = reflect1(x, (int)cd.vlen);
+    else if ((unsigned)x >= (unsigned)cd.vlen) return -1;
+    x += (int)cd.vshift;
+    if ((unsigned)x >= (unsigned)p.len) return -1;
+    return x;
 }
 
 // New input samples [q, q + hop) a frame needs beyond the previous one, per thread.
@@ -108,12 +109,12 @@ __device__ __forceinline__ float2 frame_sample(const Params& p, const ChunkDesc&
         r = q - p.g.n_fft / 2;
         if (r < 0 || r >= p.g.Lc) return make_float2(0.0f, 0.0f);
     } else {
-        r = (int)reflect1((int64_t)q - p.g.n_fft / 2, lxf);
-        if (p.g.ht_pad) r = (int)reflect1(r - p.g.ht_pad, p.g.Lc);
+        r = reflect1(q - p.g.n_fft / 2, lxf);
+        if (p.g.ht_pad) r = reflect1(r - p.g.ht_pad, p.g.Lc);
     }
-    const float a = chunk_sample(p, cd, chL, r);
-    const float b = p.n_channels > 1 ? chunk_sample(p, cd, chR, r) : 0.0f;
-    return make_float2(a, b);
+    const int x = chunk_index(p, cd, r);   // one index for both channels
+    if (x < 0) return make_float2(0.0f, 0.0f);
+    return make_float2(ld_stream(chL + x), p.n_channels > 1 ? ld_stream(chR + x) : 0.0f);
 }
 
 template <int N> __device__ __forceinline__ int ring_slot(int q) {

@@ -139,6 +139,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     float2* tw_s = out_ring + N;                          // [STW] twiddle table copy
     float* win_s = reinterpret_cast<float*>(tw_s + (STW ? N : 0));   // [SWIN] window copy
     int2* btab_s = reinterpret_cast<int2*>(win_s + (SWIN ? N : 0));   // [RoFormer] bin table copy
+    float* env_s = reinterpret_cast<float*>(btab_s + (ARCH == ARCH_ROFORMER ? N / 2 + 2 : 0));   // envelope period
     using Tw = std::conditional_t<STW, TwShared, TwGlobal>;
     const Tw tw{STW ? tw_s : p.tw};
     const float* win = SWIN ? win_s : p.win;
@@ -158,6 +159,9 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
         for (int i = tid; i < N; i += T) tw_s[i] = __ldg(p.tw + i);
     if constexpr (SWIN)
         for (int i = tid; i < N; i += T) win_s[i] = __ldg(p.win + i);
+    const bool env_on = p.env_period != nullptr;
+    if (env_on)
+        for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
 
     MaskOp<ARCH, N, T> mk;
     InPrefetch<T, FftCfg<N>::HOPMAX> nx;
@@ -261,6 +265,13 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             const bool last = t == t_end - 1;
             const int ny = (last && last_tile) ? N : hop;
             const int nflush = last ? N : hop;
+            // the envelope from the shared-memory period where it repeats (r: the period slot
+            // of this thread's sample, advanced by T per iteration)
+            int r = 0;
+            if (env_on) {
+                r = (q0 - G.out_offset + tid - p.env_lo) % hop;
+                if (r < 0) r += hop;
+            }
             for (int u = tid; u < nflush; u += T) {
                 const int q = q0 + u;
                 float2& o = out_ring[ring_slot<N>(q)];
@@ -268,7 +279,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 o = make_float2(0.f, 0.f);
                 const int j = q - G.out_offset;
                 const bool in = j >= 0 && j < G.Lout;
-                const float ie = in ? ld_stream(p.inv_env + j) : 0.0f;
+                float ie = 0.0f;
+                if (in) ie = env_on && j >= p.env_lo && j < p.env_hi ? env_s[r] : ld_stream(p.inv_env + j);
+                if (env_on) {
+                    r += T;
+                    while (r >= hop) r -= hop;
+                }
                 if (u < ny) {
                     if (in) {
                         Ys[j] = v.x * ie;
@@ -386,7 +402,8 @@ template <int ARCH, int N> static size_t smem_bytes_t() {
     return sizeof(float2) * ((size_t)padded_size(N) + 2 * (size_t)N) +
            (FftCfg<N>::SMEM_TW ? sizeof(float2) * (size_t)N : 0) +
            (FftCfg<N>::SMEM_WIN ? sizeof(float) * (size_t)N : 0) +
-           (ARCH == ARCH_ROFORMER ? sizeof(int2) * (size_t)(N / 2 + 2) : 0);
+           (ARCH == ARCH_ROFORMER ? sizeof(int2) * (size_t)(N / 2 + 2) : 0) +
+           sizeof(float) * (size_t)FftCfg<N>::HOPMAX;   // the envelope period
 }
 
 size_t fused_smem_bytes(int arch, int n) {

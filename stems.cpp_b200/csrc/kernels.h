@@ -75,6 +75,8 @@ struct FusedParams {
     const float* win;          // periodic Hann [n_fft]
     const float2* tw;          // the FFT plan's per-pass twiddles (fft.cuh: twiddle_index)
     const float* inv_env;      // [Lout]: 1 / sum of squared windows, 0 where it vanishes
+    const float* env_period;   // [hop]: inv_env over [env_lo, env_hi), where it repeats every hop
+    int env_lo, env_hi;        // (empty when env_period is null)
     float fwd_scale, inv_scale;
     // mask (the stand-in for the network's output), one block per chunk; TFC-TDF masks in the
     // t-major layout of launch_mask_transpose
@@ -160,6 +162,8 @@ struct SplitParams {
     const float2* tw;
     float fwd_scale, inv_scale;
     const float* inv_env;
+    const float* env_period;   // as FusedParams
+    int env_lo, env_hi;
     int layout;                // FrontLayout or BackLayout
     int n_bins;                // bins the layout holds
     int zero_bins;             // FRONT_TFC

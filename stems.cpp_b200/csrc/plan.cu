@@ -100,6 +100,22 @@ void finish_plan(HostPlan& P, int env_frames) {
     P.max_out_len = 0;
     for (const ChunkDesc& c : P.chunks) P.max_out_len = std::max<int64_t>(P.max_out_len, c.out_len);
     P.env = inv_envelope(N, hop, env_frames, P.g.out_offset, P.g.Lout);
+    // Where every frame overlapping a sample exists, the window sum repeats every hop, bit for
+    // bit (the same squares summed in the same order): the kernels read that stretch from a
+    // hop-long table in shared memory instead of the envelope in global memory.
+    P.env_lo = P.env_hi = 0;
+    P.env_period.clear();
+    {
+        const int lo = std::max(0, N - P.g.out_offset);
+        const int hi = std::min(P.g.Lout, env_frames * hop - P.g.out_offset);
+        bool periodic = hi - lo >= hop;
+        for (int j = lo + hop; periodic && j < hi; j++) periodic = P.env[j] == P.env[j - hop];
+        if (periodic) {
+            P.env_lo = lo;
+            P.env_hi = hi;
+            P.env_period.assign(P.env.begin() + lo, P.env.begin() + lo + hop);
+        }
+    }
 }
 
 } // namespace
@@ -569,6 +585,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
     f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
     f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
+    f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
     f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
     f.mask_chunk_stride = P.mask_per_chunk;
     f.bin_tab = D.btab;
@@ -651,6 +668,9 @@ SplitParams split_params(const HostPlan& P, const PlanDevice& D, const float* d_
     s.fwd_scale = P.fwd_scale;
     s.inv_scale = P.inv_scale;
     s.inv_env = D.env;
+    s.env_period = D.env_period;
+    s.env_lo = P.env_lo;
+    s.env_hi = P.env_hi;
     s.bin_tab = D.btab;
     s.bin_multi = P.bin_multi;
     s.bin_ebeg = D.ebeg;
@@ -697,6 +717,7 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
         f.chunks = D.chunks + first; f.n_chunks = n;
         f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
         f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
+    f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
         f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
         f.mask = d_net_out; f.mask_chunk_stride = P.mask_per_chunk;
         f.bin_tab = D.btab; f.bin_multi = P.bin_multi;

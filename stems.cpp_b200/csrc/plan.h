@@ -51,6 +51,8 @@ struct HostPlan {
     int64_t y_chunk_stride = 0, tr_chunk_stride = 0;
     std::vector<float> W;          // crossfade weight tables (ChunkDesc::w_off)
     std::vector<float> env;        // inverse window-sum envelope of a chunk's output
+    std::vector<float> env_period; // env over [env_lo, env_hi), one hop of it (FusedParams)
+    int env_lo = 0, env_hi = 0;
     std::vector<int2> btab;        // RoFormer bin table (kernels.h: FusedParams::bin_tab)
     std::vector<int> ebeg;         // RoFormer CSR over bins
     std::vector<int2> ent;
@@ -86,6 +88,7 @@ struct PlanDevice {
     const ChunkGroup* groups = nullptr;
     const float* W = nullptr;
     const float* env = nullptr;
+    const float* env_period = nullptr;
     const int2* btab = nullptr;
     const int* ebeg = nullptr;
     const int2* ent = nullptr;

@@ -252,11 +252,15 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);
     float2* out_ring = buf + padded_size(N);
+    float* env_s = reinterpret_cast<float*>(out_ring + N);   // the envelope period
     const TwGlobal tw{p.tw};
     const int tid = threadIdx.x;
     const FrameGeom& G = p.g;
     const int hop = G.hop, C = p.n_channels;
     for (int i = tid; i < N; i += T) out_ring[i] = make_float2(0.f, 0.f);
+    const bool env_on = p.env_period != nullptr;
+    if (env_on)
+        for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
 
     for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
         const int tile = item % p.n_tiles, ci = item / p.n_tiles;
@@ -321,6 +325,11 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
                 const bool last = t == t_end - 1;
                 const int ny = (last && last_tile) ? N : hop;
                 const int nflush = last ? N : hop;
+                int r = 0;   // the envelope period slot of this thread's sample (kernels.cu)
+                if (env_on) {
+                    r = (q0 - G.out_offset + tid - p.env_lo) % hop;
+                    if (r < 0) r += hop;
+                }
                 for (int u = tid; u < nflush; u += T) {
                     const int q = q0 + u;
                     float2& o = out_ring[ring_slot<N>(q)];
@@ -328,7 +337,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
                     o = make_float2(0.f, 0.f);
                     const int j = q - G.out_offset;
                     const bool in = j >= 0 && j < G.Lout;
-                    const float ie = in ? ld_stream(p.inv_env + j) : 0.0f;
+                    float ie = 0.0f;
+                    if (in) ie = env_on && j >= p.env_lo && j < p.env_hi ? env_s[r] : ld_stream(p.inv_env + j);
+                    if (env_on) {
+                        r += T;
+                        while (r >= hop) r -= hop;
+                    }
                     if (u < ny) {
                         if (in) {
                             Ys[j] = v.x * ie;
@@ -366,7 +380,7 @@ template <int N> cudaError_t front_t(const SplitParams& p, cudaStream_t st) {
     return launch_persistent(front_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
 }
 template <int N> cudaError_t back_t(const SplitParams& p, cudaStream_t st) {
-    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N);
+    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N) + sizeof(float) * (size_t)(N / 2);
     return launch_persistent(back_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
 }
 
@@ -394,7 +408,9 @@ int back_resident_ctas(int n) {
         return per_sm * n_sm;
     };
     switch (n) {
-        case 4096: return query(back_kernel<4096>, FftCfg<4096>::T, sizeof(float2) * ((size_t)padded_size(4096) + 4096));
+        case 4096:
+            return query(back_kernel<4096>, FftCfg<4096>::T,
+                         sizeof(float2) * ((size_t)padded_size(4096) + 4096) + sizeof(float) * 2048);
     }
     return 0;
 }
