@@ -117,6 +117,33 @@ __device__ __forceinline__ float2 frame_sample(const Params& p, const ChunkDesc&
     return make_float2(ld_stream(chL + x), p.n_channels > 1 ? ld_stream(chR + x) : 0.0f);
 }
 
+// When no padding rule touches any sample frames [t_begin, t_end) of the chunk read, the tile
+// reads one linear stretch of the track: sample x = q + offset for padded position q. Returns
+// that offset, or INT_MIN when some sample needs the general rule (chunk and track edges).
+constexpr int kNoLinear = -2147483647 - 1;
+template <class Params>
+__device__ __forceinline__ int linear_offset(const Params& p, const ChunkDesc& cd, int t_begin, int t_end) {
+    const FrameGeom& G = p.g;
+    const int qa = G.first_pos + t_begin * G.hop, qb = G.first_pos + (t_end - 1) * G.hop + G.n_fft;
+    const int shift = G.n_fft / 2 + G.ht_pad;                       // chunk-local r = q - shift
+    const int ra = qa - shift, rb = qb - shift;
+    if (ra < 0 || rb > G.Lc || rb > cd.valid) return kNoLinear;
+    if (G.ht_pad && qb - G.n_fft / 2 > G.ht_lxf) return kNoLinear;  // HTDemucs' first reflect
+    const int xa = (int)cd.src0 + ra, xb = (int)cd.src0 + rb;
+    if (xa < 0 || xb > (int)cd.vlen) return kNoLinear;
+    if (xa + (int)cd.vshift < 0 || xb + (int)cd.vshift > (int)p.len) return kNoLinear;
+    return (int)cd.src0 + (int)cd.vshift - shift;
+}
+
+// frame_sample through the tile's linear offset when it has one
+template <class Params>
+__device__ __forceinline__ float2 tile_sample(const Params& p, const ChunkDesc& cd, const float* chL,
+                                              const float* chR, int lxf, int lin, int q) {
+    if (lin == kNoLinear) return frame_sample(p, cd, chL, chR, lxf, q);
+    const int x = lin + q;
+    return make_float2(ld_stream(chL + x), p.n_channels > 1 ? ld_stream(chR + x) : 0.0f);
+}
+
 template <int N> __device__ __forceinline__ int ring_slot(int q) {
     if constexpr ((N & (N - 1)) == 0) return q & (N - 1);
     else return q % N;

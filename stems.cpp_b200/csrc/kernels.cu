@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     const int t_begin = tile * p.K;
     const int t_end = min(G.T, t_begin + p.K);
     const bool last_tile = t_end == G.T;
+    const int lin = linear_offset(p, cd, t_begin, t_end);
 
     for (int s = 0; s < p.S; s++) {
         float* Ys = p.Y + (int64_t)ci * p.y_chunk_stride + (int64_t)s * C * G.Lout;
@@ -184,11 +185,11 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
         // prologue of a stem pass: the first frame's window and the next frame's new samples
         {
             const int q0 = G.first_pos + t_begin * hop;
-            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = frame_sample(p, cd, chL, chR, lxf, q0 + n);
+            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + n);
 #pragma unroll
             for (int k = 0; k < nx.K; k++) {
                 const int u = tid + k * T;
-                if (u < hop && t_begin + 1 < t_end) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + N + u);
+                if (u < hop && t_begin + 1 < t_end) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + N + u);
             }
             if constexpr (FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t_begin, tid);
         }
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 #pragma unroll
                     for (int k = 0; k < nx.K; k++) {
                         const int u = tid + k * T;
-                        if (u < hop) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + hop + N + u);
+                        if (u < hop) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + hop + N + u);
                     }
                 }
             }

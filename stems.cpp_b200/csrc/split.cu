@@ -171,14 +171,15 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
         const int tile = item % p.n_tiles, ci = item / p.n_tiles;
         const ChunkDesc cd = p.chunks[ci];
         const int t_begin = tile * p.K, t_end = min(G.T, t_begin + p.K);
+        const int lin = linear_offset(p, cd, t_begin, t_end);
         double acc_s = 0.0, acc_q = 0.0;   // FRONT_STATS
         {
             const int q0 = G.first_pos + t_begin * hop;
-            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = frame_sample(p, cd, chL, chR, lxf, q0 + n);
+            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + n);
 #pragma unroll
             for (int k = 0; k < nx.K; k++) {
                 const int u = tid + k * T;
-                if (u < hop && t_begin + 1 < t_end) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + N + u);
+                if (u < hop && t_begin + 1 < t_end) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + N + u);
             }
         }
         __syncthreads();
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
 #pragma unroll
                     for (int k = 0; k < nx.K; k++) {
                         const int u = tid + k * T;
-                        if (u < hop) nx.v[k] = frame_sample(p, cd, chL, chR, lxf, q0 + hop + N + u);
+                        if (u < hop) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + hop + N + u);
                     }
                 }
             }
