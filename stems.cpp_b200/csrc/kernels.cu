@@ -288,12 +288,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 }
                 if (u < ny) {
                     if (in) {
-                        Ys[j] = v.x * ie;
-                        if (C > 1) Ys[G.Lout + j] = v.y * ie;
+                        if (C > 1) reinterpret_cast<float2*>(Ys)[j] = make_float2(v.x * ie, v.y * ie);
+                        else Ys[j] = v.x * ie;
                     }
                 } else {
-                    Trs[u - hop] = v.x * ie;
-                    if (C > 1) Trs[(N - hop) + u - hop] = v.y * ie;
+                    if (C > 1) reinterpret_cast<float2*>(Trs)[u - hop] = make_float2(v.x * ie, v.y * ie);
+                    else Trs[u - hop] = v.x * ie;
                 }
             }
             // the next iteration's first barrier (after forward pass 1) orders these ring
@@ -341,19 +341,32 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
             const float w = __ldg(p.W + d.w_off + u);
             wsum += w;
             const int j = d.y_off + u;
-            const float* y = p.Y + (int64_t)g * p.y_chunk_stride + j;
+            const float* y = p.Y + (int64_t)g * p.y_chunk_stride + (int64_t)j * p.C;
             // the tile boundary region j falls in, if any
             const int q = j + G.out_offset - G.first_pos;
             const int tau = q / span;
             const int uu = q - tau * span;
             const float* tr = nullptr;
             if (tau >= 1 && tau < p.n_tiles && uu < ov)
-                tr = p.Tr + (int64_t)g * p.tr_chunk_stride + (int64_t)(tau - 1) * SC * ov + uu;
+                tr = p.Tr + (int64_t)g * p.tr_chunk_stride + (int64_t)(tau - 1) * SC * ov + uu * p.C;
+            if (p.C == 2) {   // the stems' (L, R) pairs as one 8-byte load each
 #pragma unroll
-            for (int k = 0; k < SC; k++) {
-                float v = __ldg(y + (int64_t)k * G.Lout);
-                if (tr) v += __ldg(tr + k * ov);
-                acc[k] = fmaf(w, v, acc[k]);
+                for (int s = 0; s < SC / 2; s++) {
+                    float2 v = __ldg(reinterpret_cast<const float2*>(y + (int64_t)s * 2 * G.Lout));
+                    if (tr) {
+                        const float2 r = __ldg(reinterpret_cast<const float2*>(tr + s * 2 * ov));
+                        v = make_float2(v.x + r.x, v.y + r.y);
+                    }
+                    acc[2 * s] = fmaf(w, v.x, acc[2 * s]);
+                    acc[2 * s + 1] = fmaf(w, v.y, acc[2 * s + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < SC; k++) {
+                    float v = __ldg(y + (int64_t)k * G.Lout);
+                    if (tr) v += __ldg(tr + k * ov);
+                    acc[k] = fmaf(w, v, acc[k]);
+                }
             }
         }
         const float inv = 1.0f / wsum;

@@ -96,9 +96,9 @@ struct FusedParams {
     // TFC-TDF
     int dim_f, zero_bins;
     // outputs
-    float* Y;                  // [chunk][S*C][Lout]
+    float* Y;                  // [chunk][S][Lout][C]: the channels of a sample side by side
     int64_t y_chunk_stride;
-    float* Tr;                 // [chunk][tile][S*C][n_fft - hop]
+    float* Tr;                 // [chunk][tile][S][n_fft - hop][C]
     int64_t tr_chunk_stride;
 };
 

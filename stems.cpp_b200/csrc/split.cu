@@ -346,12 +346,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
                     }
                     if (u < ny) {
                         if (in) {
-                            Ys[j] = v.x * ie;
-                            if (C > 1) Ys[G.Lout + j] = v.y * ie;
+                            if (C > 1) reinterpret_cast<float2*>(Ys)[j] = make_float2(v.x * ie, v.y * ie);
+                            else Ys[j] = v.x * ie;
                         }
                     } else {
-                        Trs[u - hop] = v.x * ie;
-                        if (C > 1) Trs[(N - hop) + u - hop] = v.y * ie;
+                        if (C > 1) reinterpret_cast<float2*>(Trs)[u - hop] = make_float2(v.x * ie, v.y * ie);
+                        else Trs[u - hop] = v.x * ie;
                     }
                 }
                 // the next frame's first barrier orders these ring writes before later reads
