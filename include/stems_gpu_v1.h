@@ -214,6 +214,14 @@ typedef struct {
 STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream, const stg_run_options* options);
 
+/* DualMono (src/separator.cpp:15-47): a plan of a one-channel model (n_channels 1) run on
+ * each channel of a stereo mix on its own, the results interleaved into planar stereo.
+ * d_mix [2][n_samples]; d_mask holds the left channel's masks (stg_plan_info's
+ * mask_floats_per_chunk x n_chunks floats), then the right channel's; d_out
+ * [n_out_sources][2][n_samples]. The plan keeps one channel's result as scratch. */
+STG_API stg_status stg_separate_dual_mono(stg_plan* plan, const float* d_mix, const float* d_mask,
+                                          float* d_out, void* stream);
+
 /* ---- the halves around a real network --------------------------------------------------- */
 
 /* The same separation with the network between the halves, as the reference runs it: for

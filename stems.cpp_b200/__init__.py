@@ -121,6 +121,7 @@ _SIGNATURES = {
     "stg_plan_destroy": (None, [C.c_void_p]),
     "stg_plan_get_info": (C.c_int32, [C.c_void_p, C.POINTER(PlanInfo)]),
     "stg_separate": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_dual_mono": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.POINTER(RunOptions)]),
@@ -430,6 +431,12 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+    def separate_dual_mono(self, mix, mask, out, stream=None):
+        """A one-channel plan over both channels of a stereo mix (src/separator.cpp:15-47):
+        mix [2][n], mask = the left channel's masks then the right's, out [S][2][n]."""
+        self.engine._check(lib().stg_separate_dual_mono(self._h, _ptr(mix), _ptr(mask), _ptr(out),
+                                                        _stream_of(stream, mix, mask, out)), "separate_dual_mono")
 
     def separate(self, mix, mask, out, stream=None, chunks_per_batch=0, progress=None, should_cancel=None):
         """Device buffers (torch CUDA tensors or pointers): mix [C][n], mask, out [S][C][n]."""

@@ -124,6 +124,27 @@ STG_API stg_status stg_separate(stg_plan* p, const float* d_mix, const float* d_
     return stg_separate_ex(p, d_mix, d_mask, d_out, stream, nullptr);
 }
 
+STG_API stg_status stg_separate_dual_mono(stg_plan* p, const float* d_mix, const float* d_mask, float* d_out,
+                                          void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        const HostPlan& H = p->H;
+        if (H.C != 1) fail(STG_INVALID_ARGUMENT, "dual mono needs a plan of a one-channel model");
+        if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const size_t row = sizeof(float) * (size_t)H.len;
+        p->dm_out.reserve(row * H.S_out, "dual-mono scratch");
+        const int64_t mask_per_channel = H.mask_per_chunk * (int64_t)H.chunks.size();
+        for (int c = 0; c < 2; c++) {                                  // separator.cpp:36-43
+            p->run(d_mix + (size_t)c * H.len, d_mask + c * mask_per_channel, p->dm_out.as<float>(), st, nullptr);
+            // stem s of this channel to row s * 2 + c of the stereo result
+            cuda_check(cudaMemcpy2DAsync(d_out + (size_t)c * H.len, 2 * row, p->dm_out.p, row, row, H.S_out,
+                                         cudaMemcpyDeviceToDevice, st), "interleave the channels");
+        }
+    });
+}
+
 STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const float* h_mask, float* h_out,
                                      void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;

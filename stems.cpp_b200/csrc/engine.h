@@ -104,6 +104,7 @@ struct stg_plan {
     DevBuf d_zspec;                                   // HTDemucs spectra
     const float* mono_src = nullptr;                  // the track d_mixn was normalised from
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
+    DevBuf dm_out;                 // one channel's result (stg_separate_dual_mono)
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
 
@@ -163,7 +164,7 @@ struct stg_plan {
 
     void run(const float* d_mix, const float* d_mask, float* d_out, cudaStream_t st, const stg_run_options* opt) {
         if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
-        if (reinterpret_cast<uintptr_t>(d_mask) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+        H.check_mask(d_mask);
         cuda_check(cudaSetDevice(engine->device), "cudaSetDevice");
         timing.timed = engine->profiling;
         if (timing.timed)

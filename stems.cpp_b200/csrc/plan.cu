@@ -551,7 +551,7 @@ const float* normalise_mix(const HostPlan& P, const PlanDevice& D, const float* 
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing) {
     if (!d_mix_in || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
-    if (reinterpret_cast<uintptr_t>(d_mask) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+    P.check_mask(d_mask);
     const bool timed = timing && timing->timed;
     if (timing) timing->launches = 0;
     if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
@@ -711,7 +711,7 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     check_range(P, first, n);
     if (P.back_is_fused) {
         // RoFormer: the network's masks are exactly the fused kernel's mask input
-        if (reinterpret_cast<uintptr_t>(d_net_out) % 16) fail(STG_INVALID_ARGUMENT, "mask must be 16-byte aligned");
+        P.check_mask(d_net_out);
         FusedParams f{};
         f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
         f.chunks = D.chunks + first; f.n_chunks = n;

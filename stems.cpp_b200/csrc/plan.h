@@ -65,6 +65,13 @@ struct HostPlan {
 
     bool primitive = false;        // a single-chunk DSP primitive: the output is the chunk's
     int64_t arch_out_len() const { return primitive ? g.Lout : len; }
+    // the alignment the masks need: RoFormer's kernel reads a bin's entries as one vector of
+    // 2C floats; the other layouts go through the transposition, which reads floats
+    int mask_align() const { return arch == ARCH_ROFORMER ? 8 * C : 4; }
+    void check_mask(const void* m) const {
+        if (reinterpret_cast<uintptr_t>(m) % mask_align())
+            fail(STG_INVALID_ARGUMENT, "mask must be " + std::to_string(mask_align()) + "-byte aligned");
+    }
     int64_t n_chunks() const { return (int64_t)chunks.size(); }
     int64_t out_floats() const { return (int64_t)S_out * C * len; }
     size_t y_bytes() const { return sizeof(float) * (size_t)y_chunk_stride * chunks.size(); }

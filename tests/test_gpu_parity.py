@@ -153,3 +153,34 @@ def test_deterministic_and_host_entry(pkg, engine):
     c = plan.separate_host(mix, mask)
     assert np.array_equal(a, b), "two runs differ bitwise"
     assert np.array_equal(a, c), "host entry point differs from the device one"
+
+
+# ---- DualMono (src/separator.cpp:15-47) ----------------------------------------------------------
+def test_dual_mono_roformer_matches_oracle(pkg, engine, oracle_mod):
+    """A mono RoFormer (a dereverb model's layout) over a stereo mix, channel by channel."""
+    import torch
+    sizes, freqs = pkg.bands.bs_bands()
+    chunk, n = 441 * 40, 441 * 90 + 11
+    plan = engine.plan_roformer(n, sizes, freqs, n_channels=1, chunk=chunk, num_overlap=2, complement=True)
+    mix = synth_audio(91, n)
+    mask = synth_mask(92, 2 * plan.mask_floats, 0.5)   # left channel's masks, then the right's
+    out = torch.empty((plan.n_out_sources, 2, n), device="cuda")
+    plan.separate_dual_mono(torch.from_numpy(mix).cuda(), torch.from_numpy(mask).cuda(), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    p = oracle_mod.rf_params(sizes, freqs, n_channels=1, chunk=chunk, num_overlap=2, complement=1, threads=8)
+    for c in range(2):
+        want = oracle_mod.rf_separate(p, mix[c:c + 1], mask[c * plan.mask_floats:(c + 1) * plan.mask_floats])
+        check(got[:, c:c + 1], want, f"dual mono channel {c}")
+
+
+def test_misaligned_mask_is_rejected(pkg, engine):
+    import torch
+    sizes, freqs = pkg.bands.bs_bands()
+    n = 441 * 60
+    plan = engine.plan_roformer(n, sizes, freqs, chunk=441 * 40, num_overlap=2)
+    mask = torch.zeros(plan.mask_floats + 4, device="cuda")
+    with pytest.raises(pkg.StemsError) as e:
+        plan.separate(torch.zeros((2, n), device="cuda"), mask[1:], torch.empty(plan.out_shape, device="cuda"))
+    assert e.value.code == 1 and "aligned" in str(e.value)
+
