@@ -214,6 +214,15 @@ typedef struct {
 STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream, const stg_run_options* options);
 
+/* Output samples [sample_begin, sample_end) of every output row of the separation, running only
+ * the chunks that reach them: the same floats stg_separate writes there (each sample sums the
+ * same chunks in the same order). d_mix, d_mask and d_out are the whole track's buffers; other
+ * samples of d_out are left as they are. One track split over several GPUs by sample ranges
+ * needs no exchange between them; the chunks at a range's edges run on both neighbours. No
+ * reference counterpart: the reference separates a track in one call. */
+STG_API stg_status stg_separate_part(stg_plan* plan, const float* d_mix, const float* d_mask,
+                                     int64_t sample_begin, int64_t sample_end, float* d_out, void* stream);
+
 /* DualMono (src/separator.cpp:15-47): a plan of a one-channel model (n_channels 1) run on
  * each channel of a stereo mix on its own, the results interleaved into planar stereo.
  * d_mix [2][n_samples]; d_mask holds the left channel's masks (stg_plan_info's

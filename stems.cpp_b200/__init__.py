@@ -121,6 +121,8 @@ _SIGNATURES = {
     "stg_plan_destroy": (None, [C.c_void_p]),
     "stg_plan_get_info": (C.c_int32, [C.c_void_p, C.POINTER(PlanInfo)]),
     "stg_separate": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_part": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
+                                      C.c_void_p]),
     "stg_separate_dual_mono": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -431,6 +433,12 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+    def separate_part(self, mix, mask, out, sample_begin, sample_end, stream=None):
+        """Samples [sample_begin, sample_end) of every output row (out is the whole track's
+        buffer), from the chunks that reach them only."""
+        self.engine._check(lib().stg_separate_part(self._h, _ptr(mix), _ptr(mask), sample_begin, sample_end,
+                                                   _ptr(out), _stream_of(stream, mix, mask, out)), "separate_part")
 
     def separate_dual_mono(self, mix, mask, out, stream=None):
         """A one-channel plan over both channels of a stereo mix (src/separator.cpp:15-47):

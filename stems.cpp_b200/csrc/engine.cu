@@ -124,6 +124,14 @@ STG_API stg_status stg_separate(stg_plan* p, const float* d_mix, const float* d_
     return stg_separate_ex(p, d_mix, d_mask, d_out, stream, nullptr);
 }
 
+STG_API stg_status stg_separate_part(stg_plan* p, const float* d_mix, const float* d_mask, int64_t sample_begin,
+                                     int64_t sample_end, float* d_out, void* stream) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] {
+        p->run(d_mix, d_mask, d_out, static_cast<cudaStream_t>(stream), nullptr, sample_begin, sample_end);
+    });
+}
+
 STG_API stg_status stg_separate_dual_mono(stg_plan* p, const float* d_mix, const float* d_mask, float* d_out,
                                           void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;

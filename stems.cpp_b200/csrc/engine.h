@@ -162,7 +162,8 @@ struct stg_plan {
         D.Tr = d_tr.as<float>();
     }
 
-    void run(const float* d_mix, const float* d_mask, float* d_out, cudaStream_t st, const stg_run_options* opt) {
+    void run(const float* d_mix, const float* d_mask, float* d_out, cudaStream_t st, const stg_run_options* opt,
+             int64_t sample_begin = 0, int64_t sample_end = -1) {
         if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
         H.check_mask(d_mask);
         cuda_check(cudaSetDevice(engine->device), "cudaSetDevice");
@@ -170,7 +171,7 @@ struct stg_plan {
         if (timing.timed)
             for (cudaEvent_t& e : timing.ev)
                 if (!e) cuda_check(cudaEventCreate(&e), "cudaEventCreate");
-        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing);
+        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing, sample_begin, sample_end);
     }
 
     // The mix the front half reads: with the mono normalisation, chunk 0's call normalises

@@ -312,8 +312,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 // and divide by the summed weight; then average the groups and finish (epilogue).
 template <int SC>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= p.len) return;
+    const int i = (int)(p.i_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= p.i_end) return;
     const FrameGeom& G = p.g;
     const int step = (int)p.step_out;
     const int span = p.K * G.hop, ov = G.n_fft - G.hop;
@@ -570,9 +570,9 @@ cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int 
 }
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
-    if (p.len <= 0) return cudaSuccess;
+    if (p.i_end <= p.i_begin) return cudaSuccess;
     const int threads = 256;
-    const unsigned blocks = (unsigned)((p.len + threads - 1) / threads);
+    const unsigned blocks = (unsigned)((p.i_end - p.i_begin + threads - 1) / threads);
     switch (p.S * p.C) {
         case 1: combine_kernel<1><<<blocks, threads, 0, st>>>(p); break;
         case 2: combine_kernel<2><<<blocks, threads, 0, st>>>(p); break;

@@ -120,6 +120,7 @@ struct CombineParams {
     const float* W;            // weight tables
     int S, C;
     int64_t len;               // output samples per row
+    int64_t i_begin, i_end;    // the output samples this launch writes
     int mode;                  // ARCH_*
     int nan_to_zero;
     float compensate;          // multiplies the stems (1 = off)

@@ -548,38 +548,71 @@ const float* normalise_mix(const HostPlan& P, const PlanDevice& D, const float* 
     return D.mixn;
 }
 
+// The chunks whose outputs reach output samples [b, e), as index ranges (one per chunk group,
+// adjacent ones merged). Chunks of a group are in output order.
+std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_t e) {
+    std::vector<std::pair<int, int>> r;
+    for (const ChunkGroup& g : P.groups) {
+        int lo = -1, hi = -1;
+        for (int k = g.c0; k < g.c1; k++) {
+            const ChunkDesc& d = P.chunks[k];
+            if (d.out0 < e + g.out_shift && d.out0 + d.out_len > b + g.out_shift) {
+                if (lo < 0) lo = k;
+                hi = k + 1;
+            }
+        }
+        if (lo < 0) continue;
+        if (!r.empty() && r.back().second == lo) r.back().second = hi;
+        else r.emplace_back(lo, hi);
+    }
+    return r;
+}
+
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
-                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing) {
+                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
+                 int64_t sample_begin, int64_t sample_end) {
     if (!d_mix_in || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
     P.check_mask(d_mask);
+    if (sample_end < 0) sample_end = P.len;
+    if (sample_begin < 0 || sample_begin >= sample_end || sample_end > P.len)
+        fail(STG_INVALID_ARGUMENT, "sample range outside the track");
+    const bool whole = sample_begin == 0 && sample_end == P.len;
+    const std::vector<std::pair<int, int>> ranges =
+        whole ? std::vector<std::pair<int, int>>{{0, (int)P.chunks.size()}} : chunks_for(P, sample_begin, sample_end);
+    int total = 0;
+    for (const auto& rg : ranges) total += rg.second - rg.first;
     const bool timed = timing && timing->timed;
     if (timing) timing->launches = 0;
     if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
     const float* d_mix = normalise_mix(P, D, d_mix_in, st);
     if (timing && P.mono_norm) timing->launches += 5;
-    const int G = (int)P.chunks.size();
     const bool zpath = P.z_per_chunk() > 0;   // HTDemucs: spectra once, then the back kernel per stem
-    if (zpath) {
-        if (!D.zspec || !D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the segment spectra");
-        SplitParams z = split_params(P, D, d_mix, 0, G);
-        z.layout = FRONT_ZSPEC;
-        z.n_bins = P.front_bins;
-        z.zspec = D.zspec;
-        z.z_chunk_stride = P.z_per_chunk();
-        if (P.cac_norm) {
-            if (!D.cac_part || !D.cac_stats) fail(STG_INTERNAL_ERROR, "no scratch for the CaC normalisation");
-            z.stats_out = D.cac_part;
-        }
-        cuda_check(stg::launch_front(z, st), "segment spectra launch");
-        if (timing) timing->launches++;
-        if (P.cac_norm) {
-            const double count = 2.0 * P.C * P.front_bins * P.g.T;
-            cuda_check(launch_cac_finish(D.cac_part, G, P.n_tiles, count, D.cac_stats, st), "CaC statistics launch");
+    for (const auto& rg : ranges) {
+        const int c0 = rg.first, G = rg.second - rg.first;
+        if (zpath) {
+            if (!D.zspec || !D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the segment spectra");
+            SplitParams z = split_params(P, D, d_mix, c0, G);
+            z.layout = FRONT_ZSPEC;
+            z.n_bins = P.front_bins;
+            z.zspec = D.zspec + (int64_t)c0 * P.z_per_chunk();
+            z.z_chunk_stride = P.z_per_chunk();
+            if (P.cac_norm) {
+                if (!D.cac_part || !D.cac_stats) fail(STG_INTERNAL_ERROR, "no scratch for the CaC normalisation");
+                z.stats_out = D.cac_part + (int64_t)c0 * P.n_tiles;
+            }
+            cuda_check(stg::launch_front(z, st), "segment spectra launch");
             if (timing) timing->launches++;
+            if (P.cac_norm) {
+                const double count = 2.0 * P.C * P.front_bins * P.g.T;
+                cuda_check(launch_cac_finish(D.cac_part + (int64_t)c0 * P.n_tiles, G, P.n_tiles, count,
+                                             D.cac_stats + c0, st),
+                           "CaC statistics launch");
+                if (timing) timing->launches++;
+            }
+        } else if (P.cac_norm) {
+            const int k = cac_statistics(P, D, d_mix, c0, G, st);
+            if (timing) timing->launches += k;
         }
-    } else if (P.cac_norm) {
-        const int k = cac_statistics(P, D, d_mix, 0, G, st);
-        if (timing) timing->launches += k;
     }
     FusedParams f{};
     f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
@@ -587,60 +620,67 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
     f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
     f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
-    f.mask_chunk_stride = P.mask_per_chunk;
     f.bin_tab = D.btab;
     f.bin_multi = P.bin_multi;
     f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
     f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
     f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
     f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
-    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : G;
-    for (int b0 = 0; b0 < G; b0 += per) {
-        if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
-        const int nb = std::min(per, G - b0);
-        f.chunks = D.chunks + b0;
-        f.n_chunks = nb;
-        f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
-        f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
-        f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
-        if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
-            if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
-            cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins, P.g.T,
-                                             D.mask_t, P.mask_t_per_chunk(), st),
-                       "mask transposition launch");
+    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total;
+    int done = 0;
+    bool first_batch = true;
+    for (const auto& rg : ranges) {
+        for (int b0 = rg.first; b0 < rg.second; b0 += per) {
+            if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
+            const int nb = std::min(per, rg.second - b0);
+            f.chunks = D.chunks + b0;
+            f.n_chunks = nb;
+            f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
+            f.mask_chunk_stride = P.mask_per_chunk;
+            f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
+            f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
+            if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
+                if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
+                cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins,
+                                                 P.g.T, D.mask_t, P.mask_t_per_chunk(), st),
+                           "mask transposition launch");
+                if (timing) timing->launches++;
+                f.mask = reinterpret_cast<const float*>(D.mask_t);
+                f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
+            }
+            if (timed && first_batch) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
+            first_batch = false;
+            if (zpath) {   // every stem's ox = Z * M (CaC-normalised), iSTFT and overlap-add
+                SplitParams b = split_params(P, D, d_mix, b0, nb);
+                b.layout = BACK_ZMASK;
+                b.n_bins = P.back_bins;
+                b.net = const_cast<float*>(f.mask);
+                b.net_chunk_stride = f.mask_chunk_stride;
+                b.zspec = D.zspec + (int64_t)b0 * P.z_per_chunk();
+                b.z_chunk_stride = P.z_per_chunk();
+                b.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
+                cuda_check(stg::launch_back(b, st), "back kernel launch");
+            } else {
+                cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+            }
             if (timing) timing->launches++;
-            f.mask = reinterpret_cast<const float*>(D.mask_t);
-            f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
-        }
-        if (timed && b0 == 0) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
-        if (zpath) {   // every stem's ox = Z * M (CaC-normalised), iSTFT and overlap-add
-            SplitParams b = split_params(P, D, d_mix, b0, nb);
-            b.layout = BACK_ZMASK;
-            b.n_bins = P.back_bins;
-            b.net = const_cast<float*>(f.mask);
-            b.net_chunk_stride = f.mask_chunk_stride;
-            b.zspec = D.zspec + (int64_t)b0 * P.z_per_chunk();
-            b.z_chunk_stride = P.z_per_chunk();
-            b.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
-            cuda_check(stg::launch_back(b, st), "back kernel launch");
-        } else {
-            cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
-        }
-        if (timing) timing->launches++;
-        if (opt && opt->on_progress) {
-            cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
-            opt->on_progress(opt->user, b0 + nb, G);
+            done += nb;
+            if (opt && opt->on_progress) {
+                cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
+                opt->on_progress(opt->user, done, total);
+            }
         }
     }
     CombineParams c{};
     c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
     c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
-    c.chunks = D.chunks; c.n_chunks = G;
+    c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
     c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
     c.step_out = P.step_out; c.max_out_len = P.max_out_len;
     c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
     c.W = D.W;
     c.S = P.S; c.C = P.C; c.len = P.len;
+    c.i_begin = sample_begin; c.i_end = sample_end;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
     c.mono_stats = P.mono_norm ? D.mono : nullptr;
@@ -749,6 +789,7 @@ void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, f
     c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
     c.W = D.W;
     c.S = P.S; c.C = P.C; c.len = P.arch_out_len();
+    c.i_begin = 0; c.i_end = c.len;
     c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
     c.complement = P.complement; c.mix = d_mix; c.out = d_out;
     c.mono_stats = P.mono_norm ? D.mono : nullptr;

@@ -137,8 +137,11 @@ struct RunTiming {
 
 // Run a separation on device buffers with the plan's device tables: the fused kernel over
 // chunk batches (progress and cancellation between batches), then the combine.
+// With a sample range, only the chunks reaching output samples [sample_begin, sample_end) run
+// and only those samples of every output row are written (end < 0: the whole track).
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
-                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing);
+                 float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
+                 int64_t sample_begin = 0, int64_t sample_end = -1);
 
 // The halves around a real network, on chunks [first, first + n): the front writes the
 // network's input (net_in_per_chunk floats per chunk) into d_net_in; the back reads its

@@ -184,3 +184,38 @@ def test_misaligned_mask_is_rejected(pkg, engine):
         plan.separate(torch.zeros((2, n), device="cuda"), mask[1:], torch.empty(plan.out_shape, device="cuda"))
     assert e.value.code == 1 and "aligned" in str(e.value)
 
+
+# ---- a track split by output samples (stg_separate_part) -----------------------------------------
+def _parts_equal_whole(pkg, plan, mix, mask, parts):
+    import torch
+    d_mix, d_mask = torch.from_numpy(mix).cuda(), torch.from_numpy(mask).cuda()
+    whole = torch.empty(plan.out_shape, device="cuda")
+    plan.separate(d_mix, d_mask, whole)
+    split = torch.full(plan.out_shape, float("nan"), device="cuda")
+    for r in range(parts):
+        b, e = pkg.sharding.sample_range_for_rank(plan.n_samples, r, parts)
+        plan.separate_part(d_mix, d_mask, split, b, e)
+    torch.cuda.synchronize()
+    assert torch.equal(split, whole)
+
+
+@pytest.mark.parametrize("shifts", [0, 2])
+def test_roformer_parts_equal_whole(pkg, engine, shifts):
+    sizes, freqs = pkg.bands.mel_bands()
+    n = 441 * 200 + 77
+    plan = engine.plan_roformer(n, sizes, freqs, chunk=441 * 40, num_overlap=4, complement=True, shifts=shifts,
+                                seed=4)
+    _parts_equal_whole(pkg, plan, synth_audio(93, n), synth_mask(94, plan.mask_floats, 0.5), 3)
+
+
+def test_htdemucs_parts_equal_whole(pkg, engine):
+    n = 1024 * 24 * 5 + 123
+    plan = engine.plan_htdemucs(n, n_sources=4, segment=1024 * 24)
+    _parts_equal_whole(pkg, plan, synth_audio(95, n), synth_mask(96, plan.mask_floats, 1.0), 4)
+
+
+def test_tfc_parts_equal_whole(pkg, engine):
+    n = 120000
+    plan = engine.plan_tfc(n, dim_t=32, overlap=0.5, compensate=1.009, complement=True)
+    _parts_equal_whole(pkg, plan, synth_audio(97, n), synth_mask(98, plan.mask_floats, 1.0), 2)
+

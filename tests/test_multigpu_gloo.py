@@ -44,6 +44,14 @@ def _worker(rank, world, port, n_tracks, length, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("n,world", [(1000, 1), (1000, 3), (7, 8), (2646000, 8)])
+def test_sample_ranges_tile_the_track(pkg, n, world):
+    got = [pkg.sharding.sample_range_for_rank(n, r, world) for r in range(world)]
+    assert got[0][0] == 0 and got[-1][1] == n
+    assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
+    assert max(e - b for b, e in got) - min(e - b for b, e in got) <= 1
+
+
 def test_round_robin_split_covers_every_track_once(pkg):
     world, n = 3, 10
     got = sorted(k for r in range(world) for k in pkg.sharding.tracks_for_rank(n, r, world))
