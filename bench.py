@@ -665,6 +665,9 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
     if world > 1:
+        # stdout carries the one JSON line: keep NCCL's version banner off it unless asked for
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
