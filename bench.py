@@ -2,7 +2,8 @@
 """bench.py -- throughput of the B200 spectral path (chunking -> STFT -> mask -> iSTFT -> OLA).
 
 Metric: audio-seconds per second of the whole separation, whole job over
-all GPUs; plus the fused kernel's achieved HBM bandwidth against the measured peak.
+all GPUs; plus the dominant kernel's achieved HBM bandwidth against the measured peak (the
+fused kernel for RoFormer and TFC-TDF, the back kernel for HTDemucs).
 
 Workload (default ``cfg1``, the headline configuration): Mel-Band RoFormer (Kim) front/back
 end on 60 s of seeded stereo 44.1 kHz audio: chunks of 352800 samples, num_overlap 4
@@ -10,11 +11,13 @@ end on 60 s of seeded stereo 44.1 kHz audio: chunks of 352800 samples, num_overl
 band-bin entries, duplicates averaged), complex mask N(0, 0.5) in the network's band-major
 layout, iSTFT, windowed overlap-add across chunks. One step = one such track. The mask
 (913 MB) and the mix are resident in HBM before the timed region; they exceed the 126 MB
-L2, so no flush is needed between steps. Other workloads: cfg0, cfg2, cfg3 (see WORKLOADS).
+L2, so no flush is needed between steps. Other workloads: cfg0, cfg2, cfg3, cfg4 (the
+BASELINE configurations), vr3band and io48k (see WORKLOADS).
 
 Multi-GPU (torchrun, one process per GPU): every rank separates its own track; there is no
 data-path collective (weak scaling). NCCL is used only for the barrier and the max-over-
-ranks of the device-timed duration.
+ranks of the device-timed duration. ``--split-track`` splits one track's output samples
+across the ranks instead (strong scaling, still without an exchange).
 
 ``--impl reference`` times the reference's CPU implementation of the same path on this
 box's host cores (rank 0 only): the reference's own stft.h compiled from its sources
