@@ -194,8 +194,18 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             if constexpr (FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t_begin, tid);
         }
         __syncthreads();
+        // TFC-TDF: frame t's mask row (dim_f float4, 16-byte aligned) requested from L2 a frame
+        // before its loads
+        const auto mask_row_to_l2 = [&](int t) {
+            if constexpr (ARCH == ARCH_TFC && FftCfg<N>::MASK_L2)
+                if (tid == 0 && t < t_end)
+                    prefetch_l2(p.mask + (int64_t)ci * p.mask_chunk_stride + ((int64_t)s * G.T + t) * p.dim_f * 4,
+                                (unsigned)p.dim_f * 16u);
+        };
+        mask_row_to_l2(t_begin);
         for (int t = t_begin; t < t_end; t++) {
             const int q0 = G.first_pos + t * hop;
+            mask_row_to_l2(t + 1);
             // forward pass 1: windowed frame straight from the input ring
             pass_io<N, R1, 1, T, false, false>(
                 tw, tid,

@@ -757,7 +757,7 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
         f.chunks = D.chunks + first; f.n_chunks = n;
         f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
         f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
-    f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
+        f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
         f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
         f.mask = d_net_out; f.mask_chunk_stride = P.mask_per_chunk;
         f.bin_tab = D.btab; f.bin_multi = P.bin_multi;
