@@ -111,6 +111,9 @@ struct stg_plan {
     ~stg_plan() {
         for (cudaEvent_t& e : timing.ev)
             if (e) cudaEventDestroy(e);
+        if (D.fork) cudaEventDestroy(D.fork);
+        if (D.join) cudaEventDestroy(D.join);
+        if (D.side) cudaStreamDestroy(D.side);
     }
 
     // Device copies of the tables, and the scratch the fused kernel writes.
@@ -140,6 +143,11 @@ struct stg_plan {
         if (H.mask_planes) {
             d_mask_t.reserve(H.mask_t_bytes(), "t-major masks");
             D.mask_t = reinterpret_cast<float4*>(d_mask_t.p);
+            if (H.z_per_chunk() && !D.side) {
+                cuda_check(cudaStreamCreateWithFlags(&D.side, cudaStreamNonBlocking), "cudaStreamCreate");
+                cuda_check(cudaEventCreateWithFlags(&D.fork, cudaEventDisableTiming), "cudaEventCreate");
+                cuda_check(cudaEventCreateWithFlags(&D.join, cudaEventDisableTiming), "cudaEventCreate");
+            }
         }
         if (H.cac_norm) {
             d_cac_part.reserve(H.cac_part_bytes(), "CaC partial sums");

@@ -532,7 +532,8 @@ cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st) {
 
 // ---- mask transposition -------------------------------------------------------------------
 // f-major planes [S][P][F][T] per chunk (t fastest) -> t-major [S][T][F] float4 per chunk,
-// component p = plane p (zero from P up). One CTA moves a 32 x 32 (f, t) tile of every plane:
+// component p = plane p (zero from P up). A CTA moves 32 x 32 (f, t) tiles of every plane,
+// work item w = ((chunk * S + stem) * f tiles + f tile) * t tiles + t tile, striding by the grid:
 // rows read 32 consecutive t (128 bytes), rows written 32 consecutive f (512 bytes of float4).
 constexpr int kTile = 32;
 
@@ -541,8 +542,13 @@ __global__ void __launch_bounds__(256) mask_transpose(const float* __restrict__ 
                                                       float4* __restrict__ out, int64_t out_chunk_stride) {
     __shared__ float tile[4][kTile][kTile + 1];
     const int lx = threadIdx.x & 31, ly = threadIdx.x >> 5;
-    const int f0 = blockIdx.y * kTile, t0 = blockIdx.x * kTile;
-    for (int cs = blockIdx.z; cs < n_cs; cs += gridDim.z) {
+    const int ntx = (T + kTile - 1) / kTile, nty = (F + kTile - 1) / kTile;
+    const int64_t n_work = (int64_t)ntx * nty * n_cs;
+    for (int64_t w = blockIdx.x; w < n_work; w += gridDim.x) {
+        const int tx = (int)(w % ntx);
+        const int64_t rest = w / ntx;
+        const int ty = (int)(rest % nty), cs = (int)(rest / nty);
+        const int f0 = ty * kTile, t0 = tx * kTile;
         const int ci = cs / S, s = cs - ci * S;
         const float* src = in + ci * in_chunk_stride + (int64_t)s * P * F * T;
         // all 16 loads of a thread in flight before the first shared-memory store
@@ -570,12 +576,14 @@ __global__ void __launch_bounds__(256) mask_transpose(const float* __restrict__ 
 }
 
 cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int n_chunks, int S, int P, int F,
-                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st) {
+                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st, int max_ctas) {
     if (n_chunks <= 0) return cudaSuccess;
     if (P < 1 || P > 4 || F < 1 || T < 1 || S < 1) return cudaErrorInvalidValue;
     const int n_cs = n_chunks * S;
-    const dim3 grid((T + kTile - 1) / kTile, (F + kTile - 1) / kTile, std::min(n_cs, 65535));
-    mask_transpose<<<grid, 256, 0, st>>>(in, in_chunk_stride, n_cs, S, P, F, T, out, out_chunk_stride);
+    const int64_t n_work = (int64_t)((T + kTile - 1) / kTile) * ((F + kTile - 1) / kTile) * n_cs;
+    int64_t blocks = std::min<int64_t>(n_work, INT32_MAX);
+    if (max_ctas > 0) blocks = std::min<int64_t>(blocks, max_ctas);
+    mask_transpose<<<(unsigned)blocks, 256, 0, st>>>(in, in_chunk_stride, n_cs, S, P, F, T, out, out_chunk_stride);
     return cudaGetLastError();
 }
 

@@ -191,8 +191,10 @@ cudaError_t launch_back(const SplitParams& p, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 // f-major mask planes [S][P][F][T] per chunk (in_chunk_stride floats apart) -> t-major
 // [S][T][F] float4 per chunk (out_chunk_stride float4 apart), plane p in component p.
+// max_ctas > 0 caps the grid (the CTAs stride over the tiles), leaving room on the SMs for
+// a kernel that runs beside it.
 cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int n_chunks, int S, int P, int F,
-                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st);
+                                  int T, float4* out, int64_t out_chunk_stride, cudaStream_t st, int max_ctas = 0);
 size_t fused_smem_bytes(int arch, int n_fft);
 int fused_threads(int n_fft);
 int fused_max_hop(int n_fft);      // the largest hop the fused kernel takes at this n_fft

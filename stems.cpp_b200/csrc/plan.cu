@@ -584,9 +584,26 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     const bool timed = timing && timing->timed;
     if (timing) timing->launches = 0;
     if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
+    const bool zpath = P.z_per_chunk() > 0;   // HTDemucs: spectra once, then the back kernel per stem
+    // HTDemucs: the masks' transposition (HBM-bound) on the side stream, beside the
+    // normalisation and the front kernel (latency-bound); every segment has its own slot of
+    // the scratch. The fork orders it after the caller's earlier work, including the previous
+    // separation's back kernels, which read the same scratch.
+    const bool side_t = zpath && P.mask_planes && D.side;
+    // the caller's stream waits for the side stream before anything after this point,
+    // the back kernels, or a failure, can hand the masks back to the caller
+    struct Join {
+        cudaStream_t st = nullptr;
+        cudaEvent_t ev = nullptr;
+        void now() {
+            if (ev) cudaStreamWaitEvent(st, ev, 0);
+            ev = nullptr;
+        }
+        ~Join() { now(); }
+    } join;
     const float* d_mix = normalise_mix(P, D, d_mix_in, st);
     if (timing && P.mono_norm) timing->launches += 5;
-    const bool zpath = P.z_per_chunk() > 0;   // HTDemucs: spectra once, then the back kernel per stem
+    if (side_t) cuda_check(cudaEventRecord(D.fork, st), "cudaEventRecord");
     for (const auto& rg : ranges) {
         const int c0 = rg.first, G = rg.second - rg.first;
         if (zpath) {
@@ -614,6 +631,21 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             if (timing) timing->launches += k;
         }
     }
+    if (side_t) {
+        if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
+        cuda_check(cudaStreamWaitEvent(D.side, D.fork, 0), "cudaStreamWaitEvent");
+        for (const auto& rg : ranges) {
+            cuda_check(launch_mask_transpose(d_mask + (int64_t)rg.first * P.mask_per_chunk, P.mask_per_chunk,
+                                             rg.second - rg.first, P.S, P.mask_planes, P.mask_bins, P.g.T,
+                                             D.mask_t + (int64_t)rg.first * P.mask_t_per_chunk(),
+                                             P.mask_t_per_chunk(), D.side),
+                       "mask transposition launch");
+            if (timing) timing->launches++;
+        }
+        cuda_check(cudaEventRecord(D.join, D.side), "cudaEventRecord");
+        join.st = st;
+        join.ev = D.join;
+    }
     FusedParams f{};
     f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
     f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
@@ -639,7 +671,11 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             f.mask_chunk_stride = P.mask_per_chunk;
             f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
             f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
-            if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
+            if (side_t) {   // transposed on the side stream
+                join.now();
+                f.mask = reinterpret_cast<const float*>(D.mask_t + (int64_t)b0 * P.mask_t_per_chunk());
+                f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
+            } else if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
                 if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
                 cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins,
                                                  P.g.T, D.mask_t, P.mask_t_per_chunk(), st),

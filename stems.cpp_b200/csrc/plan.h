@@ -110,6 +110,11 @@ struct PlanDevice {
     double2* cac_stats = nullptr;  // scratch: per-chunk CaC (mean, std)
     float4* mask_t = nullptr;      // scratch: t-major masks (HostPlan::mask_planes)
     float4* zspec = nullptr;       // scratch: HTDemucs spectra (HostPlan::z_per_chunk)
+    // HTDemucs: a second stream on which every segment's mask transposition runs beside the
+    // normalisation and the front kernel, joined before the first back kernel (null: the
+    // transpositions run in order on the caller's stream)
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
