@@ -21,14 +21,15 @@ namespace stg {
 
 namespace {
 
-// The spectra of bin f (zl, zr) to the front layout, frame t of chunk ci.
-template <int N>
+// The spectra of bin f (zl, zr) to the front layout, frame t of chunk ci. L: the layout, or
+// -1 to read it from p.layout.
+template <int N, int L>
 __device__ __forceinline__ void front_store(const SplitParams& p, const int2* btab, int ci, int t, int f,
                                             float2 zl, float2 zr) {
     const int T = p.g.T, C = p.n_channels;
     float* out = p.net + (int64_t)ci * p.net_chunk_stride;
     const int64_t plane = (int64_t)p.n_bins * T, idx = (int64_t)f * T + t;
-    switch (p.layout) {
+    switch (L >= 0 ? L : p.layout) {
         case FRONT_COMPLEX:
             if (f < p.n_bins) {
                 reinterpret_cast<float2*>(out)[idx] = zl;
@@ -144,8 +145,14 @@ __device__ __forceinline__ void zmask_apply(const SplitParams& p, int ci, float4
     }
 }
 
-template <int N>
-__global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p) {
+// The CTAs per SM the HTDemucs segment-spectra instance (FRONT_ZSPEC) aims its registers at
+// (two: at three, the 80-register cap spills and the separation is slower); 0 leaves the
+// other instances to the compiler's default, which an explicit 1 would raise by 30-70 registers.
+template <int N, int L> constexpr int front_minb() { return L == FRONT_ZSPEC && N == 4096 ? 2 : 0; }
+
+// L: the layout (the HTDemucs FRONT_ZSPEC instance), or -1 to read it from p.layout.
+template <int N, int L>
+__global__ void __launch_bounds__(FftCfg<N>::T, (front_minb<N, L>())) front_kernel(const SplitParams p) {
     constexpr int T = FftCfg<N>::T;
     using Plan = typename FftCfg<N>::Plan;
     constexpr int R1 = Head<Plan>::first;
@@ -210,20 +217,26 @@ __global__ void __launch_bounds__(FftCfg<N>::T) front_kernel(const SplitParams p
                 }
             }
             passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
-            for (int f = tid; f < p.n_bins && f <= N / 2; f += T) {
-                const int fm = f == 0 ? 0 : N - f;
-                const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
-                const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
-                const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
-                if (p.stats_out && f < p.n_bins) {
-                    acc_s += (double)zl.x + (double)zl.y;
-                    acc_q += (double)zl.x * zl.x + (double)zl.y * zl.y;
-                    if (C > 1) {
-                        acc_s += (double)zr.x + (double)zr.y;
-                        acc_q += (double)zr.x * zr.x + (double)zr.y * zr.y;
+            // the thread's bins f = tid + i*T (the FRONT_ZSPEC instance unrolls over its slots)
+            constexpr int BPT = L == FRONT_ZSPEC ? (N / 2 + T) / T : 1;
+#pragma unroll
+            for (int i = 0; i < BPT; i++) {
+                for (int f = tid + i * T; f < p.n_bins && f <= N / 2; f += BPT * T) {
+                    const int fm = f == 0 ? 0 : N - f;
+                    const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
+                    const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
+                    const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
+                    if (p.stats_out && f < p.n_bins) {
+                        acc_s += (double)zl.x + (double)zl.y;
+                        acc_q += (double)zl.x * zl.x + (double)zl.y * zl.y;
+                        if (C > 1) {
+                            acc_s += (double)zr.x + (double)zr.y;
+                            acc_q += (double)zr.x * zr.x + (double)zr.y * zr.y;
+                        }
                     }
+                    if (L == FRONT_ZSPEC || (L < 0 && p.layout != FRONT_STATS)) front_store<N, L>(p, btab, ci, t, f, zl, zr);
+                    if constexpr (L == FRONT_ZSPEC) break;
                 }
-                if (p.layout != FRONT_STATS) front_store<N>(p, btab, ci, t, f, zl, zr);
             }
             __syncthreads();
         }
@@ -377,8 +390,12 @@ cudaError_t launch_persistent(K kernel, int threads, size_t smem, int64_t items,
 }
 
 template <int N> cudaError_t front_t(const SplitParams& p, cudaStream_t st) {
-    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N) + sizeof(int2) * (size_t)(N / 2 + 2);
-    return launch_persistent(front_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
+    const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N);   // frame and input ring
+    const int64_t items = (int64_t)p.n_tiles * p.n_chunks;
+    if constexpr (N == 4096)
+        if (p.layout == FRONT_ZSPEC)
+            return launch_persistent(front_kernel<N, FRONT_ZSPEC>, FftCfg<N>::T, smem, items, st, p);
+    return launch_persistent(front_kernel<N, -1>, FftCfg<N>::T, smem + sizeof(int2) * (size_t)(N / 2 + 2), items, st, p);
 }
 template <int N> cudaError_t back_t(const SplitParams& p, cudaStream_t st) {
     const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N) + sizeof(float) * (size_t)(N / 2);
