@@ -410,6 +410,148 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     }
 }
 
+// Stereo rows, V = 4 consecutive output samples per thread: the same sums in the same order as
+// combine_kernel (so the same floats), with the group and chunk bookkeeping (the divisions
+// by the chunk step, the chunk table loads, the tile of each sample) done once per four
+// samples; the tile of the next sample is the previous one's advanced by one. Every load
+// address is clamped into its table or buffer, so that a load the compiler issues ahead of
+// its sample's guard (the four samples are unrolled) still reads memory the plan owns: the
+// first unguarded version faulted on RoFormer plans, whose first chunk starts before sample 0.
+constexpr int kCombineV = 4;
+
+template <int SC>
+__global__ void __launch_bounds__(256) combine_kernel4(const CombineParams p) {
+    constexpr int V = kCombineV;
+    const int64_t il = p.i_begin + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * V;
+    if (il >= p.i_end) return;
+    const int i0 = (int)il;
+    const int nv = (int)min((int64_t)V, p.i_end - il);
+    const FrameGeom& G = p.g;
+    const int step = (int)p.step_out;
+    const int span = p.K * G.hop, ov = G.n_fft - G.hop;
+    float res[V][SC];
+#pragma unroll
+    for (int s = 0; s < V; s++)
+#pragma unroll
+        for (int k = 0; k < SC; k++) res[s][k] = 0.0f;
+    for (int gi = 0; gi < p.n_groups; gi++) {
+        const ChunkGroup grp = p.groups[gi];
+        const int P0 = i0 + grp.out_shift;
+        const int out00 = (int)p.chunks[grp.c0].out0;
+        const int n = grp.c1 - grp.c0;
+        // the union of the four samples' chunk ranges of combine_kernel
+        const int ghi = min((P0 + V - 1 - out00) / step, n - 1);
+        const int glo = max((P0 - out00 - (int)p.max_out_len) / step, 0);
+        float acc[V][SC];
+        float wsum[V];
+#pragma unroll
+        for (int s = 0; s < V; s++) {
+            wsum[s] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < SC; k++) acc[s][k] = 0.0f;
+        }
+        for (int gl = glo; gl <= ghi + 1 && gl < n; gl++) {
+            const int g = grp.c0 + gl;
+            const ChunkDesc& d = p.chunks[g];
+            const int u0 = P0 - (int)d.out0, olen = d.out_len;
+            if (olen <= 0 || u0 + V <= 0 || u0 >= olen) continue;
+            const float* Wg = p.W + d.w_off;
+            const float* yg = p.Y + (int64_t)g * p.y_chunk_stride;
+            const float* tg = p.Tr + (int64_t)g * p.tr_chunk_stride;
+            const int j0 = d.y_off + u0;
+            const int q0 = j0 + G.out_offset - G.first_pos;
+            const int tau0 = q0 / span, uu0 = q0 - tau0 * span;
+#pragma unroll
+            for (int s = 0; s < V; s++) {
+                const int u = u0 + s;
+                if (s >= nv || u < 0 || u >= olen) continue;
+                // the tile boundary region of sample s (q0 + s), as q / span would give it
+                int tau, uu;
+                if (q0 >= 0) {
+                    tau = tau0;
+                    uu = uu0 + s;
+                    if (uu >= span) { uu -= span; tau++; }
+                } else {
+                    tau = (q0 + s) / span;
+                    uu = q0 + s - tau * span;
+                }
+                const int uc = min(max(u, 0), olen - 1);   // = u here; clamped for the address
+                const float w = __ldg(Wg + uc);
+                wsum[s] += w;
+                const float2* y = reinterpret_cast<const float2*>(yg) + (d.y_off + uc);
+                const bool has_tr = tau >= 1 && tau < p.n_tiles && uu < ov;
+                const int tc = min(max(tau, 1), p.n_tiles) - 1, uc2 = min(max(uu, 0), ov - 1);
+                const float2* tr = reinterpret_cast<const float2*>(tg + (int64_t)tc * SC * ov) + uc2;
+#pragma unroll
+                for (int st = 0; st < SC / 2; st++) {
+                    float2 v = __ldg(y + (int64_t)st * G.Lout);
+                    if (has_tr) {
+                        const float2 r = __ldg(tr + st * ov);
+                        v = make_float2(v.x + r.x, v.y + r.y);
+                    }
+                    acc[s][2 * st] = fmaf(w, v.x, acc[s][2 * st]);
+                    acc[s][2 * st + 1] = fmaf(w, v.y, acc[s][2 * st + 1]);
+                }
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < V; s++) {
+            const float inv = 1.0f / wsum[s];
+#pragma unroll
+            for (int k = 0; k < SC; k++) {
+                float v = acc[s][k] * inv;
+                if (p.nan_to_zero && !isfinite(v)) v = 0.0f;
+                res[s][k] += p.shift_mean == 2 ? v / (float)p.n_groups : v;
+            }
+        }
+    }
+    float outv[V][SC];
+#pragma unroll
+    for (int s = 0; s < V; s++)
+#pragma unroll
+        for (int k = 0; k < SC; k++) {
+            float v = p.shift_mean == 1 ? res[s][k] / (float)p.n_groups : res[s][k];
+            v *= p.compensate;
+            if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
+            outv[s][k] = v;
+        }
+    // rows of 4 samples as one 16-byte store where the row offset allows it
+    const bool vec = nv == V && (p.len % V) == 0 && (i0 % V) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.out) % (sizeof(float) * V)) == 0;
+    const auto put = [&](int row, const float (&v)[V]) {
+        float* o = p.out + (int64_t)row * p.len + i0;
+        if (vec) {
+            *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int s = 0; s < V; s++)
+                if (s < nv) o[s] = v[s];
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < SC; k++) {
+        float v[V];
+#pragma unroll
+        for (int s = 0; s < V; s++) v[s] = outv[s][k];
+        put(k, v);
+    }
+    if (p.complement) {
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            float v[V];
+#pragma unroll
+            for (int s = 0; s < V; s++) {
+                const float m = __ldg(p.mix + (int64_t)c * p.len + i0 + min(s, nv - 1));
+                v[s] = s < nv ? m : 0.0f;
+#pragma unroll
+                for (int k = 0; k < SC; k++)
+                    if (k % 2 == c && (p.complement == 2 || k < 2)) v[s] -= outv[s][k];
+            }
+            put(SC + c, v);
+        }
+    }
+}
+
 // ---- launchers ----------------------------------------------------------------------------
 bool fused_supported(int n) { return n == 2048 || n == 4096 || n == 7680; }
 
@@ -590,6 +732,14 @@ cudaError_t launch_mask_transpose(const float* in, int64_t in_chunk_stride, int 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
     if (p.i_end <= p.i_begin) return cudaSuccess;
     const int threads = 256;
+    if (p.C == 2 && p.S <= 2) {   // one or two stereo stems: four samples per thread (from
+        // three stems up, its registers cost more occupancy than the shared bookkeeping saves)
+        const int64_t per = (int64_t)threads * kCombineV;
+        const unsigned b4 = (unsigned)((p.i_end - p.i_begin + per - 1) / per);
+        if (p.S == 1) combine_kernel4<2><<<b4, threads, 0, st>>>(p);
+        else combine_kernel4<4><<<b4, threads, 0, st>>>(p);
+        return cudaGetLastError();
+    }
     const unsigned blocks = (unsigned)((p.i_end - p.i_begin + threads - 1) / threads);
     switch (p.S * p.C) {
         case 1: combine_kernel<1><<<blocks, threads, 0, st>>>(p); break;
