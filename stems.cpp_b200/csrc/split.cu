@@ -257,8 +257,9 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (front_minb<N, L>())) front_kern
     }
 }
 
+// n_fft 4096 (HTDemucs): registers capped for three CTAs per SM, which its shared memory allows
 template <int N>
-__global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p) {
+__global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel(const SplitParams p) {
     constexpr int T = FftCfg<N>::T;
     using Plan = typename FftCfg<N>::Plan;
     using InvInit = typename Init<Plan>::type;
@@ -272,6 +273,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
     const FrameGeom& G = p.g;
     const int hop = G.hop, C = p.n_channels;
     for (int i = tid; i < N; i += T) out_ring[i] = make_float2(0.f, 0.f);
+    // the window (times the inverse scale) at the samples this thread overlap-adds, tid + r*NSL,
+    // in registers when the last pass has one butterfly per thread
+    constexpr bool RW = N / RL == T;
+    float wreg[RW ? RL : 1];
+#pragma unroll
+    for (int r = 0; r < (RW ? RL : 1); r++) wreg[r] = RW ? __ldg(p.win + tid + r * NSL) * p.inv_scale : 0.0f;
     const bool env_on = p.env_period != nullptr;
     if (env_on)
         for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
@@ -285,6 +292,16 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
             float* Trs = p.Tr + (int64_t)ci * p.tr_chunk_stride + ((int64_t)tile * p.S + s) * C * (N - hop);
             for (int t = t_begin; t < t_end; t++) {
                 const int q0 = G.first_pos + t * hop;
+                // BACK_ZMASK: the next frame's Z and mask rows (contiguous, 16-byte aligned) asked
+                // of L2 a frame ahead (cfg4's back kernel 1.41 -> 1.28 ms)
+                if (p.layout == BACK_ZMASK && tid == 0) {
+                    const int tn = t + 1 < t_end ? t + 1 : t_begin, sn = t + 1 < t_end ? s : s + 1;
+                    if (sn < p.S) {
+                        const unsigned bytes = (unsigned)p.n_bins * 16u;
+                        if (tn != t) prefetch_l2(p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)tn * p.n_bins, bytes);
+                        prefetch_l2(p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)sn * G.T + tn) * p.n_bins, bytes);
+                    }
+                }
                 auto pack = [&](int f, float2 yl, float2 yr) {
                     if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
                     const int fm = f == 0 ? 0 : N - f;
@@ -331,7 +348,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T) back_kernel(const SplitParams p)
                     tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                     [&](int base, int r, float2 v) {
                         const int n = base + r * NSL;
-                        const float w = __ldg(p.win + n) * p.inv_scale;
+                        const float w = RW ? wreg[r] : __ldg(p.win + n) * p.inv_scale;
                         float2& o = out_ring[ring_slot<N>(q0 + n)];
                         o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
                     });
