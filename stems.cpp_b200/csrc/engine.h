@@ -104,6 +104,11 @@ struct stg_plan {
     DevBuf d_zspec;                                   // HTDemucs spectra
     const float* mono_src = nullptr;                  // the track d_mixn was normalised from
     DevBuf s_mix, s_mask, s_out;   // device staging for stg_separate_host
+    // stg_separate_host: a copy stream that brings the masks in batch by batch, and the events
+    // the batches' kernels wait for
+    cudaStream_t copy_st = nullptr;
+    cudaEvent_t copy_fork = nullptr;
+    std::vector<cudaEvent_t> copy_ev;
     DevBuf dm_out;                 // one channel's result (stg_separate_dual_mono)
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
@@ -114,6 +119,10 @@ struct stg_plan {
         if (D.fork) cudaEventDestroy(D.fork);
         if (D.join) cudaEventDestroy(D.join);
         if (D.side) cudaStreamDestroy(D.side);
+        for (cudaEvent_t e : copy_ev)
+            if (e) cudaEventDestroy(e);
+        if (copy_fork) cudaEventDestroy(copy_fork);
+        if (copy_st) cudaStreamDestroy(copy_st);
     }
 
     // Device copies of the tables, and the scratch the fused kernel writes.
@@ -171,7 +180,7 @@ struct stg_plan {
     }
 
     void run(const float* d_mix, const float* d_mask, float* d_out, cudaStream_t st, const stg_run_options* opt,
-             int64_t sample_begin = 0, int64_t sample_end = -1) {
+             int64_t sample_begin = 0, int64_t sample_end = -1, const BatchHook* before_batch = nullptr) {
         if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
         H.check_mask(d_mask);
         cuda_check(cudaSetDevice(engine->device), "cudaSetDevice");
@@ -179,7 +188,7 @@ struct stg_plan {
         if (timing.timed)
             for (cudaEvent_t& e : timing.ev)
                 if (!e) cuda_check(cudaEventCreate(&e), "cudaEventCreate");
-        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing, sample_begin, sample_end);
+        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing, sample_begin, sample_end, before_batch);
     }
 
     // The mix the front half reads: with the mono normalisation, chunk 0's call normalises

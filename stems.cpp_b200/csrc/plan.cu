@@ -570,7 +570,7 @@ std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_
 
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
-                 int64_t sample_begin, int64_t sample_end) {
+                 int64_t sample_begin, int64_t sample_end, const BatchHook* before_batch) {
     if (!d_mix_in || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
     P.check_mask(d_mask);
     if (sample_end < 0) sample_end = P.len;
@@ -665,6 +665,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         for (int b0 = rg.first; b0 < rg.second; b0 += per) {
             if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
             const int nb = std::min(per, rg.second - b0);
+            if (before_batch) (*before_batch)(b0, nb);
             f.chunks = D.chunks + b0;
             f.n_chunks = nb;
             f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;

@@ -153,6 +153,20 @@ def test_deterministic_and_host_entry(pkg, engine):
     c = plan.separate_host(mix, mask)
     assert np.array_equal(a, b), "two runs differ bitwise"
     assert np.array_equal(a, c), "host entry point differs from the device one"
+    assert np.array_equal(a, plan.separate_host(mix, mask)), "second host call differs"
+
+
+def test_host_entry_tfc_batches(pkg, engine):
+    """The host entry point brings the masks in batch by batch (the TFC-TDF ones transposed per
+    batch): the same floats as the device entry point, call after call."""
+    length = 44100 * 8 + 17
+    plan = engine.plan_tfc(length, dim_t=32, complement=True)
+    assert plan.n_chunks >= 9
+    mix = synth_audio(43, length)
+    mask = synth_mask(44, plan.mask_floats, 1.0)
+    a = run_gpu(plan, mix, mask)
+    for _ in range(2):
+        assert np.array_equal(a, plan.separate_host(mix, mask))
 
 
 # ---- DualMono (src/separator.cpp:15-47) ----------------------------------------------------------
