@@ -4,7 +4,9 @@
 //
 //   mono-mix normalisation (src/htdemucs.cpp:539-549, 638-642): mono = mean over channels
 //     (rounded to float), mean and unbiased std over the track in double, std at least 1e-8;
-//     the mix becomes (x - mean) / std and every stem v / 1 * std + mean.
+//     the mix becomes (x - mean) / std and every stem v / 1 * std + mean. One pass sums mono
+//     and mono^2 in double; the variance is (sum sq - sum * mean) / (n - 1), which for audio
+//     (|mono| <= 1, n < 2^29) agrees with the reference's second pass to about 1e-15.
 //   CaC normalisation (src/htdemucs.cpp:434-436, 466-469): mean and unbiased std over all
 //     2C x F x T spectrogram values of a segment; the network sees (v - mean) / (1e-5 + std)
 //     and its output is mapped back by v * std + mean.
@@ -17,14 +19,17 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kBlocks = 512;
 
-__device__ __forceinline__ double block_sum(double v, double* red) {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+__device__ __forceinline__ double2 block_sum2(double2 v, double2* red) {
+    for (int o = 16; o > 0; o >>= 1) {
+        v.x += __shfl_down_sync(0xffffffffu, v.x, o);
+        v.y += __shfl_down_sync(0xffffffffu, v.y, o);
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (lane == 0) red[warp] = v;
     __syncthreads();
-    double s = 0.0;
+    double2 s = make_double2(0.0, 0.0);
     if (threadIdx.x == 0)
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) { s.x += red[w].x; s.y += red[w].y; }
     __syncthreads();
     return s;   // valid in thread 0
 }
@@ -35,35 +40,38 @@ __device__ __forceinline__ float mono_at(const float* mix, int64_t len, int C, i
     return (float)(s / C);
 }
 
-// pass 0: partial sums of mono; pass 1: partial sums of (mono - mean)^2 (mean from stats[0]).
+// Per block: the partial sums of mono and of mono^2.
 __global__ void __launch_bounds__(kThreads) mono_partials(const float* __restrict__ mix, int64_t len, int C,
-                                                          int pass, const double* __restrict__ stats,
-                                                          double* __restrict__ partial) {
-    __shared__ double red[kThreads / 32];
-    const double mean = pass ? stats[0] : 0.0;
-    double acc = 0.0;
+                                                          double2* __restrict__ partial) {
+    __shared__ double2 red[kThreads / 32];
+    double2 acc = make_double2(0.0, 0.0);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (int64_t)gridDim.x * blockDim.x) {
         const double m = mono_at(mix, len, C, i);
-        acc += pass ? (m - mean) * (m - mean) : m;
+        acc.x += m;
+        acc.y = fma(m, m, acc.y);
     }
-    const double s = block_sum(acc, red);
+    const double2 s = block_sum2(acc, red);
     if (threadIdx.x == 0) partial[blockIdx.x] = s;
 }
 
-// Sums the kBlocks partials by a fixed tree (one block of kBlocks threads): pass 0 writes the
-// mean, pass 1 the std (at least 1e-8).
-__global__ void __launch_bounds__(kBlocks) mono_finish(const double* __restrict__ partial, int64_t len, int pass,
+// Sums the kBlocks partials by a fixed tree (one block of kBlocks threads) and writes the mean
+// and the std (at least 1e-8).
+__global__ void __launch_bounds__(kBlocks) mono_finish(const double2* __restrict__ partial, int64_t len,
                                                        double* stats) {
-    __shared__ double s[kBlocks];
+    __shared__ double2 s[kBlocks];
     s[threadIdx.x] = partial[threadIdx.x];
     __syncthreads();
     for (int o = kBlocks / 2; o > 0; o >>= 1) {
-        if ((int)threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o];
+        if ((int)threadIdx.x < o) {
+            s[threadIdx.x].x += s[threadIdx.x + o].x;
+            s[threadIdx.x].y += s[threadIdx.x + o].y;
+        }
         __syncthreads();
     }
     if (threadIdx.x != 0) return;
-    if (pass == 0) stats[0] = s[0] / (double)len;
-    else stats[1] = fmax(sqrt(s[0] / (double)(len - 1)), 1e-8);
+    const double mean = s[0].x / (double)len;
+    stats[0] = mean;
+    stats[1] = fmax(sqrt(fmax(s[0].y - s[0].x * mean, 0.0) / (double)(len - 1)), 1e-8);
 }
 
 __global__ void __launch_bounds__(kThreads) mono_apply(const float* __restrict__ mix, int64_t n,
@@ -97,15 +105,13 @@ __global__ void __launch_bounds__(128) cac_finish(const double2* __restrict__ pa
 
 } // namespace
 
-size_t mono_scratch_doubles() { return kBlocks + 2; }
+size_t mono_scratch_doubles() { return 2 * kBlocks + 2; }
 
 cudaError_t launch_mono_norm(const float* mix, int64_t len, int C, double* scratch, float* out, cudaStream_t st) {
-    double* partial = scratch + 2;
+    double2* partial = reinterpret_cast<double2*>(scratch + 2);   // scratch is 16-byte aligned
     double* stats = scratch;
-    for (int pass = 0; pass < 2; pass++) {
-        mono_partials<<<kBlocks, kThreads, 0, st>>>(mix, len, C, pass, stats, partial);
-        mono_finish<<<1, kBlocks, 0, st>>>(partial, len, pass, stats);
-    }
+    mono_partials<<<kBlocks, kThreads, 0, st>>>(mix, len, C, partial);
+    mono_finish<<<1, kBlocks, 0, st>>>(partial, len, stats);
     mono_apply<<<kBlocks, kThreads, 0, st>>>(mix, (int64_t)C * len, stats, out);
     return cudaGetLastError();
 }

@@ -602,7 +602,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         ~Join() { now(); }
     } join;
     const float* d_mix = normalise_mix(P, D, d_mix_in, st);
-    if (timing && P.mono_norm) timing->launches += 5;
+    if (timing && P.mono_norm) timing->launches += 3;
     if (side_t) cuda_check(cudaEventRecord(D.fork, st), "cudaEventRecord");
     for (const auto& rg : ranges) {
         const int c0 = rg.first, G = rg.second - rg.first;
