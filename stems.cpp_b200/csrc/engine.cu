@@ -173,11 +173,10 @@ STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const floa
         cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
         // The masks are most of the bytes (RoFormer cfg1: 934 MB against 21 MB of audio) and
         // the PCIe copy takes some 30 times the kernels. They come in batch by batch on a copy
-        // stream, and each batch's kernels wait only for their own masks, so the kernels run
-        // under the next batches' copies. HTDemucs transposes every segment's masks before its
-        // first back kernel, so its masks come in as one copy.
+        // stream, and each batch's kernels (HTDemucs: its transposition, then its back kernel)
+        // wait only for their own masks, so the kernels run under the next batches' copies.
         const int n = (int)H.chunks.size();
-        const int batches = H.z_per_chunk() ? 1 : std::min(n, kHostBatches);
+        const int batches = std::min(n, kHostBatches);
         if (batches <= 1) {
             cuda_check(cudaMemcpyAsync(p->s_mask.p, h_mask, mask_b, cudaMemcpyHostToDevice, st), "copy masks in");
             p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr);
@@ -207,11 +206,8 @@ STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const floa
             stg_run_options o{};
             o.size = sizeof(o);
             o.chunks_per_batch = per;
-            const BatchHook wait = [&](int first, int) {
-                cuda_check(cudaStreamWaitEvent(st, p->copy_ev[first / per], 0), "cudaStreamWaitEvent");
-            };
             try {
-                p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o, 0, -1, &wait);
+                p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o, 0, -1, &p->copy_ev);
             } catch (...) {   // no copy may still read the caller's host buffer after the return
                 cudaStreamSynchronize(p->copy_st);
                 throw;

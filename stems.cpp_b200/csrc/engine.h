@@ -109,6 +109,7 @@ struct stg_plan {
     cudaStream_t copy_st = nullptr;
     cudaEvent_t copy_fork = nullptr;
     std::vector<cudaEvent_t> copy_ev;
+    std::vector<cudaEvent_t> side_ev;   // HTDemucs: per batch, its masks transposed (PlanDevice::side_ev)
     DevBuf dm_out;                 // one channel's result (stg_separate_dual_mono)
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
@@ -120,6 +121,8 @@ struct stg_plan {
         if (D.join) cudaEventDestroy(D.join);
         if (D.side) cudaStreamDestroy(D.side);
         for (cudaEvent_t e : copy_ev)
+            if (e) cudaEventDestroy(e);
+        for (cudaEvent_t e : side_ev)
             if (e) cudaEventDestroy(e);
         if (copy_fork) cudaEventDestroy(copy_fork);
         if (copy_st) cudaStreamDestroy(copy_st);
@@ -156,6 +159,7 @@ struct stg_plan {
                 cuda_check(cudaStreamCreateWithFlags(&D.side, cudaStreamNonBlocking), "cudaStreamCreate");
                 cuda_check(cudaEventCreateWithFlags(&D.fork, cudaEventDisableTiming), "cudaEventCreate");
                 cuda_check(cudaEventCreateWithFlags(&D.join, cudaEventDisableTiming), "cudaEventCreate");
+                D.side_ev = &side_ev;
             }
         }
         if (H.cac_norm) {
@@ -180,7 +184,7 @@ struct stg_plan {
     }
 
     void run(const float* d_mix, const float* d_mask, float* d_out, cudaStream_t st, const stg_run_options* opt,
-             int64_t sample_begin = 0, int64_t sample_end = -1, const BatchHook* before_batch = nullptr) {
+             int64_t sample_begin = 0, int64_t sample_end = -1, const std::vector<cudaEvent_t>* ready = nullptr) {
         if (!d_mix || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
         H.check_mask(d_mask);
         cuda_check(cudaSetDevice(engine->device), "cudaSetDevice");
@@ -188,7 +192,7 @@ struct stg_plan {
         if (timing.timed)
             for (cudaEvent_t& e : timing.ev)
                 if (!e) cuda_check(cudaEventCreate(&e), "cudaEventCreate");
-        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing, sample_begin, sample_end, before_batch);
+        launch_plan(H, D, d_mix, d_mask, d_out, st, opt, &timing, sample_begin, sample_end, ready);
     }
 
     // The mix the front half reads: with the mono normalisation, chunk 0's call normalises

@@ -570,7 +570,7 @@ std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_
 
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
-                 int64_t sample_begin, int64_t sample_end, const BatchHook* before_batch) {
+                 int64_t sample_begin, int64_t sample_end, const std::vector<cudaEvent_t>* ready) {
     if (!d_mix_in || !d_mask || !d_out) fail(STG_INVALID_ARGUMENT, "null buffer");
     P.check_mask(d_mask);
     if (sample_end < 0) sample_end = P.len;
@@ -589,7 +589,11 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     // normalisation and the front kernel (latency-bound); every segment has its own slot of
     // the scratch. The fork orders it after the caller's earlier work, including the previous
     // separation's back kernels, which read the same scratch.
-    const bool side_t = zpath && P.mask_planes && D.side;
+    const bool side_t = zpath && P.mask_planes && D.side && D.side_ev;
+    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total;
+    int n_batches = 0;
+    for (const auto& rg : ranges) n_batches += (rg.second - rg.first + per - 1) / per;
+    if (ready && (int)ready->size() < n_batches) fail(STG_INTERNAL_ERROR, "fewer mask events than batches");
     // the caller's stream waits for the side stream before anything after this point,
     // the back kernels, or a failure, can hand the masks back to the caller
     struct Join {
@@ -631,17 +635,27 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             if (timing) timing->launches += k;
         }
     }
-    if (side_t) {
+    if (side_t) {   // batch by batch, each after its masks (when streamed in)
         if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
-        cuda_check(cudaStreamWaitEvent(D.side, D.fork, 0), "cudaStreamWaitEvent");
-        for (const auto& rg : ranges) {
-            cuda_check(launch_mask_transpose(d_mask + (int64_t)rg.first * P.mask_per_chunk, P.mask_per_chunk,
-                                             rg.second - rg.first, P.S, P.mask_planes, P.mask_bins, P.g.T,
-                                             D.mask_t + (int64_t)rg.first * P.mask_t_per_chunk(),
-                                             P.mask_t_per_chunk(), D.side),
-                       "mask transposition launch");
-            if (timing) timing->launches++;
+        while ((int)D.side_ev->size() < n_batches) {
+            cudaEvent_t e = nullptr;
+            cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+            D.side_ev->push_back(e);
         }
+        cuda_check(cudaStreamWaitEvent(D.side, D.fork, 0), "cudaStreamWaitEvent");
+        int k = 0;
+        for (const auto& rg : ranges)
+            for (int b0 = rg.first; b0 < rg.second; b0 += per, k++) {
+                const int nb = std::min(per, rg.second - b0);
+                if (ready) cuda_check(cudaStreamWaitEvent(D.side, (*ready)[k], 0), "cudaStreamWaitEvent");
+                cuda_check(launch_mask_transpose(d_mask + (int64_t)b0 * P.mask_per_chunk, P.mask_per_chunk, nb, P.S,
+                                                 P.mask_planes, P.mask_bins, P.g.T,
+                                                 D.mask_t + (int64_t)b0 * P.mask_t_per_chunk(),
+                                                 P.mask_t_per_chunk(), D.side),
+                           "mask transposition launch");
+                if (timing) timing->launches++;
+                cuda_check(cudaEventRecord((*D.side_ev)[k], D.side), "cudaEventRecord");
+            }
         cuda_check(cudaEventRecord(D.join, D.side), "cudaEventRecord");
         join.st = st;
         join.ev = D.join;
@@ -658,14 +672,15 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
     f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
     f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
-    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total;
-    int done = 0;
+    int done = 0, k = 0;
     bool first_batch = true;
     for (const auto& rg : ranges) {
-        for (int b0 = rg.first; b0 < rg.second; b0 += per) {
+        for (int b0 = rg.first; b0 < rg.second; b0 += per, k++) {
             if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
             const int nb = std::min(per, rg.second - b0);
-            if (before_batch) (*before_batch)(b0, nb);
+            // the batch's masks: transposed on the side stream, or streamed in by the caller
+            if (side_t) cuda_check(cudaStreamWaitEvent(st, (*D.side_ev)[k], 0), "cudaStreamWaitEvent");
+            else if (ready) cuda_check(cudaStreamWaitEvent(st, (*ready)[k], 0), "cudaStreamWaitEvent");
             f.chunks = D.chunks + b0;
             f.n_chunks = nb;
             f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
@@ -673,7 +688,6 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
             f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
             if (side_t) {   // transposed on the side stream
-                join.now();
                 f.mask = reinterpret_cast<const float*>(D.mask_t + (int64_t)b0 * P.mask_t_per_chunk());
                 f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
             } else if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
@@ -708,6 +722,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
             }
         }
     }
+    join.now();
     CombineParams c{};
     c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
     c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;

@@ -13,7 +13,6 @@
 #include "kernels.h"
 
 #include <cstdint>
-#include <functional>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -116,6 +115,7 @@ struct PlanDevice {
     // transpositions run in order on the caller's stream)
     cudaStream_t side = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
+    std::vector<cudaEvent_t>* side_ev = nullptr;   // one per batch: its transposition done
 };
 
 void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len);
@@ -145,12 +145,12 @@ struct RunTiming {
 // chunk batches (progress and cancellation between batches), then the combine.
 // With a sample range, only the chunks reaching output samples [sample_begin, sample_end) run
 // and only those samples of every output row are written (end < 0: the whole track).
-// before_batch(first, n), when given, runs on the host before each batch's kernels are
-// enqueued: a caller that streams each batch's masks in makes st wait for them there.
-using BatchHook = std::function<void(int first, int n)>;
+// ready, when given, streams the masks in: batch k of the run (the batches of
+// opt->chunks_per_batch, in order) reads its masks only after (*ready)[k] has completed.
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
-                 int64_t sample_begin = 0, int64_t sample_end = -1, const BatchHook* before_batch = nullptr);
+                 int64_t sample_begin = 0, int64_t sample_end = -1,
+                 const std::vector<cudaEvent_t>* ready = nullptr);
 
 // The halves around a real network, on chunks [first, first + n): the front writes the
 // network's input (net_in_per_chunk floats per chunk) into d_net_in; the back reads its

@@ -169,6 +169,18 @@ def test_host_entry_tfc_batches(pkg, engine):
         assert np.array_equal(a, plan.separate_host(mix, mask))
 
 
+def test_host_entry_htdemucs_batches(pkg, engine):
+    """HTDemucs through the host entry point: each batch's masks transposed as they arrive."""
+    length = 44100 * 30 + 7
+    plan = engine.plan_htdemucs(length)
+    assert plan.n_chunks >= 4
+    mix = synth_audio(45, length)
+    mask = synth_mask(46, plan.mask_floats, 1.0)
+    a = run_gpu(plan, mix, mask)
+    for _ in range(2):
+        assert np.array_equal(a, plan.separate_host(mix, mask))
+
+
 # ---- DualMono (src/separator.cpp:15-47) ----------------------------------------------------------
 def test_dual_mono_roformer_matches_oracle(pkg, engine, oracle_mod):
     """A mono RoFormer (a dereverb model's layout) over a stereo mix, channel by channel."""
