@@ -195,7 +195,9 @@ STG_API stg_status stg_separate(stg_plan* plan, const float* d_mix, const float*
 
 /* The same on host buffers: copies the mix and the masks in, runs, copies the result out,
  * and returns when the result is in h_out. This is the end-to-end call a host such as
- * libstems' separate (src/libstems.cpp:135-219) makes. */
+ * libstems' separate (src/libstems.cpp:135-219) makes. The masks come in up to eight batches
+ * of chunks on a stream of the plan's own, each batch's kernels running as soon as its masks
+ * have arrived; pinned host buffers let the copies run at full PCIe speed. */
 STG_API stg_status stg_separate_host(stg_plan* plan, const float* h_mix, const float* h_mask,
                                      float* h_out, void* stream);
 
