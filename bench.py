@@ -619,6 +619,20 @@ def run_ours(args, w, rank, world, local_rank):
     e2e_s = (time.perf_counter() - t0) / e2e_steps
     e2e_s = max_over_ranks(e2e_s)
     barrier()
+    # the same bytes copied and nothing else: the PCIe bound of the e2e number
+    d_in_mix, d_in_mask = torch.empty_like(h_mix, device=dev), torch.empty_like(h_mask, device=dev)
+    d_res = torch.empty(plan.out_shape, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            d_in_mix.copy_(h_mix, non_blocking=True)
+            d_in_mask.copy_(h_mask, non_blocking=True)
+            h_out.copy_(d_res, non_blocking=True)
+            stream.synchronize()
+    copy_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+    del d_in_mix, d_in_mask, d_res
+    barrier()
 
     audio_s = w["seconds"] * n_tracks
     value = audio_s / (ms / 1e3)
@@ -646,7 +660,9 @@ def run_ours(args, w, rank, world, local_rank):
             "clocks": dict(clk.summary(), remeasured=remeasured),
             "e2e": {"value": w["seconds"] * world / e2e_s, "unit": "audio-s/s",
                     "h2d_bytes_per_step": 4 * (plan.n_channels * plan.n_samples + plan.mask_floats),
-                    "d2h_bytes_per_step": 4 * plan.out_floats},
+                    "d2h_bytes_per_step": 4 * plan.out_floats,
+                    "copies_only": w["seconds"] * world / copy_s,
+                    "copies_only_note": "the same host<->device copies alone, no kernels: the PCIe bound"},
             "gpu_launches": n_launch * args.steps * mine,
         }
     plan.close()
