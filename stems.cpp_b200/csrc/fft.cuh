@@ -206,14 +206,10 @@ template <bool INV> struct Dft<32, INV> : DftCT<2, 16, INV> {};
 // telescope) and the lanes of a warp, which hold consecutive k, read consecutive entries.
 template <int NS> __host__ __device__ constexpr int twiddle_index(int r, int k) { return (NS - 1) + (r - 1) * NS + k; }
 
-// Twiddle sources: the table in global memory (read through L1) or a copy in shared memory.
+// The twiddle table in global memory, read through L1.
 struct TwGlobal {
     const float2* __restrict__ p;
     __device__ __forceinline__ float2 operator()(int i) const { return __ldg(p + i); }
-};
-struct TwShared {
-    const float2* p;
-    __device__ __forceinline__ float2 operator()(int i) const { return p[i]; }
 };
 
 // One pass with caller-supplied input and output. Butterfly j reads the points

@@ -15,18 +15,14 @@ namespace stg {
 template <int N> struct FftCfg;
 template <> struct FftCfg<2048> {
     static constexpr int T = 128, MINB = 3, HOPMAX = 512;
-    static constexpr int PF_GROUPS = 1;     // mask loads issued in this many groups
-    static constexpr bool AHEAD = false;    // mask loads issued one frame ahead
     static constexpr bool MASK_L2 = false;  // TFC-TDF: the next frame's mask row prefetched into L2
-    static constexpr bool SMEM_TW = false, SMEM_WIN = false;   // table copies in shared memory
+    static constexpr bool SMEM_WIN = false;   // the window copied into shared memory
     using Plan = RadixList<8, 16, 16>;
 };
 template <> struct FftCfg<4096> {
     static constexpr int T = 256, MINB = 2, HOPMAX = 1024;
-    static constexpr int PF_GROUPS = 1;
-    static constexpr bool AHEAD = false;
     static constexpr bool MASK_L2 = false;
-    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    static constexpr bool SMEM_WIN = false;
     using Plan = RadixList<16, 16, 16>;
 };
 // 7680: radix 15 last, because a first radix-15 pass stores at stride 15, which the padding
@@ -37,19 +33,15 @@ template <> struct FftCfg<4096> {
 // a frame ahead (both measured: 1.59 -> 1.42 ms on a 180 s track).
 template <> struct FftCfg<7680> {
     static constexpr int T = 256, MINB = 1, HOPMAX = 1024;
-    static constexpr int PF_GROUPS = 1;
-    static constexpr bool AHEAD = false;
     static constexpr bool MASK_L2 = true;
-    static constexpr bool SMEM_TW = false, SMEM_WIN = true;
+    static constexpr bool SMEM_WIN = true;
     using Plan = RadixList<8, 8, 8, 15>;
 };
 // The VR bands' sizes (src/vr_dsp.h, 320 to 2048 points): front and back kernels only.
 template <int N, int TT, class P> struct SmallFft {
     static constexpr int T = TT, MINB = 1, HOPMAX = N / 2;
-    static constexpr int PF_GROUPS = 1;
-    static constexpr bool AHEAD = false;
     static constexpr bool MASK_L2 = false;
-    static constexpr bool SMEM_TW = false, SMEM_WIN = false;
+    static constexpr bool SMEM_WIN = false;
     using Plan = P;
 };
 template <> struct FftCfg<320> : SmallFft<320, 64, RadixList<8, 8, 5>> {};

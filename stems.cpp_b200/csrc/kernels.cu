@@ -41,9 +41,8 @@ template <int ARCH, int N, int T> struct MaskOp {
 
     const int2* btab;   // RoFormer: the bin table's copy in shared memory
 
-    // Issue the mask loads of the bin slots [i0, i1) (compile-time constants at every call).
-    __device__ __forceinline__ void prefetch(const FusedParams& p, int ci, int s, int t, int tid,
-                                             int i0 = 0, int i1 = BPT) {
+    // Issue the mask loads of every bin slot of the thread.
+    __device__ __forceinline__ void prefetch(const FusedParams& p, int ci, int s, int t, int tid) {
         const float* __restrict__ m = p.mask + (int64_t)ci * p.mask_chunk_stride;
         if constexpr (ARCH == ARCH_ROFORMER) {
             // src/roformer.cpp:256-269: band b's mask for frame t is the row
@@ -51,7 +50,6 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + (int64_t)s * p.stem_stride;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
-                if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 inv[i] = 0.0f;
@@ -84,7 +82,6 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + ((int64_t)s * p.g.T + t) * F * 4;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
-                if (i < i0 || i >= i1) continue;
                 const int f = tid + i * T;
                 a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (f >= f_lo && f < F) a[i] = ld_stream4(ms + 4 * f);
@@ -131,17 +128,15 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     using FwdRest = typename Head<Plan>::tail;
     using InvInit = typename Init<Plan>::type;            // inverse passes but the last
     constexpr int RL = Init<Plan>::last, NSL = Init<Plan>::prod;
-    constexpr bool STW = FftCfg<N>::SMEM_TW, SWIN = FftCfg<N>::SMEM_WIN;
+    constexpr bool SWIN = FftCfg<N>::SMEM_WIN;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
     float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
     float2* out_ring = in_ring + N;                       // overlap-add sums (L, R) by position mod N
-    float2* tw_s = out_ring + N;                          // [STW] twiddle table copy
-    float* win_s = reinterpret_cast<float*>(tw_s + (STW ? N : 0));   // [SWIN] window copy
+    float* win_s = reinterpret_cast<float*>(out_ring + N);   // [SWIN] window copy
     int2* btab_s = reinterpret_cast<int2*>(win_s + (SWIN ? N : 0));   // [RoFormer] bin table copy
     float* env_s = reinterpret_cast<float*>(btab_s + (ARCH == ARCH_ROFORMER ? N / 2 + 2 : 0));   // envelope period
-    using Tw = std::conditional_t<STW, TwShared, TwGlobal>;
-    const Tw tw{STW ? tw_s : p.tw};
+    const TwGlobal tw{p.tw};
     const float* win = SWIN ? win_s : p.win;
 
     const int tid = threadIdx.x;
@@ -155,8 +150,6 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 
     // every stem pass flushes the whole output ring at its last frame, so one zeroing lasts
     for (int i = tid; i < N; i += T) out_ring[i] = make_float2(0.f, 0.f);
-    if constexpr (STW)
-        for (int i = tid; i < N; i += T) tw_s[i] = __ldg(p.tw + i);
     if constexpr (SWIN)
         for (int i = tid; i < N; i += T) win_s[i] = __ldg(p.win + i);
     const bool env_on = p.env_period != nullptr;
@@ -191,7 +184,6 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 const int u = tid + k * T;
                 if (u < hop && t_begin + 1 < t_end) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + N + u);
             }
-            if constexpr (FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t_begin, tid);
         }
         __syncthreads();
         // TFC-TDF: frame t's mask row (dim_f float4, 16-byte aligned) requested from L2 a frame
@@ -233,18 +225,12 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 }
             }
             passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
-            // all of this frame's mask loads in flight at once (or already, a frame ahead),
-            // then the spectral op
-            // (in PF_GROUPS groups of bin slots, the next group's loads issued before the
-            // current group is applied, to bound the registers they hold)
+            // all of this frame's mask loads in flight at once, then the spectral op: split the
+            // channels, apply the stand-in network, repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
-            constexpr int NG = FftCfg<N>::PF_GROUPS, PER = (BPT + NG - 1) / NG;
-            if constexpr (!FftCfg<N>::AHEAD) mk.prefetch(p, ci, s, t, tid, 0, PER);
-            // split the channels, apply the stand-in network, repack as one Hermitian pair
+            mk.prefetch(p, ci, s, t, tid);
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
-                if constexpr (!FftCfg<N>::AHEAD)
-                    if (i % PER == 0 && i + PER < BPT) mk.prefetch(p, ci, s, t, tid, i + PER, i + 2 * PER);
                 const int f = tid + i * T;
                 if (f <= N / 2) {
                     const int fm = f == 0 ? 0 : N - f;
@@ -258,8 +244,6 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
                 }
             }
-            if constexpr (FftCfg<N>::AHEAD)
-                if (t + 1 < t_end) mk.prefetch(p, ci, s, t + 1, tid);
             __syncthreads();
             passes<N, T, true, 1>(buf, tw, tid, InvInit{});
             // inverse last pass: window and overlap-add straight into the output ring
@@ -566,7 +550,6 @@ int fused_threads(int n) {
 
 template <int ARCH, int N> static size_t smem_bytes_t() {
     return sizeof(float2) * ((size_t)padded_size(N) + 2 * (size_t)N) +
-           (FftCfg<N>::SMEM_TW ? sizeof(float2) * (size_t)N : 0) +
            (FftCfg<N>::SMEM_WIN ? sizeof(float) * (size_t)N : 0) +
            (ARCH == ARCH_ROFORMER ? sizeof(int2) * (size_t)(N / 2 + 2) : 0) +
            sizeof(float) * (size_t)FftCfg<N>::HOPMAX;   // the envelope period
