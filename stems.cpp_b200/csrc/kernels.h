@@ -205,6 +205,7 @@ std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
 bool split_supported(int n_fft);   // n_fft the front and back kernels take
 int back_resident_ctas(int n_fft); // CTAs of the back kernel resident at once (0 when unknown)
+int split_resident_ctas(int n_fft, bool front);   // the same for the front (generic) or back kernel
 int split_max_hop(int n_fft);
 
 // convert.cu. Resampling (and layout / channel conversion) of planar or interleaved audio:

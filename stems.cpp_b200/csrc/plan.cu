@@ -73,8 +73,10 @@ void finish_plan(HostPlan& P, int env_frames) {
     // [K_min, 16] with the shortest critical path, the larger on ties. K_min keeps every
     // sample within one tile boundary (K * hop >= n_fft - hop).
     // (HTDemucs separations run the back kernel over the chunks, the others the fused one)
-    const int64_t slots = std::max(1, P.arch == ARCH_HTDEMUCS && !P.primitive ? back_resident_ctas(N)
-                                                                              : fused_resident_ctas(P.arch, N));
+    // (single-chunk primitives run the front and back kernels: the fewer resident of the two)
+    const int64_t slots = std::max(1, P.primitive ? std::min(split_resident_ctas(N, true), split_resident_ctas(N, false))
+                                      : P.arch == ARCH_HTDEMUCS ? back_resident_ctas(N)
+                                                                : fused_resident_ctas(P.arch, N));
     const int k_min = std::max(1, (N - hop + hop - 1) / hop);
     P.K = std::max(16, k_min);
     int64_t best = INT64_MAX;

@@ -430,25 +430,41 @@ bool split_supported(int n) {
 
 int split_max_hop(int n) { return split_supported(n) ? n / 2 : 0; }
 
-int back_resident_ctas(int n) {
+namespace {
+template <class K> int resident_of(K kernel, int threads, size_t smem) {
     int per_sm = 0, n_sm = 0, dev = 0;
-    auto query = [&](auto kernel, int threads, size_t smem) {
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) {
-            cudaGetLastError();
-            return 0;
-        }
-        return per_sm * n_sm;
-    };
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return per_sm * n_sm;
+}
+// the resident CTAs of the front (generic layouts) or the back kernel at size N
+template <int N> int split_resident_t(bool front) {
+    const size_t ring = sizeof(float2) * ((size_t)padded_size(N) + N);
+    return front ? resident_of(front_kernel<N, -1>, FftCfg<N>::T, ring + sizeof(int2) * (size_t)(N / 2 + 2))
+                 : resident_of(back_kernel<N>, FftCfg<N>::T, ring + sizeof(float) * (size_t)(N / 2));
+}
+} // namespace
+
+int split_resident_ctas(int n, bool front) {
     switch (n) {
-        case 4096:
-            return query(back_kernel<4096>, FftCfg<4096>::T,
-                         sizeof(float2) * ((size_t)padded_size(4096) + 4096) + sizeof(float) * 2048);
+        case 320: return split_resident_t<320>(front);
+        case 512: return split_resident_t<512>(front);
+        case 640: return split_resident_t<640>(front);
+        case 960: return split_resident_t<960>(front);
+        case 1024: return split_resident_t<1024>(front);
+        case 2048: return split_resident_t<2048>(front);
+        case 4096: return split_resident_t<4096>(front);
+        case 7680: return split_resident_t<7680>(front);
     }
     return 0;
 }
+
+int back_resident_ctas(int n) { return split_resident_ctas(n, false); }
 
 cudaError_t launch_front(const SplitParams& p, cudaStream_t st) {
     if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
