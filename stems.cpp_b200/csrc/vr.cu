@@ -22,6 +22,7 @@ namespace stg {
 namespace {
 
 constexpr int kMaxBands = 16;
+constexpr size_t kResampleSmemMax = 96 * 1024;   // larger stretches use the kernel without staging
 
 // scipy-style centred upfirdn of stereo x [2][n] (src/vr_dsp.h:92-111)
 __global__ void __launch_bounds__(256) vr_resample_kernel(const float* __restrict__ x, int n, int up, int down,
@@ -37,6 +38,57 @@ __global__ void __launch_bounds__(256) vr_resample_kernel(const float* __restric
         const double h = (double)__ldg(fir + (pos - (int64_t)i * up));
         s0 = __dadd_rn(s0, __dmul_rn((double)__ldg(x + i), h));
         s1 = __dadd_rn(s1, __dmul_rn((double)__ldg(x + n + i), h));
+    }
+    y[j] = (float)s0;
+    y[out_n + j] = (float)s1;
+}
+
+// The same sums, with the block's input stretch of both channels and the FIR converted to
+// double once into shared memory (each input sample feeds about n_taps / up outputs). The
+// loads and products are the same doubles in the same order, so the outputs are the same.
+__global__ void __launch_bounds__(256) vr_resample_smem_kernel(const float* __restrict__ x, int n, int up, int down,
+                                                              const float* __restrict__ fir, int n_taps,
+                                                              float* __restrict__ y, int out_n, int cap) {
+    extern __shared__ double sm[];
+    const int j0 = blockIdx.x * blockDim.x;
+    const int jl = min(out_n - 1, j0 + (int)blockDim.x - 1);
+    const auto lo_of = [&](int j) {
+        return (int)max((int64_t)0, ((int64_t)j * down + n_taps / 2 - n_taps + up) / up);
+    };
+    const auto hi_of = [&](int j) { return (int)min((int64_t)n - 1, ((int64_t)j * down + n_taps / 2) / up); };
+    const int base = lo_of(j0), span = hi_of(jl) - base + 1;   // lo and hi grow with j
+    if (span > cap) {   // more than the launch allocated (the host bound makes this unreachable)
+        const int j = j0 + threadIdx.x;
+        if (j <= jl) {
+            const int64_t pos = (int64_t)j * down + n_taps / 2;
+            double s0 = 0.0, s1 = 0.0;
+            for (int i = lo_of(j); i <= hi_of(j); i++) {
+                const double h = (double)__ldg(fir + (pos - (int64_t)i * up));
+                s0 = __dadd_rn(s0, __dmul_rn((double)__ldg(x + i), h));
+                s1 = __dadd_rn(s1, __dmul_rn((double)__ldg(x + n + i), h));
+            }
+            y[j] = (float)s0;
+            y[out_n + j] = (float)s1;
+        }
+        return;
+    }
+    double* xs = sm;             // [2][cap]
+    double* hs = sm + 2 * cap;   // [n_taps]
+    for (int k = threadIdx.x; k < span; k += blockDim.x) {
+        xs[k] = (double)__ldg(x + base + k);
+        xs[cap + k] = (double)__ldg(x + n + base + k);
+    }
+    for (int k = threadIdx.x; k < n_taps; k += blockDim.x) hs[k] = (double)__ldg(fir + k);
+    __syncthreads();
+    const int j = j0 + threadIdx.x;
+    if (j > jl) return;
+    const int64_t pos = (int64_t)j * down + n_taps / 2;
+    const int lo = lo_of(j), hi = hi_of(j);
+    double s0 = 0.0, s1 = 0.0;
+    for (int i = lo; i <= hi; i++) {
+        const double h = hs[pos - (int64_t)i * up];
+        s0 = __dadd_rn(s0, __dmul_rn(xs[i - base], h));
+        s1 = __dadd_rn(s1, __dmul_rn(xs[cap + i - base], h));
     }
     y[j] = (float)s0;
     y[out_n + j] = (float)s1;
@@ -183,8 +235,20 @@ struct stg_vr_plan {
         }
         const int g = std::gcd(src, dst);
         const auto& h = fir(src, dst);
-        vr_resample_kernel<<<blocks_for(m), 256, 0, st>>>(x, n, dst / g, src / g, h.first.as<float>(), h.second, y,
-                                                           m);
+        const int up = dst / g, down = src / g, taps = h.second;
+        // a block's input stretch: at most 255 output steps of down/up inputs plus the FIR's
+        // reach, with a margin for the roundings of both ends
+        const int64_t span = (int64_t)255 * down / up + taps / up + 4;
+        const size_t smem = sizeof(double) * (size_t)(2 * span + taps);
+        if (smem <= kResampleSmemMax) {
+            cuda_check(cudaFuncSetAttribute(vr_resample_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kResampleSmemMax),
+                       "vr resampling kernel attribute");
+            vr_resample_smem_kernel<<<blocks_for(m), 256, smem, st>>>(x, n, up, down, h.first.as<float>(), taps, y, m,
+                                                                      (int)span);
+        } else {
+            vr_resample_kernel<<<blocks_for(m), 256, 0, st>>>(x, n, up, down, h.first.as<float>(), taps, y, m);
+        }
         cuda_check(cudaGetLastError(), "vr resampling kernel launch");
     }
 
