@@ -170,51 +170,53 @@ STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const floa
         p->s_mix.reserve(mix_b, "staging");
         p->s_mask.reserve(mask_b, "staging");
         p->s_out.reserve(out_b, "staging");
-        cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
-        // The masks are most of the bytes (RoFormer cfg1: 934 MB against 21 MB of audio) and
-        // the PCIe copy takes some 30 times the kernels. They come in batch by batch on a copy
-        // stream, and each batch's kernels (HTDemucs: its transposition, then its back kernel)
-        // wait only for their own masks, so the kernels run under the next batches' copies.
-        const int n = (int)H.chunks.size();
-        const int batches = std::min(n, kHostBatches);
-        if (batches <= 1) {
-            cuda_check(cudaMemcpyAsync(p->s_mask.p, h_mask, mask_b, cudaMemcpyHostToDevice, st), "copy masks in");
-            p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr);
-        } else {
-            if (!p->copy_st) {
-                cuda_check(cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking), "cudaStreamCreate");
-                cuda_check(cudaEventCreateWithFlags(&p->copy_fork, cudaEventDisableTiming), "cudaEventCreate");
-            }
-            while ((int)p->copy_ev.size() < batches) {
-                cudaEvent_t e = nullptr;
-                cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
-                p->copy_ev.push_back(e);
-            }
-            const int per = (n + batches - 1) / batches;
-            const size_t chunk_b = sizeof(float) * (size_t)H.mask_per_chunk;
-            // the copies overwrite the staging that the caller's earlier work on st may still read
-            cuda_check(cudaEventRecord(p->copy_fork, st), "cudaEventRecord");
-            cuda_check(cudaStreamWaitEvent(p->copy_st, p->copy_fork, 0), "cudaStreamWaitEvent");
-            for (int b = 0, c0 = 0; c0 < n; b++, c0 += per) {
-                const int nb = std::min(per, n - c0);
-                cuda_check(cudaMemcpyAsync(static_cast<char*>(p->s_mask.p) + chunk_b * c0,
-                                           reinterpret_cast<const char*>(h_mask) + chunk_b * c0,
-                                           chunk_b * nb, cudaMemcpyHostToDevice, p->copy_st),
-                           "copy masks in");
-                cuda_check(cudaEventRecord(p->copy_ev[b], p->copy_st), "cudaEventRecord");
-            }
-            stg_run_options o{};
-            o.size = sizeof(o);
-            o.chunks_per_batch = per;
-            try {
+        // on a failure, no copy may still read or write the caller's host buffers after the return
+        try {
+            cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
+            // The masks are most of the bytes (RoFormer cfg1: 934 MB against 21 MB of audio) and
+            // the PCIe copy takes some 30 times the kernels. They come in batch by batch on a copy
+            // stream, and each batch's kernels (HTDemucs: its transposition, then its back kernel)
+            // wait only for their own masks, so the kernels run under the next batches' copies.
+            const int n = (int)H.chunks.size();
+            const int batches = std::min(n, kHostBatches);
+            if (batches <= 1) {
+                cuda_check(cudaMemcpyAsync(p->s_mask.p, h_mask, mask_b, cudaMemcpyHostToDevice, st), "copy masks in");
+                p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr);
+            } else {
+                if (!p->copy_st) {
+                    cuda_check(cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking), "cudaStreamCreate");
+                    cuda_check(cudaEventCreateWithFlags(&p->copy_fork, cudaEventDisableTiming), "cudaEventCreate");
+                }
+                while ((int)p->copy_ev.size() < batches) {
+                    cudaEvent_t e = nullptr;
+                    cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+                    p->copy_ev.push_back(e);
+                }
+                const int per = (n + batches - 1) / batches;
+                const size_t chunk_b = sizeof(float) * (size_t)H.mask_per_chunk;
+                // the copies overwrite the staging that the caller's earlier work on st may still read
+                cuda_check(cudaEventRecord(p->copy_fork, st), "cudaEventRecord");
+                cuda_check(cudaStreamWaitEvent(p->copy_st, p->copy_fork, 0), "cudaStreamWaitEvent");
+                for (int b = 0, c0 = 0; c0 < n; b++, c0 += per) {
+                    const int nb = std::min(per, n - c0);
+                    cuda_check(cudaMemcpyAsync(static_cast<char*>(p->s_mask.p) + chunk_b * c0,
+                                               reinterpret_cast<const char*>(h_mask) + chunk_b * c0,
+                                               chunk_b * nb, cudaMemcpyHostToDevice, p->copy_st),
+                               "copy masks in");
+                    cuda_check(cudaEventRecord(p->copy_ev[b], p->copy_st), "cudaEventRecord");
+                }
+                stg_run_options o{};
+                o.size = sizeof(o);
+                o.chunks_per_batch = per;
                 p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o, 0, -1, &p->copy_ev);
-            } catch (...) {   // no copy may still read the caller's host buffer after the return
-                cudaStreamSynchronize(p->copy_st);
-                throw;
             }
+            cuda_check(cudaMemcpyAsync(h_out, p->s_out.p, out_b, cudaMemcpyDeviceToHost, st), "copy result out");
+            cuda_check(cudaStreamSynchronize(st), "separation");
+        } catch (...) {
+            cudaStreamSynchronize(st);
+            if (p->copy_st) cudaStreamSynchronize(p->copy_st);
+            throw;
         }
-        cuda_check(cudaMemcpyAsync(h_out, p->s_out.p, out_b, cudaMemcpyDeviceToHost, st), "copy result out");
-        cuda_check(cudaStreamSynchronize(st), "separation");
     });
 }
 
