@@ -53,7 +53,8 @@ __global__ void __launch_bounds__(256) resample_kernel(const ResampleParams p) {
                 const int t = (int)pos;
                 if (t >= kTableN) continue;
                 const double fr = pos - t;
-                const double a = __ldg(p.table + t), b = __ldg(p.table + t + 1);
+                const double2 ab = __ldg(p.table + t);
+                const double a = ab.x, b = ab.y;
                 const double w = __dadd_rn(a, __dmul_rn(__dadd_rn(b, -a), fr));
 #pragma unroll
                 for (int k = 0; k < kRows; k++)

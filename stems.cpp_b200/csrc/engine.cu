@@ -305,7 +305,7 @@ void resample_rows(stg_engine* e, const float* d_in, int interleaved, int64_t n,
     p.out_n = std::min(p.out_n, p.out_pin);
     if (src_rate != dst_rate) {
         const auto& k = e->kaiser_for(src_rate, dst_rate);
-        p.table = k.table.as<double>();
+        p.table = k.table.as<double2>();
         p.half = k.half;
         p.ratio = k.ratio;
     }

@@ -72,7 +72,10 @@ struct stg_engine {
             auto nk = std::make_unique<Kaiser>();
             std::vector<double> t;
             kaiser_table(src, dst, t, nk->half, nk->ratio);
-            upload(nk->table, t, "resampling table");
+            // entry t and its successor side by side: one 16-byte load per tap
+            std::vector<double2> pairs(t.size() - 1);
+            for (size_t i = 0; i + 1 < t.size(); i++) pairs[i] = make_double2(t[i], t[i + 1]);
+            upload(nk->table, pairs, "resampling table");
             k = std::move(nk);
         }
         return *k;

@@ -219,7 +219,7 @@ struct ResampleParams {
     int interleaved;           // 1: in[i * in_ch + c]; 0: in[c * in_n + i]
     int to_channels;
     int rows;
-    const double* table;       // kaiser_table, or null
+    const double2* table;      // kaiser_table's entries t and t + 1 side by side, or null
     double half, ratio;
     int64_t out_n;             // resampled length
     int64_t out_pin;           // row stride of the output (pinned length)
