@@ -592,7 +592,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     // the scratch. The fork orders it after the caller's earlier work, including the previous
     // separation's back kernels, which read the same scratch.
     const bool side_t = zpath && P.mask_planes && D.side && D.side_ev;
-    const int per = (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total;
+    const int per = std::max(1, (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total);
     int n_batches = 0;
     for (const auto& rg : ranges) n_batches += (rg.second - rg.first + per - 1) / per;
     if (ready && (int)ready->size() < n_batches) fail(STG_INTERNAL_ERROR, "fewer mask events than batches");
