@@ -1,9 +1,11 @@
 // kernels.cu -- the fused spectral kernel and the chunk combine for sm_100a.
 //
-// Fused kernel, one CTA per (frame tile, chunk). For every stem and every frame of its tile:
-//   1. load the frame of both channels straight from the track (reflect / zero padding of
-//      the chunk, the track and the STFT evaluated per sample), window it, and pack the two
-//      real channels as one complex frame L + iR;
+// Fused kernel, persistent CTAs taking (chunk, frame tile) items. For every stem and every
+// frame of a tile:
+//   1. load the frame's new samples of both channels from the track into an input ring, a
+//      frame ahead (reflect / zero padding of the chunk, the track and the STFT evaluated per
+//      sample where a rule applies), window the frame, and pack the two real channels as one
+//      complex frame L + iR;
 //   2. forward FFT in shared memory (fft.cuh);
 //   3. split the two channels' spectra, apply the architecture's spectral op (the stand-in
 //      for the network: RoFormer's band-averaged mask or TFC-TDF's CaC real mask), drop what
@@ -15,10 +17,10 @@
 //      tile's leading samples, so every sum is formed in a fixed order (no atomics).
 // (HTDemucs, whose four or six stems share one spectrum, runs the front kernel once per frame
 // and the back kernel per stem instead: split.cu, FRONT_ZSPEC / BACK_ZMASK.)
-// Combine kernel: one thread per output sample; it sums the chunks that cover the sample
-// with their crossfade weights (reading Y and the tile-boundary partials Tr), divides by the
-// summed weight, and applies the architecture's epilogue (nan_to_num, compensation,
-// complement).
+// Combine kernel: one thread per output sample (four for one or two stereo stems); it sums
+// the chunks that cover the sample with their crossfade weights (reading Y and the
+// tile-boundary partials Tr), divides by the summed weight, and applies the architecture's
+// epilogue (nan_to_num, compensation, complement).
 #include <algorithm>
 #include <type_traits>
 #include <vector>
