@@ -169,10 +169,12 @@ def test_host_entry_tfc_batches(pkg, engine):
         assert np.array_equal(a, plan.separate_host(mix, mask))
 
 
-def test_host_entry_htdemucs_batches(pkg, engine):
-    """HTDemucs through the host entry point: each batch's masks transposed as they arrive."""
+@pytest.mark.parametrize("shifts", [0, 2])
+def test_host_entry_htdemucs_batches(pkg, engine, shifts):
+    """HTDemucs through the host entry point: each batch's masks transposed as they arrive
+    (with shifts, the batches cross from one shift pass's segments into the next)."""
     length = 44100 * 30 + 7
-    plan = engine.plan_htdemucs(length)
+    plan = engine.plan_htdemucs(length, shifts=shifts, seed=5)
     assert plan.n_chunks >= 4
     mix = synth_audio(45, length)
     mask = synth_mask(46, plan.mask_floats, 1.0)
