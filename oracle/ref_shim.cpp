@@ -1,6 +1,6 @@
 // ref_shim.cpp -- C entry points over the reference's own DSP headers. TEST INFRASTRUCTURE.
 //
-// Compiled by oracle/build_ref.sh against the reference sources where they lie
+// Compiled by oracle/build.sh against the reference sources where they lie
 // (REF_SRC, the reference project's src/ directory) into oracle/_ref/libstems_ref.so. Nothing
 // from the reference is copied here: this file only forwards to st::FFT, st::VRFFT,
 // st::torch_stft/istft and st::htdemucs_spec/ispec (src/stft.h, src/vr_dsp.h) so the C
