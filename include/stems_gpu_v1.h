@@ -102,7 +102,18 @@ typedef struct {
                                 the plan, shift by shift */
     uint32_t seed;           /* SeparateOptions.seed: std::mt19937 seed of the shift offsets */
     int32_t sample_rate;     /* the model's sample rate (max shift = sample_rate / 2); 0 = 44100 */
+    /* Bag of models (stems.n_models, stems.bag_weights; src/htdemucs.cpp:585-642): every model
+     * runs the whole separation (shifts included) on the same normalised mix with its own masks;
+     * stem s of the result is sum_m bag_weights[m][s] * (model m's stem s), summed in model
+     * order, divided by sum_m bag_weights[m][s], then mapped back by the mono statistics once.
+     * The masks of model m follow those of model m - 1. n_models <= 0 with bag_weights NULL:
+     * one model of weight 1, the plain path. These two fields are optional: a config whose
+     * size is STG_HTDEMUCS_CONFIG_V1_SIZE (without them) is a single model. */
+    int32_t n_models;
+    const float* bag_weights;  /* [n_models][n_sources], or NULL for all 1 */
 } stg_htdemucs_config;
+/* The size of stg_htdemucs_config without the bag-of-models fields (older callers). */
+#define STG_HTDEMUCS_CONFIG_V1_SIZE ((uint32_t)offsetof(stg_htdemucs_config, n_models))
 
 /* Mel-Band / BS-RoFormer (src/roformer.cpp:360-412). */
 typedef struct {
@@ -164,12 +175,16 @@ typedef struct {
     int64_t n_samples;             /* per channel, in and out */
     int32_t n_channels;
     int32_t n_out_sources;         /* stems in the result, complement included */
-    int64_t n_chunks;              /* segments (HTDemucs) or chunks: the reference's passes */
+    int64_t n_chunks;              /* segments (HTDemucs) or chunks: the reference's passes
+                                      (a bag of models: every model's, n_models x per model) */
     int64_t n_frames;              /* STFT frames per chunk */
     int64_t mask_floats_per_chunk; /* the stand-in network output of one chunk */
     int64_t out_floats;            /* n_out_sources * n_channels * n_samples */
     int64_t scratch_bytes;         /* device scratch the plan holds */
+    int32_t n_models;              /* models of an HTDemucs bag (1 otherwise); optional field */
 } stg_plan_info;
+/* The size of stg_plan_info without n_models (older callers). */
+#define STG_PLAN_INFO_V1_SIZE ((uint32_t)offsetof(stg_plan_info, n_models))
 STG_API stg_status stg_plan_get_info(const stg_plan* plan, stg_plan_info* info);
 
 /* Layout of one chunk's mask (the network output the plan consumes):
@@ -215,6 +230,26 @@ typedef struct {
 } stg_run_options;
 STG_API stg_status stg_separate_ex(stg_plan* plan, const float* d_mix, const float* d_mask,
                                    float* d_out, void* stream, const stg_run_options* options);
+
+/* The (done, total) pairs follow each reference separator's own counting, so a caller's
+ * progress bar moves as it does with the reference (with chunks_per_batch = 1, pair for pair):
+ *   HTDemucs  total = n_models * max(1, shifts) * ceil(n_samples / stride); after every batch
+ *             (done chunks, total) (src/htdemucs.cpp:576-577, 602); with shifts the views are
+ *             longer than the track, so done can pass total, as in the reference;
+ *   RoFormer  total = max(1, shifts) * the chunks of one pass over n_samples; after every batch
+ *             but the last (done chunks, total), after the last (total, total)
+ *             (src/roformer.cpp:444-451, 479);
+ *   TFC-TDF   total = the chunks; after every batch (done chunks, total) (src/tfc_tdf.cpp:
+ *             411, 425, 577-579), and should_cancel is polled once more after the last batch,
+ *             as the reference's tick after its last chunk does.
+ * should_cancel is polled before every batch. A cancelled run returns STG_CANCELLED having
+ * enqueued no further kernel; d_out is then incomplete. */
+
+/* stg_separate_host with progress and cancellation (options may be NULL). On STG_CANCELLED
+ * (and on any failure) it returns only after every copy it enqueued from h_mix / h_mask has
+ * finished; the result is not copied, so h_out is left as it was. */
+STG_API stg_status stg_separate_host_ex(stg_plan* plan, const float* h_mix, const float* h_mask,
+                                        float* h_out, void* stream, const stg_run_options* options);
 
 /* Output samples [sample_begin, sample_end) of every output row of the separation, running only
  * the chunks that reach them: the same floats stg_separate writes there (each sample sums the
@@ -413,12 +448,19 @@ STG_API stg_status stg_htdemucs_ispec(stg_engine* engine, const float* d_spec, i
  * num_overlap 4, 56 s at num_overlap 2. Longer inputs are rejected with
  * STG_INVALID_ARGUMENT and a message saying how much they need.
  *
- * The first call on a device looks up the array's device address; make that first call
- * before capturing the stream into a CUDA graph. Every call writes the same array (the
- * fused kernel writes all the scratch a call reads, so nothing needs clearing), so calls that
- * overlap on the GPU, for instance on two streams of the same device, race: serialise them.
+ * Contexts: the call runs in the calling thread's current context when that context belongs
+ * to `device` (a host application's own context included); otherwise it makes `device`'s
+ * primary context current for the call and afterwards makes the caller's context (or none)
+ * current again. The first call in each context looks up the array's device address in that
+ * context (cudaGetSymbolAddress); make that first call before any stream capture begins.
+ * Each call copies its tables (chunk schedule, weights, window, twiddles) from host memory the
+ * library keeps into the array with one cudaMemcpyAsync on `stream`, which may wait for the
+ * stream's earlier work; a call with the same configuration and length as the previous call
+ * in the same context skips the copy. Every call writes the same array (the fused kernel
+ * writes all the scratch a call reads, so nothing needs clearing), so calls that overlap on
+ * the GPU, for instance on two streams of the same device, race: serialise them.
  * Asynchronous on `stream`; `message` (optional, message_size bytes) receives the reason for
- * a failure. `device` is made current for the call and the previous device restored. */
+ * a failure. */
 STG_API stg_status stg_separate_roformer_noalloc(int device, const stg_roformer_config* config,
                                                  int64_t n_samples, const float* d_mix,
                                                  const float* d_mask, float* d_out, void* stream,

@@ -32,7 +32,8 @@ class HtParams(C.Structure):
     _fields_ = [("n_channels", C.c_int), ("n_sources", C.c_int), ("segment", C.c_int),
                 ("overlap", C.c_float), ("cac_norm", C.c_int), ("mono_norm", C.c_int),
                 ("sample_first", C.c_int), ("sample_count", C.c_int), ("threads", C.c_int),
-                ("shifts", C.c_int), ("seed", C.c_uint), ("sample_rate", C.c_int)]
+                ("shifts", C.c_int), ("seed", C.c_uint), ("sample_rate", C.c_int),
+                ("n_models", C.c_int), ("bag", C.POINTER(C.c_float))]
 
 
 class RfParams(C.Structure):
@@ -327,9 +328,16 @@ def vr_separate(p, mix, mask):
 
 # ---- glue --------------------------------------------------------------------------------
 def ht_params(n_channels=2, n_sources=4, segment=343980, overlap=-1.0, cac_norm=0, mono_norm=0,
-              sample_first=0, sample_count=0, threads=1, shifts=0, seed=0, sample_rate=44100):
-    return HtParams(n_channels, n_sources, segment, overlap, cac_norm, mono_norm, sample_first,
-                    sample_count, threads, shifts, seed, sample_rate)
+              sample_first=0, sample_count=0, threads=1, shifts=0, seed=0, sample_rate=44100, n_models=1,
+              bag_weights=None):
+    p = HtParams(n_channels, n_sources, segment, overlap, cac_norm, mono_norm, sample_first,
+                 sample_count, threads, shifts, seed, sample_rate, n_models)
+    if bag_weights is not None:
+        w = np.ascontiguousarray(bag_weights, dtype=np.float32).reshape(-1)
+        p.n_models = w.size // n_sources
+        p.bag = w.ctypes.data_as(C.POINTER(C.c_float))
+        p._bag = w   # keeps the weights alive with the struct
+    return p
 
 
 def shift_offsets(seed, shifts, hi):

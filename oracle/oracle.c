@@ -516,6 +516,40 @@ static int ht_split(const or_ht_params* p, const float* buf, int total, int view
     return rc;
 }
 
+/* One model's estimate on the normalised mix (htdemucs.cpp:609-627): split() over the mix, or
+ * the shifts' views averaged; res [S][C][len]. */
+static int ht_model(const or_ht_params* p, const float* mix, int len, const float* mask, const float* weight,
+                    float* res) {
+    const int S = p->n_sources, C = p->n_channels;
+    int rc = 0;
+    if (p->shifts <= 0) {
+        rc = ht_split(p, mix, len, 0, len, mask, weight, 1, res);         /* :610-611 */
+    } else {
+        /* views of the mix padded by max_shift zeros per side; offset uniform in
+         * [0, max_shift], the views' estimates summed then divided (:612-626) */
+        const int ms = max_shift_of(p->sample_rate), total = len + 2 * ms;
+        float* pm = (float*)calloc((size_t)C * total, sizeof(float));
+        for (int c = 0; c < C; c++) memcpy(pm + (size_t)c * total + ms, mix + (size_t)c * len, sizeof(float) * len);
+        int* off = (int*)malloc(sizeof(int) * p->shifts);
+        or_shift_offsets(p->seed, p->shifts, ms, off);
+        memset(res, 0, sizeof(float) * (size_t)S * C * len);
+        const size_t mask_per_seg = (size_t)S * 2 * C * (HT_NFFT / 2) * or_ht_n_frames(p);
+        const float* m = mask;
+        for (int k = 0; k < p->shifts && !rc; k++) {
+            const int vl = len + ms - off[k];
+            float* o = (float*)malloc(sizeof(float) * (size_t)S * C * vl);
+            rc = ht_split(p, pm, total, off[k], vl, m, weight, 0, o);
+            for (int sc = 0; sc < S * C && !rc; sc++)
+                for (int i = 0; i < len; i++) res[(size_t)sc * len + i] += o[(size_t)sc * vl + ms - off[k] + i];
+            m += (size_t)ht_view_segments(p, vl) * mask_per_seg;
+            free(o);
+        }
+        for (size_t i = 0; i < (size_t)S * C * len && !rc; i++) res[i] /= p->shifts;
+        free(off); free(pm);
+    }
+    return rc;
+}
+
 int or_ht_separate(const or_ht_params* p, const float* mix_in, int len, const float* mask,
                    float* est) {
     if (!p || !mix_in || !mask || !est || len <= 0 || p->n_channels < 1 || p->n_sources < 1 ||
@@ -553,34 +587,36 @@ int or_ht_separate(const or_ht_params* p, const float* mix_in, int len, const fl
         for (int i = 0; i < seg; i++) weight[i] /= mx;
     }
     int rc = 0;
-    if (p->shifts <= 0) {
-        rc = ht_split(p, mix, len, 0, len, mask, weight, 1, est);         /* :610-611 */
+    const size_t n_out = (size_t)S * C * len;
+    if (p->n_models <= 1 && !p->bag) {
+        rc = ht_model(p, mix, len, mask, weight, est);
+        /* one model, weight 1: v / 1 * ref_std + ref_mean (:629-642) */
+        if (p->mono_norm && !rc)
+            for (size_t i = 0; i < n_out; i++) est[i] = (float)(est[i] * ref_std + ref_mean);
     } else {
-        /* views of the mix padded by max_shift zeros per side; offset uniform in
-         * [0, max_shift], the views' estimates summed then divided (:612-626) */
-        const int ms = max_shift_of(p->sample_rate), total = len + 2 * ms;
-        float* pm = (float*)calloc((size_t)C * total, sizeof(float));
-        for (int c = 0; c < C; c++) memcpy(pm + (size_t)c * total + ms, mix + (size_t)c * len, sizeof(float) * len);
-        int* off = (int*)malloc(sizeof(int) * p->shifts);
-        or_shift_offsets(p->seed, p->shifts, ms, off);
-        memset(est, 0, sizeof(float) * (size_t)S * C * len);
-        const size_t mask_per_seg = (size_t)S * 2 * C * (HT_NFFT / 2) * or_ht_n_frames(p);
-        const float* m = mask;
-        for (int k = 0; k < p->shifts && !rc; k++) {
-            const int vl = len + ms - off[k];
-            float* o = (float*)malloc(sizeof(float) * (size_t)S * C * vl);
-            rc = ht_split(p, pm, total, off[k], vl, m, weight, 0, o);
-            for (int sc = 0; sc < S * C && !rc; sc++)
-                for (int i = 0; i < len; i++) est[(size_t)sc * len + i] += o[(size_t)sc * vl + ms - off[k] + i];
-            m += (size_t)ht_view_segments(p, vl) * mask_per_seg;
-            free(o);
+        /* the bag (:585-642): each model's estimate weighted per stem and summed in model order
+         * (float), then divided by the weights' sum and mapped back by the mono statistics */
+        const int M = p->n_models > 1 ? p->n_models : 1;
+        const size_t mask_per_model = (size_t)or_ht_n_segments(p, len) * S * 2 * C * (HT_NFFT / 2) * or_ht_n_frames(p);
+        float* res = (float*)malloc(sizeof(float) * n_out);
+        float* totals = (float*)calloc((size_t)S, sizeof(float));
+        memset(est, 0, sizeof(float) * n_out);
+        for (int mi = 0; mi < M && !rc; mi++) {
+            rc = ht_model(p, mix, len, mask + (size_t)mi * mask_per_model, weight, res);
+            for (int s = 0; s < S && !rc; s++) {
+                const float w = p->bag ? p->bag[(size_t)mi * S + s] : 1.0f;     /* :630 */
+                totals[s] += w;
+                if (w == 0.0f) continue;
+                for (size_t i = 0; i < (size_t)C * len; i++) est[(size_t)s * C * len + i] += w * res[(size_t)s * C * len + i];
+            }
         }
-        for (size_t i = 0; i < (size_t)S * C * len && !rc; i++) est[i] /= p->shifts;
-        free(off); free(pm);
+        for (int s = 0; s < S && !rc; s++)                                   /* :638-642 */
+            for (size_t i = 0; i < (size_t)C * len; i++) {
+                float* v = &est[(size_t)s * C * len + i];
+                *v = (float)(*v / totals[s] * ref_std + ref_mean);
+            }
+        free(totals); free(res);
     }
-    /* one model, weight 1: v / 1 * ref_std + ref_mean (:629-642) */
-    if (p->mono_norm && !rc)
-        for (size_t i = 0; i < (size_t)S * C * len; i++) est[i] = (float)(est[i] * ref_std + ref_mean);
     free(weight); free(mix);
     return rc;
 }

@@ -92,9 +92,12 @@ typedef struct {
     int shifts;          /* random shifts averaged (:610-626); 0 = one pass */
     unsigned seed;       /* std::mt19937 seed of the shift offsets */
     int sample_rate;     /* max shift = sample_rate / 2; 0 = 44100 */
+    int n_models;        /* bag of models (:585-642); <= 1 with bag NULL: one model */
+    const float* bag;    /* [n_models][S] weights, or NULL for all 1 */
 } or_ht_params;
 /* mask: per segment [S][2C][F = n_fft/2][T] float (re plane 2c, im plane 2c+1), segments
- * back to back (with shifts: every shift's segments, shift by shift). out: [S][C][len]. */
+ * back to back (with shifts: every shift's segments, shift by shift; with a bag, every
+ * model's masks, model by model). out: [S][C][len]. */
 int or_ht_n_segments(const or_ht_params* p, int len);
 int or_ht_n_frames(const or_ht_params* p);
 int or_ht_separate(const or_ht_params* p, const float* mix, int len, const float* mask, float* out);

@@ -44,7 +44,7 @@ class HTDemucsConfig(C.Structure):
     _fields_ = [("size", C.c_uint32), ("n_channels", C.c_int32), ("n_sources", C.c_int32),
                 ("segment", C.c_int32), ("overlap", C.c_float), ("mono_norm", C.c_int32),
                 ("cac_norm", C.c_int32), ("shifts", C.c_int32), ("seed", C.c_uint32),
-                ("sample_rate", C.c_int32)]
+                ("sample_rate", C.c_int32), ("n_models", C.c_int32), ("bag_weights", C.POINTER(C.c_float))]
 
 
 class RoFormerConfig(C.Structure):
@@ -67,7 +67,7 @@ class PlanInfo(C.Structure):
     _fields_ = [("size", C.c_uint32), ("arch", C.c_int32), ("n_samples", C.c_int64),
                 ("n_channels", C.c_int32), ("n_out_sources", C.c_int32), ("n_chunks", C.c_int64),
                 ("n_frames", C.c_int64), ("mask_floats_per_chunk", C.c_int64),
-                ("out_floats", C.c_int64), ("scratch_bytes", C.c_int64)]
+                ("out_floats", C.c_int64), ("scratch_bytes", C.c_int64), ("n_models", C.c_int32)]
 
 
 class VrBandC(C.Structure):
@@ -125,6 +125,8 @@ _SIGNATURES = {
                                       C.c_void_p]),
     "stg_separate_dual_mono": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "stg_separate_host_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.POINTER(RunOptions)]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.POINTER(RunOptions)]),
     "stg_plan_network_info": (C.c_int32, [C.c_void_p, C.POINTER(NetworkInfo)]),
@@ -365,13 +367,24 @@ class Engine:
 
     # -- plans ---------------------------------------------------------------------------
     def plan_htdemucs(self, n_samples, n_channels=2, n_sources=4, segment=343980, overlap=-1.0,
-                      mono_norm=True, cac_norm=True, shifts=0, seed=0, sample_rate=44100):
+                      mono_norm=True, cac_norm=True, shifts=0, seed=0, sample_rate=44100, n_models=1,
+                      bag_weights=None):
         """HTDemucs.separate (src/htdemucs.cpp:534-642). Both normalisations are on by default,
         as in the reference; mono_norm / cac_norm False leave the mix / spectrogram raw.
         shifts > 0 averages that many random shifts (offsets from std::mt19937(seed)); the
-        plan's chunks are then every shift's segments, shift by shift."""
+        plan's chunks are then every shift's segments, shift by shift. n_models > 1 or
+        bag_weights ([n_models][n_sources]) make a bag of models: every model's masks, model
+        after model, weighted per stem (:628-642)."""
         cfg = HTDemucsConfig(C.sizeof(HTDemucsConfig), n_channels, n_sources, segment, overlap,
                              int(bool(mono_norm)), int(bool(cac_norm)), shifts, seed, sample_rate)
+        keep = None
+        if bag_weights is not None:
+            keep = np.ascontiguousarray(bag_weights, dtype=np.float32).reshape(-1)
+            n_models = keep.size // n_sources
+            if keep.size != n_models * n_sources or n_models < 1:
+                raise StemsError(1, "bag_weights must be [n_models][n_sources]")
+            cfg.bag_weights = keep.ctypes.data_as(C.POINTER(C.c_float))
+        cfg.n_models = n_models
         h = C.c_void_p()
         self._check(lib().stg_plan_htdemucs(self._h, C.byref(cfg), n_samples, C.byref(h)), "plan_htdemucs")
         return Plan(self, h)
@@ -418,6 +431,7 @@ class Plan:
         self.mask_floats = info.mask_floats_per_chunk * info.n_chunks
         self.out_floats = info.out_floats
         self.scratch_bytes = info.scratch_bytes
+        self.n_models = info.n_models
 
     @property
     def out_shape(self):
@@ -446,18 +460,29 @@ class Plan:
         self.engine._check(lib().stg_separate_dual_mono(self._h, _ptr(mix), _ptr(mask), _ptr(out),
                                                         _stream_of(stream, mix, mask, out)), "separate_dual_mono")
 
-    def separate(self, mix, mask, out, stream=None, chunks_per_batch=0, progress=None, should_cancel=None):
-        """Device buffers (torch CUDA tensors or pointers): mix [C][n], mask, out [S][C][n]."""
-        st = _stream_of(stream, mix, mask, out)
+    @staticmethod
+    def _options(chunks_per_batch, progress, should_cancel):
+        """stg_run_options for the callbacks (SeparateOptions.progress / should_cancel), or None;
+        the ctypes callbacks are kept alive on the returned struct."""
         if progress is None and should_cancel is None and chunks_per_batch <= 0:
+            return None
+        opts = RunOptions()
+        opts.size = C.sizeof(RunOptions)
+        opts.chunks_per_batch = chunks_per_batch
+        opts.on_progress = PROGRESS_FN(lambda u, d, t: progress(d, t)) if progress else PROGRESS_FN()
+        opts.should_cancel = (CANCEL_FN(lambda u: int(bool(should_cancel()))) if should_cancel
+                              else CANCEL_FN())
+        return opts
+
+    def separate(self, mix, mask, out, stream=None, chunks_per_batch=0, progress=None, should_cancel=None):
+        """Device buffers (torch CUDA tensors or pointers): mix [C][n], mask, out [S][C][n].
+        progress(done, total) and should_cancel() as the reference's SeparateOptions; a
+        cancelled run raises Cancelled."""
+        st = _stream_of(stream, mix, mask, out)
+        opts = self._options(chunks_per_batch, progress, should_cancel)
+        if opts is None:
             rc = lib().stg_separate(self._h, _ptr(mix), _ptr(mask), _ptr(out), st)
         else:
-            opts = RunOptions()
-            opts.size = C.sizeof(RunOptions)
-            opts.chunks_per_batch = chunks_per_batch
-            opts.on_progress = PROGRESS_FN(lambda u, d, t: progress(d, t)) if progress else PROGRESS_FN()
-            opts.should_cancel = (CANCEL_FN(lambda u: int(bool(should_cancel()))) if should_cancel
-                                  else CANCEL_FN())
             rc = lib().stg_separate_ex(self._h, _ptr(mix), _ptr(mask), _ptr(out), st, C.byref(opts))
         self.engine._check(rc, "separate")
         return out
@@ -519,8 +544,11 @@ class Plan:
         st = stream if (stream is None or isinstance(stream, int)) else stream.cuda_stream
         self.engine._check(lib().stg_separate_host(self._h, h_mix, h_mask, h_out, st), "separate_host")
 
-    def separate_host(self, mix, mask, out=None, stream=None):
-        """Host buffers (numpy float32); returns the [S][C][n] result."""
+    def separate_host(self, mix, mask, out=None, stream=None, chunks_per_batch=0, progress=None,
+                      should_cancel=None):
+        """Host buffers (numpy float32); returns the [S][C][n] result. With progress /
+        should_cancel (stg_separate_host_ex), a cancelled run raises Cancelled and leaves out
+        untouched."""
         mix = np.ascontiguousarray(mix, dtype=np.float32)
         mask = np.ascontiguousarray(mask, dtype=np.float32)
         if mix.size != self.n_channels * self.n_samples or mask.size != self.mask_floats:
@@ -528,7 +556,12 @@ class Plan:
         if out is None:
             out = np.empty(self.out_shape, np.float32)
         st = stream if (stream is None or isinstance(stream, int)) else stream.cuda_stream
-        rc = lib().stg_separate_host(self._h, mix.ctypes.data, mask.ctypes.data, out.ctypes.data, st)
+        opts = self._options(chunks_per_batch, progress, should_cancel)
+        if opts is None:
+            rc = lib().stg_separate_host(self._h, mix.ctypes.data, mask.ctypes.data, out.ctypes.data, st)
+        else:
+            rc = lib().stg_separate_host_ex(self._h, mix.ctypes.data, mask.ctypes.data, out.ctypes.data, st,
+                                            C.byref(opts))
         self.engine._check(rc, "separate_host")
         return out
 

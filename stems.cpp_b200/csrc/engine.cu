@@ -2,6 +2,8 @@
 // engine.h.
 #include "engine.h"
 
+#include <cstring>
+
 #define STG_VERSION_STRING "stems-b200 spectral 0.1 (stems_gpu abi 1)"
 
 using namespace stg;
@@ -79,6 +81,13 @@ STG_API stg_status stg_plan_last_timing_detail(stg_plan* p, float* prep_ms, floa
 }
 
 STG_API stg_status stg_plan_htdemucs(stg_engine* e, const stg_htdemucs_config* c, int64_t n, stg_plan** out) {
+    // a config without the bag-of-models fields is a single model: read it into a full one
+    stg_htdemucs_config full{};
+    if (c && c->size >= STG_HTDEMUCS_CONFIG_V1_SIZE && c->size < sizeof(full)) {
+        std::memcpy(&full, c, c->size);
+        full.size = sizeof(full);
+        c = &full;
+    }
     return make_plan(e, c, n, out, build_htdemucs);
 }
 STG_API stg_status stg_plan_roformer(stg_engine* e, const stg_roformer_config* c, int64_t n, stg_plan** out) {
@@ -95,13 +104,14 @@ STG_API void stg_plan_destroy(stg_plan* p) {
 }
 
 STG_API stg_status stg_plan_get_info(const stg_plan* p, stg_plan_info* info) {
-    if (!p || !info || info->size < sizeof(stg_plan_info)) return STG_INVALID_ARGUMENT;
+    if (!p || !info || info->size < STG_PLAN_INFO_V1_SIZE) return STG_INVALID_ARGUMENT;
     const HostPlan& H = p->H;
     info->arch = H.arch;
     info->n_samples = H.len;
     info->n_channels = H.C;
     info->n_out_sources = H.S_out;
-    info->n_chunks = H.n_chunks();
+    info->n_chunks = H.n_mask_chunks();
+    if (info->size >= sizeof(stg_plan_info)) info->n_models = H.n_models;
     info->n_frames = H.g.T;
     info->mask_floats_per_chunk = H.mask_per_chunk;
     info->out_floats = H.out_floats();
@@ -143,7 +153,7 @@ STG_API stg_status stg_separate_dual_mono(stg_plan* p, const float* d_mix, const
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         const size_t row = sizeof(float) * (size_t)H.len;
         p->dm_out.reserve(row * H.S_out, "dual-mono scratch");
-        const int64_t mask_per_channel = H.mask_per_chunk * (int64_t)H.chunks.size();
+        const int64_t mask_per_channel = H.mask_floats();
         for (int c = 0; c < 2; c++) {                                  // separator.cpp:36-43
             p->run(d_mix + (size_t)c * H.len, d_mask + c * mask_per_channel, p->dm_out.as<float>(), st, nullptr);
             // stem s of this channel to row s * 2 + c of the stereo result
@@ -153,71 +163,88 @@ STG_API stg_status stg_separate_dual_mono(stg_plan* p, const float* d_mix, const
     });
 }
 
-// mask batches of stg_separate_host
+// mask batches of stg_separate_host (per bag member)
 constexpr int kHostBatches = 8;
+
+namespace {
+void separate_host(stg_plan* p, const float* h_mix, const float* h_mask, float* h_out, cudaStream_t st,
+                   const stg_run_options* user_opt) {
+    if (!h_mix || !h_mask || !h_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+    if (user_opt && user_opt->size < sizeof(stg_run_options)) fail(STG_INVALID_ARGUMENT, "options.size is too small");
+    cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+    const HostPlan& H = p->H;
+    const size_t mix_b = sizeof(float) * (size_t)H.C * H.len;
+    const size_t mask_b = sizeof(float) * (size_t)H.mask_floats();
+    const size_t out_b = sizeof(float) * (size_t)H.out_floats();
+    p->s_mix.reserve(mix_b, "staging");
+    p->s_mask.reserve(mask_b, "staging");
+    p->s_out.reserve(out_b, "staging");
+    // on a failure or a cancellation, no copy may still read or write the caller's host buffers
+    // after the return
+    try {
+        cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
+        // The masks are most of the bytes (RoFormer cfg1: 934 MB against 21 MB of audio) and
+        // the PCIe copy takes some 30 times the kernels. They come in batch by batch on a copy
+        // stream, and each batch's kernels (HTDemucs: its transposition, then its back kernel)
+        // wait only for their own masks, so the kernels run under the next batches' copies.
+        // The batches are launch_plan's: per bag member, runs of `per` chunks.
+        const int n = (int)H.chunks.size(), M = H.bag.empty() ? 1 : H.n_models;
+        const int per = (user_opt && user_opt->chunks_per_batch > 0) ? std::min(user_opt->chunks_per_batch, n)
+                                                                      : (n + std::min(n, kHostBatches) - 1) / std::min(n, kHostBatches);
+        const int per_model = (n + per - 1) / per;
+        stg_run_options o{};
+        if (user_opt) o = *user_opt;
+        o.size = sizeof(o);
+        o.chunks_per_batch = per;
+        if (M * per_model <= 1) {
+            cuda_check(cudaMemcpyAsync(p->s_mask.p, h_mask, mask_b, cudaMemcpyHostToDevice, st), "copy masks in");
+            p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o);
+        } else {
+            if (!p->copy_st) {
+                cuda_check(cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking), "cudaStreamCreate");
+                cuda_check(cudaEventCreateWithFlags(&p->copy_fork, cudaEventDisableTiming), "cudaEventCreate");
+            }
+            while ((int)p->copy_ev.size() < M * per_model) {
+                cudaEvent_t e = nullptr;
+                cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+                p->copy_ev.push_back(e);
+            }
+            const size_t chunk_b = sizeof(float) * (size_t)H.mask_per_chunk;
+            // the copies overwrite the staging that the caller's earlier work on st may still read
+            cuda_check(cudaEventRecord(p->copy_fork, st), "cudaEventRecord");
+            cuda_check(cudaStreamWaitEvent(p->copy_st, p->copy_fork, 0), "cudaStreamWaitEvent");
+            int b = 0;
+            for (int m = 0; m < M; m++)
+                for (int c0 = 0; c0 < n; c0 += per, b++) {
+                    const size_t first = (size_t)m * n + c0, nb = (size_t)std::min(per, n - c0);
+                    cuda_check(cudaMemcpyAsync(static_cast<char*>(p->s_mask.p) + chunk_b * first,
+                                               reinterpret_cast<const char*>(h_mask) + chunk_b * first, chunk_b * nb,
+                                               cudaMemcpyHostToDevice, p->copy_st),
+                               "copy masks in");
+                    cuda_check(cudaEventRecord(p->copy_ev[b], p->copy_st), "cudaEventRecord");
+                }
+            p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o, 0, -1, &p->copy_ev);
+        }
+        cuda_check(cudaMemcpyAsync(h_out, p->s_out.p, out_b, cudaMemcpyDeviceToHost, st), "copy result out");
+        cuda_check(cudaStreamSynchronize(st), "separation");
+    } catch (...) {
+        cudaStreamSynchronize(st);
+        if (p->copy_st) cudaStreamSynchronize(p->copy_st);
+        throw;
+    }
+}
+} // namespace
 
 STG_API stg_status stg_separate_host(stg_plan* p, const float* h_mix, const float* h_mask, float* h_out,
                                      void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;
-    return guard(p->engine, [&] {
-        if (!h_mix || !h_mask || !h_out) fail(STG_INVALID_ARGUMENT, "null buffer");
-        cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
-        const cudaStream_t st = static_cast<cudaStream_t>(stream);
-        const HostPlan& H = p->H;
-        const size_t mix_b = sizeof(float) * (size_t)H.C * H.len;
-        const size_t mask_b = sizeof(float) * (size_t)H.mask_per_chunk * H.chunks.size();
-        const size_t out_b = sizeof(float) * (size_t)H.out_floats();
-        p->s_mix.reserve(mix_b, "staging");
-        p->s_mask.reserve(mask_b, "staging");
-        p->s_out.reserve(out_b, "staging");
-        // on a failure, no copy may still read or write the caller's host buffers after the return
-        try {
-            cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
-            // The masks are most of the bytes (RoFormer cfg1: 934 MB against 21 MB of audio) and
-            // the PCIe copy takes some 30 times the kernels. They come in batch by batch on a copy
-            // stream, and each batch's kernels (HTDemucs: its transposition, then its back kernel)
-            // wait only for their own masks, so the kernels run under the next batches' copies.
-            const int n = (int)H.chunks.size();
-            const int batches = std::min(n, kHostBatches);
-            if (batches <= 1) {
-                cuda_check(cudaMemcpyAsync(p->s_mask.p, h_mask, mask_b, cudaMemcpyHostToDevice, st), "copy masks in");
-                p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr);
-            } else {
-                if (!p->copy_st) {
-                    cuda_check(cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking), "cudaStreamCreate");
-                    cuda_check(cudaEventCreateWithFlags(&p->copy_fork, cudaEventDisableTiming), "cudaEventCreate");
-                }
-                while ((int)p->copy_ev.size() < batches) {
-                    cudaEvent_t e = nullptr;
-                    cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
-                    p->copy_ev.push_back(e);
-                }
-                const int per = (n + batches - 1) / batches;
-                const size_t chunk_b = sizeof(float) * (size_t)H.mask_per_chunk;
-                // the copies overwrite the staging that the caller's earlier work on st may still read
-                cuda_check(cudaEventRecord(p->copy_fork, st), "cudaEventRecord");
-                cuda_check(cudaStreamWaitEvent(p->copy_st, p->copy_fork, 0), "cudaStreamWaitEvent");
-                for (int b = 0, c0 = 0; c0 < n; b++, c0 += per) {
-                    const int nb = std::min(per, n - c0);
-                    cuda_check(cudaMemcpyAsync(static_cast<char*>(p->s_mask.p) + chunk_b * c0,
-                                               reinterpret_cast<const char*>(h_mask) + chunk_b * c0,
-                                               chunk_b * nb, cudaMemcpyHostToDevice, p->copy_st),
-                               "copy masks in");
-                    cuda_check(cudaEventRecord(p->copy_ev[b], p->copy_st), "cudaEventRecord");
-                }
-                stg_run_options o{};
-                o.size = sizeof(o);
-                o.chunks_per_batch = per;
-                p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, &o, 0, -1, &p->copy_ev);
-            }
-            cuda_check(cudaMemcpyAsync(h_out, p->s_out.p, out_b, cudaMemcpyDeviceToHost, st), "copy result out");
-            cuda_check(cudaStreamSynchronize(st), "separation");
-        } catch (...) {
-            cudaStreamSynchronize(st);
-            if (p->copy_st) cudaStreamSynchronize(p->copy_st);
-            throw;
-        }
-    });
+    return guard(p->engine, [&] { separate_host(p, h_mix, h_mask, h_out, static_cast<cudaStream_t>(stream), nullptr); });
+}
+
+STG_API stg_status stg_separate_host_ex(stg_plan* p, const float* h_mix, const float* h_mask, float* h_out,
+                                        void* stream, const stg_run_options* opt) {
+    if (!p) return STG_INVALID_ARGUMENT;
+    return guard(p->engine, [&] { separate_host(p, h_mix, h_mask, h_out, static_cast<cudaStream_t>(stream), opt); });
 }
 
 // ---- the halves around a real network ----------------------------------------------------
@@ -228,9 +255,17 @@ STG_API stg_status stg_plan_network_info(const stg_plan* p, stg_network_info* in
     return STG_OK;
 }
 
+namespace {
+void no_bag(const HostPlan& H) {
+    if (!H.bag.empty())
+        fail(STG_UNSUPPORTED, "a bag of models runs through stg_separate or stg_separate_network, not the halves");
+}
+} // namespace
+
 STG_API stg_status stg_front(stg_plan* p, const float* d_mix, int32_t first, int32_t n, float* d_net_in, void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] {
+        no_bag(p->H);
         cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         launch_front(p->H, p->D, p->front_mix(d_mix, first, st), first, n, d_net_in, st);
@@ -241,6 +276,7 @@ STG_API stg_status stg_back(stg_plan* p, const float* d_mix, const float* d_net_
                             void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] {
+        no_bag(p->H);
         cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
         launch_back(p->H, p->D, d_mix, d_net_out, first, n, static_cast<cudaStream_t>(stream));
     });
@@ -249,6 +285,7 @@ STG_API stg_status stg_back(stg_plan* p, const float* d_mix, const float* d_net_
 STG_API stg_status stg_finish(stg_plan* p, const float* d_mix, float* d_out, void* stream) {
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] {
+        no_bag(p->H);
         cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
         launch_finish(p->H, p->D, d_mix, d_out, static_cast<cudaStream_t>(stream));
     });
@@ -264,23 +301,32 @@ STG_API stg_status stg_separate_network(stg_plan* p, const float* d_mix, float* 
         cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         const HostPlan& H = p->H;
-        const int G = (int)H.chunks.size();
+        const int G = (int)H.chunks.size(), M = H.bag.empty() ? 1 : H.n_models;
         const int per = per_batch > 0 ? std::min(per_batch, G) : G;
         p->n_in.reserve(std::max<size_t>(16, sizeof(float) * (size_t)H.net_in_per_chunk * per), "network input");
         p->n_out.reserve(std::max<size_t>(16, sizeof(float) * (size_t)H.net_out_per_chunk * per), "network output");
-        for (int b0 = 0; b0 < G; b0 += per) {
-            if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
-            const int nb = std::min(per, G - b0);
-            launch_front(H, p->D, p->front_mix(d_mix, b0, st), b0, nb, p->n_in.as<float>(), st);
-            if (network(user, b0, nb, p->n_in.as<float>(), p->n_out.as<float>(), stream) != 0)
-                fail(STG_MODEL_ERROR, "the network callback failed");
-            launch_back(H, p->D, d_mix, p->n_out.as<float>(), b0, nb, st);
-            if (opt && opt->on_progress) {
-                cuda_check(cudaStreamSynchronize(st), "spectral kernels");
-                opt->on_progress(opt->user, b0 + nb, G);
+        const auto cancelled = [&] { return opt && opt->should_cancel && opt->should_cancel(opt->user); };
+        const int total = H.progress_total > 0 ? H.progress_total : M * G;
+        // a bag of models: member m sees chunk indices m * G + k, every member's chunks through
+        // the network and the back half before its combine adds its weighted stems
+        for (int m = 0; m < M; m++) {
+            for (int b0 = 0; b0 < G; b0 += per) {
+                if (cancelled()) fail(STG_CANCELLED, "cancelled");
+                const int nb = std::min(per, G - b0);
+                launch_front(H, p->D, p->front_mix(d_mix, m == 0 ? b0 : 1, st), b0, nb, p->n_in.as<float>(), st);
+                if (network(user, m * G + b0, nb, p->n_in.as<float>(), p->n_out.as<float>(), stream) != 0)
+                    fail(STG_MODEL_ERROR, "the network callback failed");
+                launch_back(H, p->D, d_mix, p->n_out.as<float>(), b0, nb, st);
+                if (opt && opt->on_progress) {
+                    cuda_check(cudaStreamSynchronize(st), "spectral kernels");
+                    const int done = m * G + b0 + nb;
+                    const bool final_batch = m == M - 1 && b0 + nb >= G;
+                    opt->on_progress(opt->user, final_batch && H.progress_final_total ? total : done, total);
+                }
             }
+            if (m == M - 1 && H.cancel_after_last && cancelled()) fail(STG_CANCELLED, "cancelled");
+            launch_finish(H, p->D, d_mix, d_out, st, m);
         }
-        launch_finish(H, p->D, d_mix, d_out, st);
     });
 }
 

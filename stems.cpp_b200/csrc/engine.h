@@ -100,7 +100,7 @@ struct stg_plan {
     stg_engine* engine = nullptr;
     HostPlan H;
     PlanDevice D;
-    DevBuf d_chunks, d_groups, d_w, d_env, d_envp, d_btab, d_ebeg, d_ent, d_binv;
+    DevBuf d_chunks, d_groups, d_w, d_env, d_envp, d_btab, d_ebeg, d_ent, d_binv, d_bag, d_bag_tot;
     DevBuf d_y, d_tr;
     DevBuf d_mixn, d_mono, d_cac_part, d_cac_stats;   // scratch of the HTDemucs normalisations
     DevBuf d_mask_t;                                  // t-major masks (HTDemucs, TFC-TDF)
@@ -143,6 +143,12 @@ struct stg_plan {
         upload(d_ebeg, H.ebeg, "band table");
         upload(d_ent, H.ent, "band table");
         upload(d_binv, H.binv, "band table");
+        if (!H.bag.empty()) {
+            upload(d_bag, H.bag, "bag weights");
+            upload(d_bag_tot, H.bag_tot, "bag weights");
+            D.bag = d_bag.as<float>();
+            D.bag_tot = d_bag_tot.as<float>();
+        }
         d_y.reserve(std::max<size_t>(16, H.y_bytes()), "chunk outputs");
         d_tr.reserve(std::max<size_t>(16, H.tr_bytes()), "tile partials");
         if (H.mono_norm) {

@@ -112,6 +112,7 @@ struct stg_model {
     uint64_t data_start = 0;
     // the configurations, and the arrays their pointers borrow
     std::vector<int32_t> band_sizes, band_freqs;
+    std::vector<float> bag;
     std::vector<stg_vr_band> vr_bands;
     std::vector<stg_vr_fir> vr_firs;
     std::vector<std::vector<float>> fir_taps;
@@ -147,6 +148,11 @@ struct stg_model {
         const Value& v = at("stems.sources");
         if (v.type != T_ARRAY || v.elem != T_STRING) fail(STG_MODEL_ERROR, path + ": bad stems.sources");
         return v.strs.size();
+    }
+    std::vector<float> floats(const std::string& k) const {
+        const Value& v = at(k);
+        if (v.type != T_ARRAY || v.elem != T_F32) fail(STG_MODEL_ERROR, path + ": bad " + k);
+        return std::vector<float>(v.nums.begin(), v.nums.end());
     }
     std::vector<int32_t> ints(const std::string& k) const {
         const Value& v = at(k);
@@ -249,7 +255,7 @@ STG_API int32_t stg_model_sample_rate(const stg_model* m) {
 
 STG_API stg_status stg_model_htdemucs_config(const stg_model* m, stg_htdemucs_config* c, char* message,
                                              size_t message_size) {
-    if (!m || !c || c->size < sizeof(stg_htdemucs_config)) return STG_INVALID_ARGUMENT;
+    if (!m || !c || c->size < STG_HTDEMUCS_CONFIG_V1_SIZE) return STG_INVALID_ARGUMENT;
     return run(message, message_size, [&] {
         if (m->arch != "htdemucs") fail(STG_MODEL_ERROR, m->path + ": not an htdemucs GGUF");   // :483
         const int64_t sr = m->integer("stems.samplerate"), num = m->integer("stems.segment_num"),
@@ -265,6 +271,22 @@ STG_API stg_status stg_model_htdemucs_config(const stg_model* m, stg_htdemucs_co
         c->mono_norm = 1;
         c->cac_norm = 1;
         c->sample_rate = (int32_t)sr;
+        // the bag (:493-499): stems.n_models and stems.bag_weights [n_models][sources]; a file
+        // without them is one model
+        if (m->has("stems.n_models") || m->has("stems.bag_weights")) {
+            const int64_t n_models = m->integer("stems.n_models");
+            std::vector<float> w = m->floats("stems.bag_weights");
+            if (n_models < 1 || n_models > 64 || w.size() != (size_t)n_models * (size_t)c->n_sources)
+                fail(STG_MODEL_ERROR, m->path + ": stems.bag_weights has the wrong size");
+            if (size >= sizeof(stg_htdemucs_config)) {
+                auto* mm = const_cast<stg_model*>(m);
+                mm->bag = std::move(w);
+                c->n_models = (int32_t)n_models;
+                c->bag_weights = mm->bag.data();
+            } else if (n_models > 1) {
+                fail(STG_INVALID_ARGUMENT, "a bag of models needs the full stg_htdemucs_config (n_models, bag_weights)");
+            }
+        }
     });
 }
 

@@ -306,6 +306,26 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 // order (src/roformer.cpp:337-340, src/tfc_tdf.cpp:420-422, src/htdemucs.cpp:598-601), each
 // value the chunk output Y plus, on a tile boundary, the previous tile's trailing partial Tr,
 // and divide by the summed weight; then average the groups and finish (epilogue).
+// The value the separator returns for row k (stem k / C) at output sample i, from this launch's
+// estimate v: the shift average's division, compensation, then either the mono-mix inverse
+// (src/htdemucs.cpp:641) or, for a bag of models, this model's weighted term added to the
+// previous models' sum in out (float products and sums in model order, :628-635) and, after
+// the last model, the division by the weights' sum and the mono inverse (:638-642).
+__device__ __forceinline__ float finish_value(const CombineParams& p, int k, int64_t i, float v) {
+    if (p.shift_mean == 1) v = v / (float)p.n_groups;
+    v *= p.compensate;
+    if (p.bag) {
+        const int s = k / p.C;
+        const float w = __ldg(p.bag + p.bag_model * p.S + s);
+        float acc = p.bag_model == 0 ? 0.0f : p.out[(int64_t)k * p.len + i];
+        if (w != 0.0f) acc = __fadd_rn(acc, __fmul_rn(w, v));
+        if (!p.bag_last) return acc;
+        v = __fdiv_rn(acc, __ldg(p.bag_tot + s));
+    }
+    if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);
+    return v;
+}
+
 template <int SC>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     const int i = (int)(p.i_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x);
@@ -376,9 +396,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     float outv[SC];
 #pragma unroll
     for (int k = 0; k < SC; k++) {
-        float v = p.shift_mean == 1 ? res[k] / (float)p.n_groups : res[k];
-        v *= p.compensate;
-        if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
+        const float v = finish_value(p, k, i, res[k]);
         outv[k] = v;
         p.out[(int64_t)k * p.len + i] = v;
     }
@@ -495,12 +513,7 @@ __global__ void __launch_bounds__(256) combine_kernel4(const CombineParams p) {
 #pragma unroll
     for (int s = 0; s < V; s++)
 #pragma unroll
-        for (int k = 0; k < SC; k++) {
-            float v = p.shift_mean == 1 ? res[s][k] / (float)p.n_groups : res[s][k];
-            v *= p.compensate;
-            if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
-            outv[s][k] = v;
-        }
+        for (int k = 0; k < SC; k++) outv[s][k] = s < nv ? finish_value(p, k, i0 + s, res[s][k]) : 0.0f;
     // rows of 4 samples as one 16-byte store where the row offset allows it
     const bool vec = nv == V && (p.len % V) == 0 && (i0 % V) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.out) % (sizeof(float) * V)) == 0;

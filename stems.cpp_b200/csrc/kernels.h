@@ -127,6 +127,12 @@ struct CombineParams {
     int complement;            // 1: first stem; 2: all stems (TFC-TDF) subtracted from the mix
     const float* mix;          // for the complement
     const double* mono_stats;  // HTDemucs mono-mix normalisation (mean, std), or null
+    // HTDemucs bag of models (src/htdemucs.cpp:628-642), or bag == null: out accumulates
+    // bag[model][s] * (this model's stem s) (the first model starts from zero), and the last
+    // model divides by bag_tot[s] and then applies mono_stats
+    const float* bag;          // [n_models][S]
+    const float* bag_tot;      // [S]
+    int bag_model, bag_last;
     float* out;                // [S(+1)][C][len]
 };
 

@@ -7,14 +7,23 @@
 // and the output buffer; the tables and the scratch of the fused kernel live in one static
 // device array of 64 MiB, reserved on every GPU that loads this library until the process
 // exits. The kernels are the same as stg_separate's.
+//
+// Contexts. The call runs in the context current on the calling thread when that context
+// belongs to `device` (a host application's own context included), and otherwise makes
+// `device`'s primary context current for the call and puts the caller's context back
+// afterwards. A __device__ array has one address per context, so the address is looked up
+// (cudaGetSymbolAddress) once per context, on that context's first call.
 #include "../../include/stems_gpu_v1.h"
 #include "kernels.h"
 #include "plan.h"
+
+#include <cuda.h>
 
 #include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -23,25 +32,45 @@ namespace {
 using namespace stg;
 
 constexpr size_t kArenaBytes = (size_t)64 << 20;
-constexpr int kMaxDevices = 64;
 
 // The scratch arena. In host code this name is a host-side stand-in, not a device address:
-// kernels get the address that cudaGetSymbolAddress returns for the current device.
+// kernels get the address that cudaGetSymbolAddress returns for the current context.
 static __device__ __align__(256) unsigned char g_arena[kArenaBytes];
 
-std::mutex g_mutex;
-void* g_arena_address[kMaxDevices];   // per device, set by the first call on that device
-
-// The arena's device address on `device` (the current device), looked up once.
-void* arena_on(int device) {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    if (!g_arena_address[device]) {
-        void* p = nullptr;
-        cuda_check(cudaGetSymbolAddress(&p, g_arena), "cudaGetSymbolAddress(arena)");
-        g_arena_address[device] = p;
+// Driver entry points through the runtime, so that the library needs no link to libcuda.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxSetCurrentFn = CUresult (*)(CUcontext);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+struct Driver {
+    CtxGetCurrentFn get = nullptr;
+    CtxSetCurrentFn set = nullptr;
+    CtxGetIdFn id = nullptr;
+};
+template <class F> F entry_point(const char* name) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) {
+        cudaGetLastError();
+        return nullptr;
     }
-    return g_arena_address[device];
+    return reinterpret_cast<F>(p);
 }
+const Driver& driver() {
+    static const Driver d{entry_point<CtxGetCurrentFn>("cuCtxGetCurrent"), entry_point<CtxSetCurrentFn>("cuCtxSetCurrent"),
+                          entry_point<CtxGetIdFn>("cuCtxGetId")};
+    return d;
+}
+
+// Per context (by the driver's unique context ID, which a later context never reuses): the
+// arena's device address, and the host copy of the tables the last call uploaded, kept for the
+// life of the library so that no copy reads host memory a return has freed.
+struct ContextState {
+    unsigned char* arena = nullptr;
+    std::vector<unsigned char> staging;
+    size_t uploaded = 0;   // bytes of staging the arena holds (0: none)
+};
+std::mutex g_mutex;
+std::map<unsigned long long, ContextState> g_contexts;
 
 // Carves 256-byte aligned regions out of the arena, in order.
 struct Carver {
@@ -54,15 +83,41 @@ struct Carver {
 };
 
 template <class T>
-void put(unsigned char* base, size_t at, const std::vector<T>& v, cudaStream_t st) {
-    if (!v.empty())
-        cuda_check(cudaMemcpyAsync(base + at, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st),
-                   "copy a table into the arena");
+void stage(std::vector<unsigned char>& host, size_t at, const std::vector<T>& v) {
+    if (!v.empty()) std::memcpy(host.data() + at, v.data(), v.size() * sizeof(T));
 }
 
 void write_message(char* msg, size_t cap, const char* text) {
     if (msg && cap) std::snprintf(msg, cap, "%s", text);
 }
+
+// Makes a context of `device` current for the call: the caller's own when it is on `device`,
+// else the device's primary context; the destructor puts the caller's context back.
+struct ContextScope {
+    bool switched = false;
+    CUcontext previous = nullptr;
+    explicit ContextScope(int device) {
+        const Driver& d = driver();
+        if (!d.get || !d.set || !d.id) fail(STG_INTERNAL_ERROR, "the CUDA driver's context entry points are unavailable");
+        if (d.get(&previous) != CUDA_SUCCESS) fail(STG_INTERNAL_ERROR, "cuCtxGetCurrent failed");
+        int current = -1;
+        if (previous) cuda_check(cudaGetDevice(&current), "cudaGetDevice");
+        if (!previous || current != device) {
+            cuda_check(cudaSetDevice(device), "cudaSetDevice");
+            switched = true;
+        }
+    }
+    ~ContextScope() {
+        if (switched) driver().set(previous);
+    }
+    static unsigned long long current_id() {
+        CUcontext c = nullptr;
+        unsigned long long id = 0;
+        if (driver().get(&c) != CUDA_SUCCESS || !c || driver().id(c, &id) != CUDA_SUCCESS)
+            fail(STG_INTERNAL_ERROR, "no current CUDA context");
+        return id;
+    }
+};
 
 } // namespace
 
@@ -71,7 +126,6 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
                                                             const float* d_mask, float* d_out, void* stream,
                                                             char* message, size_t message_size) {
     write_message(message, message_size, "");
-    int previous = -1;
     stg_status status = STG_OK;
     try {
         if (!config || config->size < sizeof(stg_roformer_config))
@@ -82,10 +136,9 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
         if (n_samples > (int64_t)INT32_MAX / 4) fail(STG_INVALID_ARGUMENT, "input is too long");
         int n_dev = 0;
         cuda_check(cudaGetDeviceCount(&n_dev), "cudaGetDeviceCount");
-        if (device < 0 || device >= n_dev || device >= kMaxDevices) fail(STG_INVALID_ARGUMENT, "no such device");
-        cuda_check(cudaGetDevice(&previous), "cudaGetDevice");
-        cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        unsigned char* arena = static_cast<unsigned char*>(arena_on(device));
+        if (device < 0 || device >= n_dev) fail(STG_INVALID_ARGUMENT, "no such device");
+        // the plan's tile size asks the current device for its resident CTAs: the context first
+        ContextScope scope(device);
 
         HostPlan H;
         H.len = n_samples;
@@ -99,12 +152,14 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
         const size_t o_groups = c.take(H.groups.size() * sizeof(ChunkGroup));
         const size_t o_w = c.take(H.W.size() * sizeof(float));
         const size_t o_env = c.take(H.env.size() * sizeof(float));
+        const size_t o_envp = c.take(std::max<size_t>(1, H.env_period.size()) * sizeof(float));
         const size_t o_btab = c.take(H.btab.size() * sizeof(int2));
         const size_t o_ebeg = c.take(H.ebeg.size() * sizeof(int));
         const size_t o_ent = c.take(std::max<size_t>(1, H.ent.size()) * sizeof(int2));
         const size_t o_binv = c.take(H.binv.size() * sizeof(float));
         const size_t o_win = c.take(win.size() * sizeof(float));
         const size_t o_tw = c.take(tw.size() * sizeof(float2));
+        const size_t tables = c.used;
         const size_t o_y = c.take(H.y_bytes());
         const size_t o_tr = c.take(std::max<size_t>(16, H.tr_bytes()));
         if (c.used > kArenaBytes) {
@@ -115,17 +170,38 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
             fail(STG_INVALID_ARGUMENT, text);
         }
 
+        // the tables as one block, laid out as in the arena
+        std::vector<unsigned char> next(tables, 0);
+        stage(next, o_chunks, H.chunks);
+        stage(next, o_groups, H.groups);
+        stage(next, o_w, H.W);
+        stage(next, o_env, H.env);
+        stage(next, o_envp, H.env_period);
+        stage(next, o_btab, H.btab);
+        stage(next, o_ebeg, H.ebeg);
+        stage(next, o_ent, H.ent);
+        stage(next, o_binv, H.binv);
+        stage(next, o_win, win);
+        stage(next, o_tw, tw);
+
+        std::lock_guard<std::mutex> lock(g_mutex);
+        ContextState& cs = g_contexts[ContextScope::current_id()];
+        if (!cs.arena) {   // once per context: the arena's address in it
+            void* p = nullptr;
+            cuda_check(cudaGetSymbolAddress(&p, g_arena), "cudaGetSymbolAddress(arena)");
+            cs.arena = static_cast<unsigned char*>(p);
+        }
+        unsigned char* arena = cs.arena;
+        // The previous call's tables are still in the arena when they are these very bytes (its
+        // scratch lies after them); otherwise one copy from the library's host staging.
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
-        put(arena, o_chunks, H.chunks, st);
-        put(arena, o_groups, H.groups, st);
-        put(arena, o_w, H.W, st);
-        put(arena, o_env, H.env, st);
-        put(arena, o_btab, H.btab, st);
-        put(arena, o_ebeg, H.ebeg, st);
-        put(arena, o_ent, H.ent, st);
-        put(arena, o_binv, H.binv, st);
-        put(arena, o_win, win, st);
-        put(arena, o_tw, tw, st);
+        if (cs.uploaded != tables || cs.staging != next) {
+            cs.uploaded = 0;
+            cs.staging.swap(next);
+            cuda_check(cudaMemcpyAsync(arena, cs.staging.data(), tables, cudaMemcpyHostToDevice, st),
+                       "copy the tables into the arena");
+            cs.uploaded = tables;
+        }
 
         // Every Y and Tr element the combine reads is written by the fused kernel of the same
         // call, so the arena needs no clearing between calls.
@@ -134,6 +210,7 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
         D.groups = reinterpret_cast<const ChunkGroup*>(arena + o_groups);
         D.W = reinterpret_cast<const float*>(arena + o_w);
         D.env = reinterpret_cast<const float*>(arena + o_env);
+        D.env_period = H.env_period.empty() ? nullptr : reinterpret_cast<const float*>(arena + o_envp);
         D.btab = reinterpret_cast<const int2*>(arena + o_btab);
         D.ebeg = reinterpret_cast<const int*>(arena + o_ebeg);
         D.ent = reinterpret_cast<const int2*>(arena + o_ent);
@@ -153,6 +230,5 @@ extern "C" STG_API stg_status stg_separate_roformer_noalloc(int device, const st
         status = STG_INTERNAL_ERROR;
         write_message(message, message_size, x.what());
     }
-    if (previous >= 0) cudaSetDevice(previous);
     return status;
 }

@@ -226,6 +226,23 @@ void build_htdemucs(HostPlan& P, const stg_htdemucs_config& c, int64_t len) {
     P.front_bins = P.back_bins = N / 2;
     P.net_in_per_chunk = (int64_t)2 * P.C * (N / 2) * T;
     P.net_out_per_chunk = P.mask_per_chunk;
+    // bag of models (:585-642): weights [n_models][S], their sums per stem
+    P.n_models = std::max(1, c.n_models);
+    if (c.n_models > 64) fail(STG_INVALID_ARGUMENT, "htdemucs: at most 64 models in a bag");
+    if (c.n_models > 1 || c.bag_weights) {
+        P.bag.assign((size_t)P.n_models * P.S, 1.0f);
+        if (c.bag_weights) std::copy(c.bag_weights, c.bag_weights + P.bag.size(), P.bag.begin());
+        P.bag_tot.assign(P.S, 0.0f);
+        for (int m = 0; m < P.n_models; m++)
+            for (int s = 0; s < P.S; s++) {
+                const float w = P.bag[(size_t)m * P.S + s];
+                if (!std::isfinite(w)) fail(STG_MODEL_ERROR, "htdemucs: bag weight is not finite");
+                P.bag_tot[s] += w;                                    // float sums in model order (:631)
+            }
+    }
+    // progress (:576-577): models x passes x ceil(len / stride) segment passes
+    P.progress_total = (int)std::min<int64_t>(INT32_MAX, (int64_t)P.n_models * std::max(1, shifts) *
+                                                             ((len + stride - 1) / stride));
     finish_plan(P, T + 4);                                            // 2 zero frames per side
 }
 
@@ -360,6 +377,13 @@ void build_roformer(HostPlan& P, const stg_roformer_config& c, int64_t len) {
     P.net_in_per_chunk = P.stem_stride;
     P.net_out_per_chunk = P.mask_per_chunk;                           // masks (:251-269)
     P.back_is_fused = true;
+    // progress (:444-451, 479): passes x the chunks of one pass over the track itself, the last
+    // report (total, total)
+    {
+        const int64_t Lp = pad ? len + 2 * (int64_t)border : len;
+        P.progress_total = (int)std::min<int64_t>(INT32_MAX, (int64_t)std::max(1, c.shifts) * ((Lp + step - 1) / step));
+        P.progress_final_total = true;
+    }
     finish_plan(P, T);
 }
 
@@ -459,6 +483,10 @@ void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len) {
     P.front_bins = P.back_bins = c.dim_f;
     P.net_in_per_chunk = (int64_t)4 * c.dim_f * c.dim_t;
     P.net_out_per_chunk = P.mask_per_chunk;
+    // progress (:411-425, 461-494, 577-579): one report per chunk; cancellation is polled once
+    // more after the last chunk
+    P.progress_total = (int)P.chunks.size();
+    P.cancel_after_last = true;
     finish_plan(P, c.dim_t);
 }
 
@@ -570,6 +598,34 @@ std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_
     return r;
 }
 
+namespace {
+// The combine of one run (or of one bag member's run) over output samples [b, e).
+CombineParams combine_params(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, int64_t b,
+                             int64_t e, int model) {
+    CombineParams c{};
+    c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
+    c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
+    c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
+    c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
+    c.step_out = P.step_out; c.max_out_len = P.max_out_len;
+    c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
+    c.W = D.W;
+    c.S = P.S; c.C = P.C; c.len = P.arch_out_len();
+    c.i_begin = b; c.i_end = e;
+    c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
+    c.complement = P.complement; c.mix = d_mix; c.out = d_out;
+    c.mono_stats = P.mono_norm ? D.mono : nullptr;
+    if (!P.bag.empty()) {
+        if (!D.bag || !D.bag_tot) fail(STG_INTERNAL_ERROR, "no device copy of the bag weights");
+        c.bag = D.bag;
+        c.bag_tot = D.bag_tot;
+        c.bag_model = model;
+        c.bag_last = model == P.n_models - 1;
+    }
+    return c;
+}
+} // namespace
+
 void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, const float* d_mask,
                  float* d_out, cudaStream_t st, const stg_run_options* opt, RunTiming* timing,
                  int64_t sample_begin, int64_t sample_end, const std::vector<cudaEvent_t>* ready) {
@@ -583,6 +639,10 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         whole ? std::vector<std::pair<int, int>>{{0, (int)P.chunks.size()}} : chunks_for(P, sample_begin, sample_end);
     int total = 0;
     for (const auto& rg : ranges) total += rg.second - rg.first;
+    // bag of models: every member runs the chunk list on its own masks, then its combine adds
+    // its weighted stems to d_out (src/htdemucs.cpp:585-636)
+    const int M = P.bag.empty() ? 1 : P.n_models;
+    const int64_t mask_per_model = P.mask_per_chunk * (int64_t)P.chunks.size();
     const bool timed = timing && timing->timed;
     if (timing) timing->launches = 0;
     if (timed) cuda_check(cudaEventRecord(timing->ev[0], st), "cudaEventRecord");
@@ -590,12 +650,13 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     // HTDemucs: the masks' transposition (HBM-bound) on the side stream, beside the
     // normalisation and the front kernel (latency-bound); every segment has its own slot of
     // the scratch. The fork orders it after the caller's earlier work, including the previous
-    // separation's back kernels, which read the same scratch.
-    const bool side_t = zpath && P.mask_planes && D.side && D.side_ev;
+    // separation's back kernels, which read the same scratch. (A bag's members transpose
+    // batch by batch on the caller's stream: they share the scratch.)
+    const bool side_t = zpath && P.mask_planes && D.side && D.side_ev && M == 1;
     const int per = std::max(1, (opt && opt->chunks_per_batch > 0) ? opt->chunks_per_batch : total);
     int n_batches = 0;
     for (const auto& rg : ranges) n_batches += (rg.second - rg.first + per - 1) / per;
-    if (ready && (int)ready->size() < n_batches) fail(STG_INTERNAL_ERROR, "fewer mask events than batches");
+    if (ready && (int)ready->size() < M * n_batches) fail(STG_INTERNAL_ERROR, "fewer mask events than batches");
     // the caller's stream waits for the side stream before anything after this point,
     // the back kernels, or a failure, can hand the masks back to the caller
     struct Join {
@@ -674,73 +735,71 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
     f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
     f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
     f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+    const auto cancelled = [&] { return opt && opt->should_cancel && opt->should_cancel(opt->user); };
     int done = 0, k = 0;
     bool first_batch = true;
-    for (const auto& rg : ranges) {
-        for (int b0 = rg.first; b0 < rg.second; b0 += per, k++) {
-            if (opt && opt->should_cancel && opt->should_cancel(opt->user)) fail(STG_CANCELLED, "cancelled");
-            const int nb = std::min(per, rg.second - b0);
-            // the batch's masks: transposed on the side stream, or streamed in by the caller
-            if (side_t) cuda_check(cudaStreamWaitEvent(st, (*D.side_ev)[k], 0), "cudaStreamWaitEvent");
-            else if (ready) cuda_check(cudaStreamWaitEvent(st, (*ready)[k], 0), "cudaStreamWaitEvent");
-            f.chunks = D.chunks + b0;
-            f.n_chunks = nb;
-            f.mask = d_mask + (int64_t)b0 * P.mask_per_chunk;
-            f.mask_chunk_stride = P.mask_per_chunk;
-            f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
-            f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
-            if (side_t) {   // transposed on the side stream
-                f.mask = reinterpret_cast<const float*>(D.mask_t + (int64_t)b0 * P.mask_t_per_chunk());
-                f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
-            } else if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
-                if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
-                cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins,
-                                                 P.g.T, D.mask_t, P.mask_t_per_chunk(), st),
-                           "mask transposition launch");
+    for (int m = 0; m < M; m++) {
+        const float* mask_m = d_mask + (int64_t)m * mask_per_model;
+        int kb = 0;   // batch of this model (the side stream's events are the first model's)
+        for (const auto& rg : ranges) {
+            for (int b0 = rg.first; b0 < rg.second; b0 += per, k++, kb++) {
+                if (cancelled()) fail(STG_CANCELLED, "cancelled");
+                const int nb = std::min(per, rg.second - b0);
+                // the batch's masks: transposed on the side stream, or streamed in by the caller
+                if (side_t) cuda_check(cudaStreamWaitEvent(st, (*D.side_ev)[kb], 0), "cudaStreamWaitEvent");
+                else if (ready) cuda_check(cudaStreamWaitEvent(st, (*ready)[k], 0), "cudaStreamWaitEvent");
+                f.chunks = D.chunks + b0;
+                f.n_chunks = nb;
+                f.mask = mask_m + (int64_t)b0 * P.mask_per_chunk;
+                f.mask_chunk_stride = P.mask_per_chunk;
+                f.Y = D.Y + (int64_t)b0 * P.y_chunk_stride;
+                f.Tr = D.Tr + (int64_t)b0 * P.tr_chunk_stride;
+                if (side_t) {   // transposed on the side stream
+                    f.mask = reinterpret_cast<const float*>(D.mask_t + (int64_t)b0 * P.mask_t_per_chunk());
+                    f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
+                } else if (P.mask_planes) {   // the batch's masks t-major, into the scratch the kernel reads
+                    if (!D.mask_t) fail(STG_INTERNAL_ERROR, "no scratch for the mask transposition");
+                    cuda_check(launch_mask_transpose(f.mask, P.mask_per_chunk, nb, P.S, P.mask_planes, P.mask_bins,
+                                                     P.g.T, D.mask_t, P.mask_t_per_chunk(), st),
+                               "mask transposition launch");
+                    if (timing) timing->launches++;
+                    f.mask = reinterpret_cast<const float*>(D.mask_t);
+                    f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
+                }
+                if (timed && first_batch) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
+                first_batch = false;
+                if (zpath) {   // every stem's ox = Z * M (CaC-normalised), iSTFT and overlap-add
+                    SplitParams b = split_params(P, D, d_mix, b0, nb);
+                    b.layout = BACK_ZMASK;
+                    b.n_bins = P.back_bins;
+                    b.net = const_cast<float*>(f.mask);
+                    b.net_chunk_stride = f.mask_chunk_stride;
+                    b.zspec = D.zspec + (int64_t)b0 * P.z_per_chunk();
+                    b.z_chunk_stride = P.z_per_chunk();
+                    b.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
+                    cuda_check(stg::launch_back(b, st), "back kernel launch");
+                } else {
+                    cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
+                }
                 if (timing) timing->launches++;
-                f.mask = reinterpret_cast<const float*>(D.mask_t);
-                f.mask_chunk_stride = 4 * P.mask_t_per_chunk();
-            }
-            if (timed && first_batch) cuda_check(cudaEventRecord(timing->ev[1], st), "cudaEventRecord");
-            first_batch = false;
-            if (zpath) {   // every stem's ox = Z * M (CaC-normalised), iSTFT and overlap-add
-                SplitParams b = split_params(P, D, d_mix, b0, nb);
-                b.layout = BACK_ZMASK;
-                b.n_bins = P.back_bins;
-                b.net = const_cast<float*>(f.mask);
-                b.net_chunk_stride = f.mask_chunk_stride;
-                b.zspec = D.zspec + (int64_t)b0 * P.z_per_chunk();
-                b.z_chunk_stride = P.z_per_chunk();
-                b.cac_stats = P.cac_norm ? D.cac_stats + b0 : nullptr;
-                cuda_check(stg::launch_back(b, st), "back kernel launch");
-            } else {
-                cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
-            }
-            if (timing) timing->launches++;
-            done += nb;
-            if (opt && opt->on_progress) {
-                cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
-                opt->on_progress(opt->user, done, total);
+                done += nb;
+                if (opt && opt->on_progress) {
+                    cuda_check(cudaStreamSynchronize(st), "fused spectral kernel");
+                    const bool final_batch = m == M - 1 && b0 + nb >= rg.second && &rg == &ranges.back();
+                    opt->on_progress(opt->user, final_batch && P.progress_final_total ? P.progress_total : done,
+                                     P.progress_total > 0 ? P.progress_total : total * M);
+                }
             }
         }
+        if (m == M - 1) {
+            join.now();
+            if (P.cancel_after_last && cancelled()) fail(STG_CANCELLED, "cancelled");
+            if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
+        }
+        cuda_check(launch_combine(combine_params(P, D, d_mix, d_out, sample_begin, sample_end, m), st),
+                   "combine kernel launch");
+        if (timing) timing->launches++;
     }
-    join.now();
-    CombineParams c{};
-    c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
-    c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
-    c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
-    c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
-    c.step_out = P.step_out; c.max_out_len = P.max_out_len;
-    c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
-    c.W = D.W;
-    c.S = P.S; c.C = P.C; c.len = P.len;
-    c.i_begin = sample_begin; c.i_end = sample_end;
-    c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
-    c.complement = P.complement; c.mix = d_mix; c.out = d_out;
-    c.mono_stats = P.mono_norm ? D.mono : nullptr;
-    if (timed) cuda_check(cudaEventRecord(timing->ev[2], st), "cudaEventRecord");
-    cuda_check(launch_combine(c, st), "combine kernel launch");
-    if (timing) timing->launches++;
     if (timed) cuda_check(cudaEventRecord(timing->ev[3], st), "cudaEventRecord");
 }
 
@@ -832,22 +891,12 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     cuda_check(stg::launch_back(s, st), "back kernel launch");
 }
 
-void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st) {
+void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st,
+                   int model) {
     if (!d_out || (P.complement && !d_mix)) fail(STG_INVALID_ARGUMENT, "null buffer");
-    CombineParams c{};
-    c.Y = D.Y; c.y_chunk_stride = P.y_chunk_stride;
-    c.Tr = D.Tr; c.tr_chunk_stride = P.tr_chunk_stride;
-    c.chunks = D.chunks; c.n_chunks = (int)P.chunks.size();
-    c.groups = D.groups; c.n_groups = (int)P.groups.size(); c.shift_mean = P.shift_mean;
-    c.step_out = P.step_out; c.max_out_len = P.max_out_len;
-    c.g = P.g; c.K = P.K; c.n_tiles = P.n_tiles;
-    c.W = D.W;
-    c.S = P.S; c.C = P.C; c.len = P.arch_out_len();
-    c.i_begin = 0; c.i_end = c.len;
-    c.mode = P.arch; c.nan_to_zero = P.nan_to_zero; c.compensate = P.compensate;
-    c.complement = P.complement; c.mix = d_mix; c.out = d_out;
-    c.mono_stats = P.mono_norm ? D.mono : nullptr;
-    cuda_check(launch_combine(c, st), "combine kernel launch");
+    if (model < 0 || model >= P.n_models) fail(STG_INVALID_ARGUMENT, "no such model in the bag");
+    cuda_check(launch_combine(combine_params(P, D, d_mix, d_out, 0, P.arch_out_len(), model), st),
+               "combine kernel launch");
 }
 
 } // namespace stg

@@ -44,6 +44,16 @@ struct HostPlan {
     float compensate = 1.0f;
     int zero_dc = 0, dim_f = 0, zero_bins = 0, bin_multi = 0;
     int mono_norm = 0, cac_norm = 0;   // HTDemucs: mono-mix and CaC normalisation
+    // HTDemucs bag of models (src/htdemucs.cpp:585-642): every model runs the chunk list on its
+    // own masks (model m's after model m - 1's); bag [n_models][S] weights and bag_tot [S] their
+    // sums. Empty bag: one model of weight 1 (no accumulation pass).
+    int n_models = 1;
+    std::vector<float> bag, bag_tot;
+    // progress as the reference separator counts it (stg_separate_ex): the total it reports,
+    // whether its last report is (total, total) (RoFormer) and whether it polls should_cancel
+    // once more after the last chunk (TFC-TDF)
+    int progress_total = 0;
+    bool progress_final_total = false, cancel_after_last = false;
     // f-major masks (HTDemucs, TFC-TDF): planes and bins per stem; the fused kernel reads
     // them after launch_mask_transpose, 0 planes for the other layouts
     int mask_planes = 0, mask_bins = 0;
@@ -73,6 +83,9 @@ struct HostPlan {
             fail(STG_INVALID_ARGUMENT, "mask must be " + std::to_string(mask_align()) + "-byte aligned");
     }
     int64_t n_chunks() const { return (int64_t)chunks.size(); }
+    // chunks whose masks the caller passes: every model's (the mask buffer's chunks)
+    int64_t n_mask_chunks() const { return (int64_t)n_models * (int64_t)chunks.size(); }
+    int64_t mask_floats() const { return mask_per_chunk * n_mask_chunks(); }
     int64_t out_floats() const { return (int64_t)S_out * C * len; }
     size_t y_bytes() const { return sizeof(float) * (size_t)y_chunk_stride * chunks.size(); }
     size_t tr_bytes() const { return sizeof(float) * (size_t)tr_chunk_stride * chunks.size(); }
@@ -110,6 +123,8 @@ struct PlanDevice {
     double2* cac_stats = nullptr;  // scratch: per-chunk CaC (mean, std)
     float4* mask_t = nullptr;      // scratch: t-major masks (HostPlan::mask_planes)
     float4* zspec = nullptr;       // scratch: HTDemucs spectra (HostPlan::z_per_chunk)
+    const float* bag = nullptr;    // HostPlan::bag and bag_tot (null without a bag)
+    const float* bag_tot = nullptr;
     // HTDemucs: a second stream on which every segment's mask transposition runs beside the
     // normalisation and the front kernel, joined before the first back kernel (null: the
     // transpositions run in order on the caller's stream)
@@ -163,6 +178,9 @@ void launch_front(const HostPlan& P, const PlanDevice& D, const float* d_mix, in
                   float* d_net_in, cudaStream_t st);
 void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, const float* d_net_out, int first,
                  int n, cudaStream_t st);
-void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st);
+// model: the bag member whose chunk outputs the scratch holds (its weights accumulate into d_out,
+// the last one divides and maps back); ignored without a bag.
+void launch_finish(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, cudaStream_t st,
+                   int model = 0);
 
 } // namespace stg

@@ -80,6 +80,25 @@ def test_htdemucs_config(pkg, tmp_path):
     assert c.overlap < 0
 
 
+def test_htdemucs_bag_config(pkg, tmp_path):
+    """htdemucs_ft-style file: stems.n_models 4 and one-hot stems.bag_weights (src/htdemucs.cpp:493-499)."""
+    p = tmp_path / "ft.gguf"
+    kv = _common("htdemucs", ["drums", "bass", "other", "vocals"])
+    w = np.eye(4, dtype=np.float32)
+    kv.update({"stems.segment_num": (G.U32, 39), "stems.segment_den": (G.U32, 5), "stems.n_models": (G.U32, 4),
+               "stems.bag_weights": (G.ARRAY, G.F32, [float(x) for x in w.reshape(-1)])})
+    G.write(p, kv)
+    c = pkg.Model(str(p)).config()
+    assert c.n_models == 4
+    assert [c.bag_weights[i] for i in range(16)] == list(w.reshape(-1))
+    # a bag whose weights do not match n_models x sources is a model error
+    kv["stems.bag_weights"] = (G.ARRAY, G.F32, [1.0] * 15)
+    q = tmp_path / "bad.gguf"
+    G.write(q, kv)
+    with pytest.raises(pkg.StemsError):
+        pkg.Model(str(q)).config()
+
+
 def test_roformer_config(pkg, tmp_path):
     p = tmp_path / "r.gguf"
     sizes, freqs = roformer_file(p, pkg)

@@ -317,3 +317,49 @@ def test_band_tables(pkg):
     bs, bf = pkg.bands.bs_bands()
     assert bs.size == 62 and bs.sum() == 1025 and list(bs[-2:]) == [128, 129]
     assert np.array_equal(bf, np.arange(1025))
+
+
+# ---- HTDemucs bag of models (src/htdemucs.cpp:585-642) ------------------------------------------
+def _bag_inputs(oracle_mod, n_models, seg=1024 * 12, length=30000, S=4):
+    p1 = oracle_mod.ht_params(n_sources=S, segment=seg, threads=4)
+    per_model = oracle_mod.ht_n_segments(p1, length) * S * 4 * 2048 * oracle_mod.ht_n_frames(p1)
+    rng = np.random.default_rng(41)
+    mix = (0.2 * rng.standard_normal((2, length))).astype(np.float32)
+    mask = rng.standard_normal(n_models * per_model).astype(np.float32)
+    return mix, mask, per_model
+
+
+@pytest.mark.parametrize("mono", [0, 1])
+def test_bag_one_hot_picks_each_models_stem(oracle_mod, mono):
+    """htdemucs_ft's bag: four models, one-hot weights. Stem s is model s's stem s alone: the sum
+    over the bag adds it to zero once and divides by 1, so it equals a one-model run bit for bit."""
+    S, seg, length = 4, 1024 * 12, 30000
+    mix, mask, per = _bag_inputs(oracle_mod, 4)
+    p = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=mono, cac_norm=1, threads=4,
+                             bag_weights=np.eye(4))
+    got = oracle_mod.ht_separate(p, mix, mask)
+    for s in range(S):
+        one = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=mono, cac_norm=1, threads=4)
+        want = oracle_mod.ht_separate(one, mix, mask[s * per:(s + 1) * per])
+        np.testing.assert_array_equal(got[s], want[s])
+
+
+def test_bag_weights_follow_the_reference_arithmetic(oracle_mod):
+    """Arbitrary weights: float32 products summed in model order, divided by the float32 sum of
+    the weights (then the mono inverse, off here), against the models' own one-model runs."""
+    S, seg, length = 4, 1024 * 12, 30000
+    w = np.array([[0.5, 1.0, 0.0, 2.0], [1.5, 0.25, 1.0, 0.0], [0.0, 3.0, 1.0, 1.0]], np.float32)
+    mix, mask, per = _bag_inputs(oracle_mod, 3)
+    p = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=0, cac_norm=1, threads=4, bag_weights=w)
+    got = oracle_mod.ht_separate(p, mix, mask)
+    est = np.zeros((S, 2, length), np.float32)
+    tot = np.zeros(S, np.float32)
+    for m in range(3):
+        one = oracle_mod.ht_params(n_sources=S, segment=seg, mono_norm=0, cac_norm=1, threads=4)
+        res = oracle_mod.ht_separate(one, mix, mask[m * per:(m + 1) * per])
+        for s in range(S):
+            tot[s] = np.float32(tot[s] + w[m, s])
+            if w[m, s] != 0:
+                est[s] = (est[s] + (w[m, s] * res[s]).astype(np.float32)).astype(np.float32)
+    want = (est / tot[:, None, None]).astype(np.float32)
+    np.testing.assert_array_equal(got, want)

@@ -56,6 +56,90 @@ def test_noalloc_matches_the_ordinary_entry_point(pkg, engine, chunk, num_overla
         assert err <= TOL, f"call {call}: max rel err {err:.3e}"
 
 
+def _noalloc(pkg, cfg, length, mix_ptr, mask_ptr, out_ptr, stream):
+    msg = C.create_string_buffer(512)
+    rc = pkg.lib().stg_separate_roformer_noalloc(0, C.byref(cfg), length, mix_ptr, mask_ptr, out_ptr, stream, msg,
+                                                  C.sizeof(msg))
+    assert rc == 0, msg.value.decode()
+
+
+def _plan_result(pkg, engine, sizes, freqs, chunk, num_overlap, length, mix, mask):
+    import torch
+    plan = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=num_overlap)
+    want = torch.empty(plan.out_shape, device="cuda", dtype=torch.float32)
+    plan.separate(torch.from_numpy(mix).cuda(), torch.from_numpy(mask).cuda(), want)
+    torch.cuda.synchronize()
+    return plan, want.cpu().numpy()
+
+
+def test_noalloc_small_after_large_reads_nothing_stale(pkg, engine):
+    """A 10 s call fills the array's scratch; a 3 s call after it, with a different chunk size,
+    must not read any of it: its output equals the plan path's."""
+    import torch
+    sizes, freqs = pkg.bands.mel_bands()
+    stream = torch.cuda.current_stream().cuda_stream
+    runs = [(352800, 4, 10.0), (441 * 40, 2, 3.0), (441 * 40, 2, 3.0)]
+    for chunk, nov, seconds in runs:
+        length = int(seconds * 44100) + 77
+        mix = synth_audio(57, length)
+        n_mask = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=nov).mask_floats
+        mask = synth_mask(58, n_mask, 0.5)
+        plan, want = _plan_result(pkg, engine, sizes, freqs, chunk, nov, length, mix, mask)
+        d_mix, d_mask = torch.from_numpy(mix).cuda(), torch.from_numpy(mask).cuda()
+        out = torch.full(plan.out_shape, float("nan"), device="cuda", dtype=torch.float32)
+        _noalloc(pkg, _config(pkg, sizes, freqs, chunk, nov), length, d_mix.data_ptr(), d_mask.data_ptr(),
+                 out.data_ptr(), stream)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert max_rel_err(got, want) <= TOL, f"{seconds} s after the previous call"
+
+
+def test_noalloc_in_the_callers_own_context(pkg, engine):
+    """A host that made its own (non-primary) context current: the call runs in it, with
+    buffers and a stream of that context, and leaves it current."""
+    cu = pytest.importorskip("cuda.bindings.driver")
+    sizes, freqs = pkg.bands.mel_bands()
+    chunk, nov = 441 * 40, 4
+    length = int(2.0 * 44100) + 5
+    mix = synth_audio(59, length)
+    plan0 = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=nov)
+    mask = synth_mask(60, plan0.mask_floats, 0.5)
+    _, want = _plan_result(pkg, engine, sizes, freqs, chunk, nov, length, mix, mask)
+
+    def ok(r):
+        err = r[0] if isinstance(r, tuple) else r
+        assert int(err) == 0, f"driver call failed: {err}"
+        return r[1] if isinstance(r, tuple) and len(r) == 2 else r
+
+    ok(cu.cuInit(0))
+    dev = ok(cu.cuDeviceGet(0))
+    ctx = ok(cu.cuCtxCreate(0, dev))
+    bufs = []
+    try:
+        def upload(a):
+            p = ok(cu.cuMemAlloc(a.nbytes))
+            bufs.append(p)
+            ok(cu.cuMemcpyHtoD(p, a.ctypes.data, a.nbytes))
+            return p
+        d_mix, d_mask = upload(mix), upload(mask)
+        out_h = np.full(want.shape, np.nan, np.float32)
+        d_out = upload(out_h)
+        stream = ok(cu.cuStreamCreate(0))
+        for _ in range(2):
+            _noalloc(pkg, _config(pkg, sizes, freqs, chunk, nov), length, int(d_mix), int(d_mask), int(d_out),
+                     int(stream))
+            ok(cu.cuStreamSynchronize(stream))
+            assert int(ok(cu.cuCtxGetCurrent())) == int(ctx)
+            ok(cu.cuMemcpyDtoH(out_h.ctypes.data, d_out, out_h.nbytes))
+            assert max_rel_err(out_h, want) <= TOL
+        ok(cu.cuStreamDestroy(stream))
+    finally:
+        for p in bufs:
+            cu.cuMemFree(p)
+        cu.cuCtxDestroy(ctx)
+
+
 def test_noalloc_rejects_what_does_not_fit(pkg, engine):
     import torch
     sizes, freqs = pkg.bands.mel_bands()
