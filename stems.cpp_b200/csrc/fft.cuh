@@ -217,16 +217,24 @@ struct TwGlobal {
 // st(base, r, v); r is a compile-time constant after unrolling, so callers fold it into
 // immediate offsets. MID_SYNC puts a barrier between the loads and the stores, which an
 // in-place pass needs; a pass that reads one buffer and writes another does not.
-template <int N, int R, int NS, int T, bool INV, bool MID_SYNC, class Tw, class Ld, class St>
+// TW_EARLY: load the pass's twiddles with the points, ahead of the barrier (a kernel that has
+// the registers for them).
+template <int N, int R, int NS, int T, bool INV, bool MID_SYNC, bool TW_EARLY = false, class Tw, class Ld, class St>
 __device__ __forceinline__ void pass_io(const Tw& tw, int tid, Ld&& ld, St&& st) {
     constexpr int NB = N / R;
     constexpr int ROUNDS = (NB + T - 1) / T;
     constexpr bool EXACT = (NB % T) == 0;
     float2 v[ROUNDS][R];
+    constexpr bool HOIST = TW_EARLY && NS > 1 && ROUNDS * (R - 1) <= 16;
+    float2 wv[HOIST ? ROUNDS : 1][HOIST ? R : 1];
 #pragma unroll
     for (int rd = 0; rd < ROUNDS; rd++) {
         const int j = tid + rd * T;
         if (EXACT || j < NB) {
+            if constexpr (HOIST) {
+#pragma unroll
+                for (int r = 1; r < R; r++) wv[rd][r] = tw(twiddle_index<NS>(r, j % NS));
+            }
 #pragma unroll
             for (int r = 0; r < R; r++) v[rd][r] = ld(j, r);
         }
@@ -240,7 +248,9 @@ __device__ __forceinline__ void pass_io(const Tw& tw, int tid, Ld&& ld, St&& st)
             if constexpr (NS > 1) {
 #pragma unroll
                 for (int r = 1; r < R; r++) {
-                    float2 w = tw(twiddle_index<NS>(r, k));
+                    float2 w;
+                    if constexpr (HOIST) w = wv[rd][r];
+                    else w = tw(twiddle_index<NS>(r, k));
                     if (INV) w.y = -w.y;
                     v[rd][r] = cmul(v[rd][r], w);
                 }
@@ -263,13 +273,16 @@ template <int N, int R> __device__ __forceinline__ int pad_load(int j, int r) {
 template <int R, int NS> __device__ __forceinline__ int pad_store(int base, int r) {
     if constexpr (NS % 16 == 0) return pad_idx(base) + r * (NS + NS / 16);
     else if constexpr (NS == 1 && 16 % R == 0) return pad_idx(base) + r;   // base = j*R
+    // NS divides 16 and NS*R is a multiple of 16: base mod 16 = k < NS and (r*NS) mod 16 is a
+    // multiple of NS below 16, so the pair never crosses a 16-boundary beyond r*NS's own
+    else if constexpr (16 % NS == 0 && (NS * R) % 16 == 0) return pad_idx(base) + r * NS + (r * NS) / 16;
     else return pad_idx(base + r * NS);
 }
 
 // In-place pass on the padded shared-memory frame buf, ending with a barrier.
-template <int N, int R, int NS, int T, bool INV, class Tw>
+template <int N, int R, int NS, int T, bool INV, bool TW_EARLY = false, class Tw>
 __device__ __forceinline__ void stockham_pass(float2* buf, const Tw& tw, int tid) {
-    pass_io<N, R, NS, T, INV, true>(
+    pass_io<N, R, NS, T, INV, true, TW_EARLY>(
         tw, tid, [&](int j, int r) { return buf[pad_load<N, R>(j, r)]; },
         [&](int base, int r, float2 v) { buf[pad_store<R, NS>(base, r)] = v; });
     __syncthreads();
@@ -296,13 +309,26 @@ template <int R, int... Rest> struct Head<RadixList<R, Rest...>> {
     using tail = RadixList<Rest...>;
 };
 
+// In-place passes for the radices of a list, the first of them at stride NS; hook() runs
+// before the last of them.
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw, class Hook, int R, int... Rest>
+__device__ __forceinline__ void passes_hook(float2* buf, const Tw& tw, int tid, Hook&& hook, RadixList<R, Rest...>) {
+    if constexpr (sizeof...(Rest) == 0) {
+        hook();
+        stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
+    } else {
+        stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
+        passes_hook<N, T, INV, NS * R, TW_EARLY>(buf, tw, tid, hook, RadixList<Rest...>{});
+    }
+}
+
 // In-place passes for the radices of a list, the first of them at stride NS.
-template <int N, int T, bool INV, int NS, class Tw>
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw>
 __device__ __forceinline__ void passes(float2*, const Tw&, int, RadixList<>) {}
-template <int N, int T, bool INV, int NS, class Tw, int R, int... Rest>
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw, int R, int... Rest>
 __device__ __forceinline__ void passes(float2* buf, const Tw& tw, int tid, RadixList<R, Rest...>) {
-    stockham_pass<N, R, NS, T, INV>(buf, tw, tid);
-    passes<N, T, INV, NS * R>(buf, tw, tid, RadixList<Rest...>{});
+    stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
+    passes<N, T, INV, NS * R, TW_EARLY>(buf, tw, tid, RadixList<Rest...>{});
 }
 
 // Transform the frame in buf (padded layout) in place: X[k] = sum_n x[n] W_N^{nk}, W = e^{-2 pi i/N}

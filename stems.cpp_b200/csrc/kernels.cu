@@ -131,6 +131,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     using InvInit = typename Init<Plan>::type;            // inverse passes but the last
     constexpr int RL = Init<Plan>::last, NSL = Init<Plan>::prod;
     constexpr bool SWIN = FftCfg<N>::SMEM_WIN;
+    // the RoFormer instance at n_fft 2048 has the registers to load each pass's twiddles early
+    constexpr bool TW_EARLY = ARCH == ARCH_ROFORMER && N == 2048;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
     float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
@@ -180,7 +182,15 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
         // prologue of a stem pass: the first frame's window and the next frame's new samples
         {
             const int q0 = G.first_pos + t_begin * hop;
-            for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + n);
+            if constexpr (N == 2048) {   // every load in flight before the first store
+                float2 pv[N / T];
+#pragma unroll
+                for (int k = 0; k < N / T; k++) pv[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + tid + k * T);
+#pragma unroll
+                for (int k = 0; k < N / T; k++) in_ring[ring_slot<N>(q0 + tid + k * T)] = pv[k];
+            } else {
+                for (int n = tid; n < N; n += T) in_ring[ring_slot<N>(q0 + n)] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + n);
+            }
 #pragma unroll
             for (int k = 0; k < nx.K; k++) {
                 const int u = tid + k * T;
@@ -226,17 +236,38 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     }
                 }
             }
-            passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
-            // all of this frame's mask loads in flight at once, then the spectral op: split the
+            // all of this frame's mask loads in flight at once (at n_fft 2048 before the last
+            // forward pass, whose work hides their latency), then the spectral op: split the
             // channels, apply the stand-in network, repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
-            mk.prefetch(p, ci, s, t, tid);
+            if constexpr (N == 2048) {
+                passes_hook<N, T, false, R1, TW_EARLY>(buf, tw, tid, [&] { mk.prefetch(p, ci, s, t, tid); }, FwdRest{});
+            } else {
+                passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
+                mk.prefetch(p, ci, s, t, tid);
+            }
+            // at n_fft 2048 and 7680 every bin's two spectrum points are loaded before the
+            // arithmetic and the stores (the stores could alias later loads as far as the compiler
+            // knows); at 4096 the 128-register cap leaves no room for it
+            constexpr bool BATCH = N == 2048;
+            float2 Xa[BATCH ? BPT : 1], Xb[BATCH ? BPT : 1];
+            if constexpr (BATCH) {
+#pragma unroll
+                for (int i = 0; i < BPT; i++) {
+                    const int f = tid + i * T;
+                    if (f <= N / 2) {
+                        Xa[i] = buf[pad_idx(f)];
+                        Xb[i] = buf[pad_idx(f == 0 ? 0 : N - f)];
+                    }
+                }
+            }
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
                 const int f = tid + i * T;
                 if (f <= N / 2) {
                     const int fm = f == 0 ? 0 : N - f;
-                    const float2 X = buf[pad_idx(f)], Xm = buf[pad_idx(fm)];
+                    const float2 X = BATCH ? Xa[BATCH ? i : 0] : buf[pad_idx(f)];
+                    const float2 Xm = BATCH ? Xb[BATCH ? i : 0] : buf[pad_idx(fm)];
                     const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
                     const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
                     float2 yl, yr;
@@ -247,7 +278,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 }
             }
             __syncthreads();
-            passes<N, T, true, 1>(buf, tw, tid, InvInit{});
+            passes<N, T, true, 1, TW_EARLY>(buf, tw, tid, InvInit{});
             // inverse last pass: window and overlap-add straight into the output ring
             pass_io<N, RL, NSL, T, true, false>(
                 tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
@@ -269,27 +300,61 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 r = (q0 - G.out_offset + tid - p.env_lo) % hop;
                 if (r < 0) r += hop;
             }
-            for (int u = tid; u < nflush; u += T) {
-                const int q = q0 + u;
-                float2& o = out_ring[ring_slot<N>(q)];
-                const float2 v = o;
-                o = make_float2(0.f, 0.f);
-                const int j = q - G.out_offset;
-                const bool in = j >= 0 && j < G.Lout;
-                float ie = 0.0f;
-                if (in) ie = env_on && j >= p.env_lo && j < p.env_hi ? env_s[r] : ld_stream(p.inv_env + j);
-                if (env_on) {
+            if (BATCH && !last && env_on) {
+                // a frame inside the tile: hop samples to Y, every ring and envelope load of the
+                // thread issued before its first store
+                constexpr int KF = (FftCfg<N>::HOPMAX + T - 1) / T;
+                float2 fv[KF];
+                float fe[KF];
+#pragma unroll
+                for (int k = 0; k < KF; k++) {
+                    const int u = tid + k * T;
+                    fe[k] = 0.0f;
+                    if (u < hop) {
+                        const int q = q0 + u;
+                        fv[k] = out_ring[ring_slot<N>(q)];
+                        const int j = q - G.out_offset;
+                        if (j >= 0 && j < G.Lout) fe[k] = j >= p.env_lo && j < p.env_hi ? env_s[r] : ld_stream(p.inv_env + j);
+                    }
                     r += T;
                     while (r >= hop) r -= hop;
                 }
-                if (u < ny) {
-                    if (in) {
-                        if (C > 1) reinterpret_cast<float2*>(Ys)[j] = make_float2(v.x * ie, v.y * ie);
-                        else Ys[j] = v.x * ie;
+#pragma unroll
+                for (int k = 0; k < KF; k++) {
+                    const int u = tid + k * T;
+                    if (u < hop) {
+                        const int q = q0 + u;
+                        out_ring[ring_slot<N>(q)] = make_float2(0.f, 0.f);
+                        const int j = q - G.out_offset;
+                        if (j >= 0 && j < G.Lout) {
+                            if (C > 1) reinterpret_cast<float2*>(Ys)[j] = make_float2(fv[k].x * fe[k], fv[k].y * fe[k]);
+                            else Ys[j] = fv[k].x * fe[k];
+                        }
                     }
-                } else {
-                    if (C > 1) reinterpret_cast<float2*>(Trs)[u - hop] = make_float2(v.x * ie, v.y * ie);
-                    else Trs[u - hop] = v.x * ie;
+                }
+            } else {
+                for (int u = tid; u < nflush; u += T) {
+                    const int q = q0 + u;
+                    float2& o = out_ring[ring_slot<N>(q)];
+                    const float2 v = o;
+                    o = make_float2(0.f, 0.f);
+                    const int j = q - G.out_offset;
+                    const bool in = j >= 0 && j < G.Lout;
+                    float ie = 0.0f;
+                    if (in) ie = env_on && j >= p.env_lo && j < p.env_hi ? env_s[r] : ld_stream(p.inv_env + j);
+                    if (env_on) {
+                        r += T;
+                        while (r >= hop) r -= hop;
+                    }
+                    if (u < ny) {
+                        if (in) {
+                            if (C > 1) reinterpret_cast<float2*>(Ys)[j] = make_float2(v.x * ie, v.y * ie);
+                            else Ys[j] = v.x * ie;
+                        }
+                    } else {
+                        if (C > 1) reinterpret_cast<float2*>(Trs)[u - hop] = make_float2(v.x * ie, v.y * ie);
+                        else Trs[u - hop] = v.x * ie;
+                    }
                 }
             }
             // the next iteration's first barrier (after forward pass 1) orders these ring
@@ -308,20 +373,25 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
 // and divide by the summed weight; then average the groups and finish (epilogue).
 // The value the separator returns for row k (stem k / C) at output sample i, from this launch's
 // estimate v: the shift average's division, compensation, then either the mono-mix inverse
-// (src/htdemucs.cpp:641) or, for a bag of models, this model's weighted term added to the
-// previous models' sum in out (float products and sums in model order, :628-635) and, after
-// the last model, the division by the weights' sum and the mono inverse (:638-642).
-__device__ __forceinline__ float finish_value(const CombineParams& p, int k, int64_t i, float v) {
+// (src/htdemucs.cpp:641; finish_plain) or, for a bag of models (finish_bag), this model's
+// weighted term added to the previous models' sum in out (float products and sums in model
+// order, :628-635) and, after the last model, the division by the weights' sum and the mono
+// inverse (:638-642).
+__device__ __forceinline__ float finish_plain(const CombineParams& p, float v) {
+    v = p.shift_mean == 1 ? v / (float)p.n_groups : v;
+    v *= p.compensate;
+    if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);   // htdemucs.cpp:641
+    return v;
+}
+__device__ __forceinline__ float finish_bag(const CombineParams& p, int k, int64_t i, float v) {
     if (p.shift_mean == 1) v = v / (float)p.n_groups;
     v *= p.compensate;
-    if (p.bag) {
-        const int s = k / p.C;
-        const float w = __ldg(p.bag + p.bag_model * p.S + s);
-        float acc = p.bag_model == 0 ? 0.0f : p.out[(int64_t)k * p.len + i];
-        if (w != 0.0f) acc = __fadd_rn(acc, __fmul_rn(w, v));
-        if (!p.bag_last) return acc;
-        v = __fdiv_rn(acc, __ldg(p.bag_tot + s));
-    }
+    const int s = k / p.C;
+    const float w = __ldg(p.bag + p.bag_model * p.S + s);
+    float acc = p.bag_model == 0 ? 0.0f : p.out[(int64_t)k * p.len + i];
+    if (w != 0.0f) acc = __fadd_rn(acc, __fmul_rn(w, v));
+    if (!p.bag_last) return acc;
+    v = __fdiv_rn(acc, __ldg(p.bag_tot + s));
     if (p.mono_stats) v = (float)((double)v * p.mono_stats[1] + p.mono_stats[0]);
     return v;
 }
@@ -394,12 +464,15 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
         }
     }
     float outv[SC];
+    if (!p.bag) {
 #pragma unroll
-    for (int k = 0; k < SC; k++) {
-        const float v = finish_value(p, k, i, res[k]);
-        outv[k] = v;
-        p.out[(int64_t)k * p.len + i] = v;
+        for (int k = 0; k < SC; k++) outv[k] = finish_plain(p, res[k]);
+    } else {   // a bag member's pass reads the previous members' sums in out
+#pragma unroll
+        for (int k = 0; k < SC; k++) outv[k] = finish_bag(p, k, i, res[k]);
     }
+#pragma unroll
+    for (int k = 0; k < SC; k++) p.out[(int64_t)k * p.len + i] = outv[k];
     if (p.complement) {
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -510,10 +583,17 @@ __global__ void __launch_bounds__(256) combine_kernel4(const CombineParams p) {
         }
     }
     float outv[V][SC];
+    if (!p.bag) {
 #pragma unroll
-    for (int s = 0; s < V; s++)
+        for (int s = 0; s < V; s++)
 #pragma unroll
-        for (int k = 0; k < SC; k++) outv[s][k] = s < nv ? finish_value(p, k, i0 + s, res[s][k]) : 0.0f;
+            for (int k = 0; k < SC; k++) outv[s][k] = finish_plain(p, res[s][k]);
+    } else {   // a bag member's pass reads the previous members' sums in out
+#pragma unroll
+        for (int s = 0; s < V; s++)
+#pragma unroll
+            for (int k = 0; k < SC; k++) outv[s][k] = s < nv ? finish_bag(p, k, i0 + s, res[s][k]) : 0.0f;
+    }
     // rows of 4 samples as one 16-byte store where the row offset allows it
     const bool vec = nv == V && (p.len % V) == 0 && (i0 % V) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.out) % (sizeof(float) * V)) == 0;
