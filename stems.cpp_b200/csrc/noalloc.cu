@@ -8,11 +8,13 @@
 // device array of 64 MiB, reserved on every GPU that loads this library until the process
 // exits. The kernels are the same as stg_separate's.
 //
-// Contexts. The call runs in the context current on the calling thread when that context
-// belongs to `device` (a host application's own context included), and otherwise makes
-// `device`'s primary context current for the call and puts the caller's context back
-// afterwards. A __device__ array has one address per context, so the address is looked up
-// (cudaGetSymbolAddress) once per context, on that context's first call.
+// Contexts. The call runs in `device`'s primary context, the one the CUDA runtime and the
+// applications built on it use: when another device's primary context (or none) is current
+// on the calling thread, it makes `device`'s current for the call and puts the caller's back
+// afterwards. A context the caller created with the driver API (cuCtxCreate) is refused with
+// STG_UNSUPPORTED before any GPU work: the runtime resolves the array's address, and loads the
+// library's kernels, for primary contexts. The address is looked up (cudaGetSymbolAddress)
+// once per context, on its first call, and kept by the driver's unique context ID.
 #include "../../include/stems_gpu_v1.h"
 #include "kernels.h"
 #include "plan.h"
@@ -41,10 +43,17 @@ static __device__ __align__(256) unsigned char g_arena[kArenaBytes];
 using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 using CtxSetCurrentFn = CUresult (*)(CUcontext);
 using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+using CtxGetDeviceFn = CUresult (*)(CUdevice*);
+using PrimaryRetainFn = CUresult (*)(CUcontext*, CUdevice);
+using PrimaryReleaseFn = CUresult (*)(CUdevice);
 struct Driver {
     CtxGetCurrentFn get = nullptr;
     CtxSetCurrentFn set = nullptr;
     CtxGetIdFn id = nullptr;
+    CtxGetDeviceFn device = nullptr;
+    PrimaryRetainFn retain = nullptr;
+    PrimaryReleaseFn release = nullptr;
+    bool ok() const { return get && set && id && device && retain && release; }
 };
 template <class F> F entry_point(const char* name) {
     void* p = nullptr;
@@ -57,7 +66,9 @@ template <class F> F entry_point(const char* name) {
 }
 const Driver& driver() {
     static const Driver d{entry_point<CtxGetCurrentFn>("cuCtxGetCurrent"), entry_point<CtxSetCurrentFn>("cuCtxSetCurrent"),
-                          entry_point<CtxGetIdFn>("cuCtxGetId")};
+                          entry_point<CtxGetIdFn>("cuCtxGetId"), entry_point<CtxGetDeviceFn>("cuCtxGetDevice"),
+                          entry_point<PrimaryRetainFn>("cuDevicePrimaryCtxRetain"),
+                          entry_point<PrimaryReleaseFn>("cuDevicePrimaryCtxRelease")};
     return d;
 }
 
@@ -91,18 +102,30 @@ void write_message(char* msg, size_t cap, const char* text) {
     if (msg && cap) std::snprintf(msg, cap, "%s", text);
 }
 
-// Makes a context of `device` current for the call: the caller's own when it is on `device`,
-// else the device's primary context; the destructor puts the caller's context back.
+// Makes `device`'s primary context current for the call (refusing a caller-created context);
+// the destructor puts the caller's context back.
 struct ContextScope {
     bool switched = false;
     CUcontext previous = nullptr;
     explicit ContextScope(int device) {
         const Driver& d = driver();
-        if (!d.get || !d.set || !d.id) fail(STG_INTERNAL_ERROR, "the CUDA driver's context entry points are unavailable");
+        if (!d.ok()) fail(STG_INTERNAL_ERROR, "the CUDA driver's context entry points are unavailable");
         if (d.get(&previous) != CUDA_SUCCESS) fail(STG_INTERNAL_ERROR, "cuCtxGetCurrent failed");
-        int current = -1;
-        if (previous) cuda_check(cudaGetDevice(&current), "cudaGetDevice");
-        if (!previous || current != device) {
+        bool ours = false;   // previous is `device`'s primary context
+        if (previous) {
+            CUdevice dev = 0;
+            CUcontext primary = nullptr;
+            if (d.device(&dev) != CUDA_SUCCESS || d.retain(&primary, dev) != CUDA_SUCCESS)
+                fail(STG_INTERNAL_ERROR, "cannot query the current context");
+            d.release(dev);
+            if (primary != previous)
+                fail(STG_UNSUPPORTED, "the current CUDA context is not a primary context: this entry point runs in "
+                                      "the device's primary context (the CUDA runtime's)");
+            int current = -1;
+            cuda_check(cudaGetDevice(&current), "cudaGetDevice");
+            ours = current == device;
+        }
+        if (!ours) {
             cuda_check(cudaSetDevice(device), "cudaSetDevice");
             switched = true;
         }

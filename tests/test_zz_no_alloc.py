@@ -95,17 +95,14 @@ def test_noalloc_small_after_large_reads_nothing_stale(pkg, engine):
         assert max_rel_err(got, want) <= TOL, f"{seconds} s after the previous call"
 
 
-def test_noalloc_in_the_callers_own_context(pkg, engine):
-    """A host that made its own (non-primary) context current: the call runs in it, with
-    buffers and a stream of that context, and leaves it current."""
+def test_noalloc_refuses_a_driver_created_context(pkg, engine):
+    """A host that made its own (cuCtxCreate) context current: the call is refused with
+    STG_UNSUPPORTED before any GPU work, and the caller's context is still current after it.
+    The arena's address is resolved for the runtime's primary context only, so running there
+    could hand a kernel an address the caller's context does not map."""
     cu = pytest.importorskip("cuda.bindings.driver")
     sizes, freqs = pkg.bands.mel_bands()
-    chunk, nov = 441 * 40, 4
-    length = int(2.0 * 44100) + 5
-    mix = synth_audio(59, length)
-    plan0 = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=nov)
-    mask = synth_mask(60, plan0.mask_floats, 0.5)
-    _, want = _plan_result(pkg, engine, sizes, freqs, chunk, nov, length, mix, mask)
+    chunk, nov, length = 441 * 40, 4, 2 * 44100
 
     def ok(r):
         err = r[0] if isinstance(r, tuple) else r
@@ -115,29 +112,54 @@ def test_noalloc_in_the_callers_own_context(pkg, engine):
     ok(cu.cuInit(0))
     dev = ok(cu.cuDeviceGet(0))
     ctx = ok(cu.cuCtxCreate(0, dev))
-    bufs = []
     try:
-        def upload(a):
-            p = ok(cu.cuMemAlloc(a.nbytes))
-            bufs.append(p)
-            ok(cu.cuMemcpyHtoD(p, a.ctypes.data, a.nbytes))
-            return p
-        d_mix, d_mask = upload(mix), upload(mask)
-        out_h = np.full(want.shape, np.nan, np.float32)
-        d_out = upload(out_h)
-        stream = ok(cu.cuStreamCreate(0))
-        for _ in range(2):
-            _noalloc(pkg, _config(pkg, sizes, freqs, chunk, nov), length, int(d_mix), int(d_mask), int(d_out),
-                     int(stream))
-            ok(cu.cuStreamSynchronize(stream))
-            assert int(ok(cu.cuCtxGetCurrent())) == int(ctx)
-            ok(cu.cuMemcpyDtoH(out_h.ctypes.data, d_out, out_h.nbytes))
-            assert max_rel_err(out_h, want) <= TOL
-        ok(cu.cuStreamDestroy(stream))
+        msg = C.create_string_buffer(512)
+        cfg = _config(pkg, sizes, freqs, chunk, nov)
+        # the buffers are never touched: the call stops before any GPU work
+        rc = pkg.lib().stg_separate_roformer_noalloc(0, C.byref(cfg), length, 256, 256, 256, None, msg, C.sizeof(msg))
+        assert rc == 2, msg.value.decode()
+        assert "primary context" in msg.value.decode()
+        assert int(ok(cu.cuCtxGetCurrent())) == int(ctx)
     finally:
-        for p in bufs:
-            cu.cuMemFree(p)
         cu.cuCtxDestroy(ctx)
+
+
+def test_noalloc_from_a_thread_without_a_context(pkg, engine):
+    """A thread that never touched CUDA: the call makes the device's primary context current
+    for itself and leaves the thread as it found it (no context current)."""
+    import threading
+
+    import torch
+    cu = pytest.importorskip("cuda.bindings.driver")
+    sizes, freqs = pkg.bands.mel_bands()
+    chunk, nov = 441 * 40, 4
+    length = int(2.0 * 44100) + 5
+    mix = synth_audio(59, length)
+    plan0 = engine.plan_roformer(length, sizes, freqs, chunk=chunk, num_overlap=nov)
+    mask = synth_mask(60, plan0.mask_floats, 0.5)
+    _, want = _plan_result(pkg, engine, sizes, freqs, chunk, nov, length, mix, mask)
+    d_mix, d_mask = torch.from_numpy(mix).cuda(), torch.from_numpy(mask).cuda()
+    out = torch.full(want.shape, float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    result = {}
+
+    def worker():
+        before = cu.cuCtxGetCurrent()[1]
+        msg = C.create_string_buffer(512)
+        cfg = _config(pkg, sizes, freqs, chunk, nov)
+        result["rc"] = pkg.lib().stg_separate_roformer_noalloc(0, C.byref(cfg), length, d_mix.data_ptr(),
+                                                               d_mask.data_ptr(), out.data_ptr(), None, msg,
+                                                               C.sizeof(msg))
+        result["msg"] = msg.value.decode()
+        result["before"], result["after"] = int(before), int(cu.cuCtxGetCurrent()[1])
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert result["rc"] == 0, result["msg"]
+    assert result["before"] == 0 and result["after"] == 0
+    torch.cuda.synchronize()
+    assert max_rel_err(out.cpu().numpy(), want) <= TOL
 
 
 def test_noalloc_rejects_what_does_not_fit(pkg, engine):
