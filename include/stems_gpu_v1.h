@@ -260,6 +260,19 @@ STG_API stg_status stg_separate_host_ex(stg_plan* plan, const float* h_mix, cons
 STG_API stg_status stg_separate_part(stg_plan* plan, const float* d_mix, const float* d_mask,
                                      int64_t sample_begin, int64_t sample_end, float* d_out, void* stream);
 
+/* One track over several GPUs of this node, from host buffers, in one call: plans[d] (one per
+ * device, each from an engine of its own, all of the same model configuration and length)
+ * writes output samples [n * d / n_plans, n * (d + 1) / n_plans) of every output row, running
+ * only the chunks that reach them (stg_separate_part); the chunks at a range's edge run on
+ * both neighbours, so nothing is exchanged and every sample is the float one GPU writes. One
+ * host thread and one stream per device; each copies in the mix and the masks of its own
+ * chunks and copies its range of h_out back. Returns when h_out holds the whole result, or the
+ * first failure's status after every device has stopped. Pinned host buffers let the devices'
+ * copies run side by side. No reference counterpart: libstems separates a track on one device
+ * (src/libstems.cpp:188); this is the node-wide form of that call. */
+STG_API stg_status stg_separate_multi_host(stg_plan* const* plans, int32_t n_plans, const float* h_mix,
+                                           const float* h_mask, float* h_out);
+
 /* DualMono (src/separator.cpp:15-47): a plan of a one-channel model (n_channels 1) run on
  * each channel of a stereo mix on its own, the results interleaved into planar stereo.
  * d_mix [2][n_samples]; d_mask holds the left channel's masks (stg_plan_info's
@@ -448,11 +461,13 @@ STG_API stg_status stg_htdemucs_ispec(stg_engine* engine, const float* d_spec, i
  * num_overlap 4, 56 s at num_overlap 2. Longer inputs are rejected with
  * STG_INVALID_ARGUMENT and a message saying how much they need.
  *
- * Contexts: the call runs in the calling thread's current context when that context belongs
- * to `device` (a host application's own context included); otherwise it makes `device`'s
- * primary context current for the call and afterwards makes the caller's context (or none)
- * current again. The first call in each context looks up the array's device address in that
- * context (cudaGetSymbolAddress); make that first call before any stream capture begins.
+ * Contexts: the call runs in `device`'s primary context, the one the CUDA runtime (and an
+ * application built on it) uses. When the calling thread has no current context, or another
+ * device's primary context, it makes `device`'s current for the call and afterwards makes the
+ * caller's (or none) current again. A context the caller created with the driver API
+ * (cuCtxCreate) is refused with STG_UNSUPPORTED before any GPU work; the buffers and the stream
+ * must belong to the primary context. The first call in a context looks up the array's device
+ * address there (cudaGetSymbolAddress); make that first call before any stream capture begins.
  * Each call copies its tables (chunk schedule, weights, window, twiddles) from host memory the
  * library keeps into the array with one cudaMemcpyAsync on `stream`, which may wait for the
  * stream's earlier work; a call with the same configuration and length as the previous call

@@ -127,6 +127,7 @@ _SIGNATURES = {
     "stg_separate_host": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_host_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.POINTER(RunOptions)]),
+    "stg_separate_multi_host": (C.c_int32, [C.POINTER(C.c_void_p), C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "stg_separate_ex": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.POINTER(RunOptions)]),
     "stg_plan_network_info": (C.c_int32, [C.c_void_p, C.POINTER(NetworkInfo)]),
@@ -223,6 +224,25 @@ def _stream_of(stream, *tensors):
             import torch
             return torch.cuda.current_stream(t.device).cuda_stream
     return None
+
+
+def separate_multi_host(plans, mix, mask, out=None):
+    """One track over several devices (stg_separate_multi_host): plans[d], each of its own
+    engine and all of one configuration and length, writes the d-th range of output samples.
+    Host buffers (numpy float32); returns the [S][C][n] result."""
+    if not plans:
+        raise StemsError(1, "no plans")
+    p0 = plans[0]
+    mix = np.ascontiguousarray(mix, dtype=np.float32)
+    mask = np.ascontiguousarray(mask, dtype=np.float32)
+    if mix.size != p0.n_channels * p0.n_samples or mask.size != p0.mask_floats:
+        raise StemsError(1, "buffer sizes do not match the plans")
+    if out is None:
+        out = np.empty(p0.out_shape, np.float32)
+    handles = (C.c_void_p * len(plans))(*[p._h for p in plans])
+    rc = lib().stg_separate_multi_host(handles, len(plans), mix.ctypes.data, mask.ctypes.data, out.ctypes.data)
+    p0.engine._check(rc, "separate_multi_host")
+    return out
 
 
 class Engine:

@@ -3,6 +3,7 @@
 #include "engine.h"
 
 #include <cstring>
+#include <thread>
 
 #define STG_VERSION_STRING "stems-b200 spectral 0.1 (stems_gpu abi 1)"
 
@@ -245,6 +246,82 @@ STG_API stg_status stg_separate_host_ex(stg_plan* p, const float* h_mix, const f
                                         void* stream, const stg_run_options* opt) {
     if (!p) return STG_INVALID_ARGUMENT;
     return guard(p->engine, [&] { separate_host(p, h_mix, h_mask, h_out, static_cast<cudaStream_t>(stream), opt); });
+}
+
+// ---- one track over several devices -----------------------------------------------------------
+namespace {
+// Device d's share of a multi-device separation: output samples [b, e) of every row.
+void separate_range(stg_plan* p, const float* h_mix, const float* h_mask, float* h_out, int64_t b, int64_t e) {
+    cuda_check(cudaSetDevice(p->engine->device), "cudaSetDevice");
+    const HostPlan& H = p->H;
+    if (!p->multi_st) cuda_check(cudaStreamCreateWithFlags(&p->multi_st, cudaStreamNonBlocking), "cudaStreamCreate");
+    const cudaStream_t st = p->multi_st;
+    const size_t mix_b = sizeof(float) * (size_t)H.C * H.len;
+    const size_t chunk_b = sizeof(float) * (size_t)H.mask_per_chunk;
+    const size_t out_b = sizeof(float) * (size_t)H.out_floats();
+    p->s_mix.reserve(mix_b, "staging");
+    p->s_mask.reserve(sizeof(float) * (size_t)H.mask_floats(), "staging");
+    p->s_out.reserve(out_b, "staging");
+    try {
+        cuda_check(cudaMemcpyAsync(p->s_mix.p, h_mix, mix_b, cudaMemcpyHostToDevice, st), "copy mix in");
+        // the masks of the chunks that reach [b, e), every bag member's, at their own offsets
+        const int n = (int)H.chunks.size(), M = H.bag.empty() ? 1 : H.n_models;
+        for (const auto& rg : chunks_for(H, b, e))
+            for (int m = 0; m < M; m++) {
+                const size_t first = (size_t)m * n + rg.first, count = (size_t)(rg.second - rg.first);
+                cuda_check(cudaMemcpyAsync(static_cast<char*>(p->s_mask.p) + chunk_b * first,
+                                           reinterpret_cast<const char*>(h_mask) + chunk_b * first, chunk_b * count,
+                                           cudaMemcpyHostToDevice, st),
+                           "copy masks in");
+            }
+        p->run(p->s_mix.as<float>(), p->s_mask.as<float>(), p->s_out.as<float>(), st, nullptr, b, e);
+        // samples [b, e) of every output row
+        const size_t row = sizeof(float) * (size_t)H.len;
+        cuda_check(cudaMemcpy2DAsync(h_out + b, row, p->s_out.as<float>() + b, row, sizeof(float) * (size_t)(e - b),
+                                     (size_t)H.S_out * H.C, cudaMemcpyDeviceToHost, st),
+                   "copy the result out");
+        cuda_check(cudaStreamSynchronize(st), "separation");
+    } catch (...) {
+        cudaStreamSynchronize(st);
+        throw;
+    }
+}
+} // namespace
+
+STG_API stg_status stg_separate_multi_host(stg_plan* const* plans, int32_t n_plans, const float* h_mix,
+                                           const float* h_mask, float* h_out) {
+    if (!plans || n_plans < 1 || !plans[0]) return STG_INVALID_ARGUMENT;
+    return guard(plans[0]->engine, [&] {
+        if (!h_mix || !h_mask || !h_out) fail(STG_INVALID_ARGUMENT, "null buffer");
+        const HostPlan& H0 = plans[0]->H;
+        for (int d = 0; d < n_plans; d++) {
+            if (!plans[d]) fail(STG_INVALID_ARGUMENT, "null plan");
+            const HostPlan& H = plans[d]->H;
+            if (H.arch != H0.arch || H.len != H0.len || H.C != H0.C || H.S_out != H0.S_out ||
+                H.chunks.size() != H0.chunks.size() || H.mask_per_chunk != H0.mask_per_chunk ||
+                H.n_models != H0.n_models)
+                fail(STG_INVALID_ARGUMENT, "the plans differ: they must share the model configuration and length");
+            for (int k = 0; k < d; k++)
+                if (plans[k] == plans[d] || plans[k]->engine == plans[d]->engine)
+                    fail(STG_INVALID_ARGUMENT, "every plan needs an engine of its own");
+        }
+        const int64_t len = H0.len;
+        std::vector<std::string> errors(n_plans);
+        std::vector<stg_status> codes(n_plans, STG_OK);
+        std::vector<std::thread> workers;
+        workers.reserve(n_plans);
+        for (int d = 0; d < n_plans; d++) {
+            const int64_t b = len * d / n_plans, e = len * (d + 1) / n_plans;
+            if (b >= e) continue;
+            workers.emplace_back([&, d, b, e] {
+                codes[d] = guard(plans[d]->engine, [&] { separate_range(plans[d], h_mix, h_mask, h_out, b, e); });
+                if (codes[d] != STG_OK) errors[d] = plans[d]->engine->last_error;
+            });
+        }
+        for (std::thread& t : workers) t.join();
+        for (int d = 0; d < n_plans; d++)
+            if (codes[d] != STG_OK) fail(codes[d], "device part " + std::to_string(d) + ": " + errors[d]);
+    });
 }
 
 // ---- the halves around a real network ----------------------------------------------------

@@ -114,6 +114,7 @@ struct stg_plan {
     std::vector<cudaEvent_t> copy_ev;
     std::vector<cudaEvent_t> side_ev;   // HTDemucs: per batch, its masks transposed (PlanDevice::side_ev)
     DevBuf dm_out;                 // one channel's result (stg_separate_dual_mono)
+    cudaStream_t multi_st = nullptr;   // stg_separate_multi_host: this plan's device's stream
     DevBuf n_in, n_out;            // one batch of network input and output (stg_separate_network)
     RunTiming timing;
 
@@ -129,6 +130,7 @@ struct stg_plan {
             if (e) cudaEventDestroy(e);
         if (copy_fork) cudaEventDestroy(copy_fork);
         if (copy_st) cudaStreamDestroy(copy_st);
+        if (multi_st) cudaStreamDestroy(multi_st);
     }
 
     // Device copies of the tables, and the scratch the fused kernel writes.

@@ -122,14 +122,12 @@ void finish_plan(HostPlan& P, int env_frames) {
 
 } // namespace
 
-void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
-    const std::vector<double> w = hann_periodic(n);
-    win.assign(w.begin(), w.end());
-    // per-pass tables of the kernel's radix plan: the pass at stride NS (radix R) holds
-    // W_{NS*R}^{k*r} at (NS - 1) + (r - 1)*NS + k (fft.cuh: twiddle_index)
+void fft_twiddles(int n, const std::vector<int>& radices, std::vector<float2>& tw) {
+    // per-pass tables of a radix plan: the pass at stride NS (radix R) holds W_{NS*R}^{k*r} at
+    // (NS - 1) + (r - 1)*NS + k (fft.cuh: twiddle_index)
     tw.assign(n, make_float2(1.0f, 0.0f));
     int ns = 1;
-    for (int R : fused_radices(n)) {
+    for (int R : radices) {
         for (int r = 1; r < R; r++)
             for (int k = 0; k < ns; k++) {
                 const double th = -2.0 * M_PI * (double)k * r / ((double)ns * R);
@@ -138,6 +136,12 @@ void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
         ns *= R;
     }
     if (ns != n) fail(STG_INTERNAL_ERROR, "radix plan does not multiply to n_fft");
+}
+
+void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
+    const std::vector<double> w = hann_periodic(n);
+    win.assign(w.begin(), w.end());
+    fft_twiddles(n, fused_radices(n), tw);
 }
 
 // The offsets of the random-shift passes: std::mt19937 seeded with `seed`, one draw of
@@ -599,6 +603,23 @@ std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_
 }
 
 namespace {
+// The fused kernel's parameters apart from the chunk range and the mask.
+FusedParams fused_params(const HostPlan& P, const PlanDevice& D, const float* d_mix) {
+    FusedParams f{};
+    f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
+    f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
+    f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
+    f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
+    f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
+    f.bin_tab = D.btab;
+    f.bin_multi = P.bin_multi;
+    f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
+    f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
+    f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
+    f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+    return f;
+}
+
 // The combine of one run (or of one bag member's run) over output samples [b, e).
 CombineParams combine_params(const HostPlan& P, const PlanDevice& D, const float* d_mix, float* d_out, int64_t b,
                              int64_t e, int model) {
@@ -723,18 +744,7 @@ void launch_plan(const HostPlan& P, const PlanDevice& D, const float* d_mix_in, 
         join.st = st;
         join.ev = D.join;
     }
-    FusedParams f{};
-    f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
-    f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
-    f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
-    f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
-    f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
-    f.bin_tab = D.btab;
-    f.bin_multi = P.bin_multi;
-    f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
-    f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
-    f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
-    f.y_chunk_stride = P.y_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+    FusedParams f = fused_params(P, D, d_mix);
     const auto cancelled = [&] { return opt && opt->should_cancel && opt->should_cancel(opt->user); };
     int done = 0, k = 0;
     bool first_batch = true;
@@ -865,20 +875,11 @@ void launch_back(const HostPlan& P, const PlanDevice& D, const float* d_mix, con
     if (P.back_is_fused) {
         // RoFormer: the network's masks are exactly the fused kernel's mask input
         P.check_mask(d_net_out);
-        FusedParams f{};
-        f.mix = d_mix; f.len = P.len; f.n_channels = P.C;
+        FusedParams f = fused_params(P, D, d_mix);
         f.chunks = D.chunks + first; f.n_chunks = n;
-        f.g = P.g; f.K = P.K; f.n_tiles = P.n_tiles; f.S = P.S;
-        f.win = D.win; f.tw = D.tw; f.inv_env = D.env;
-        f.env_period = D.env_period; f.env_lo = P.env_lo; f.env_hi = P.env_hi;
-        f.fwd_scale = P.fwd_scale; f.inv_scale = P.inv_scale;
         f.mask = d_net_out; f.mask_chunk_stride = P.mask_per_chunk;
-        f.bin_tab = D.btab; f.bin_multi = P.bin_multi;
-        f.bin_ebeg = D.ebeg; f.bin_ent = D.ent; f.bin_inv = D.binv;
-        f.zero_dc = P.zero_dc; f.stem_stride = P.stem_stride;
-        f.dim_f = P.dim_f; f.zero_bins = P.zero_bins;
-        f.Y = D.Y + (int64_t)first * P.y_chunk_stride; f.y_chunk_stride = P.y_chunk_stride;
-        f.Tr = D.Tr + (int64_t)first * P.tr_chunk_stride; f.tr_chunk_stride = P.tr_chunk_stride;
+        f.Y = D.Y + (int64_t)first * P.y_chunk_stride;
+        f.Tr = D.Tr + (int64_t)first * P.tr_chunk_stride;
         cuda_check(launch_fused(P.arch, f, st), "fused spectral kernel launch");
         return;
     }

@@ -15,6 +15,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace stg {
@@ -147,6 +148,8 @@ void build_tfc(HostPlan& P, const stg_tfc_config& c, int64_t len);
 
 // The window and twiddle tables the fused kernel reads for n_fft (host copies).
 void fft_tables(int n_fft, std::vector<float>& win, std::vector<float2>& tw);
+// The per-pass twiddles of a radix plan of n_fft points (fft.cuh: twiddle_index).
+void fft_twiddles(int n_fft, const std::vector<int>& radices, std::vector<float2>& tw);
 
 // Optional timing of one run: events recorded on the run's stream around the kernels.
 struct RunTiming {
@@ -155,6 +158,10 @@ struct RunTiming {
     bool timed = false;
     int launches = 0;
 };
+
+// The chunks whose outputs reach output samples [b, e), as index ranges of the plan's chunk
+// list (one per chunk group, adjacent ones merged).
+std::vector<std::pair<int, int>> chunks_for(const HostPlan& P, int64_t b, int64_t e);
 
 // Run a separation on device buffers with the plan's device tables: the fused kernel over
 // chunk batches (progress and cancellation between batches), then the combine.
