@@ -26,7 +26,7 @@
 
 namespace stg {
 
-// ---- stubs for the device side (values as kernels.cu / split.cu / roformer.cu give them) ----
+// ---- stubs for the device side (values as kernels.cu and split.cu give them) ------------
 static int g_slots = 444;
 bool fused_supported(int n) { return n == 2048 || n == 4096 || n == 7680; }
 int fused_max_hop(int n) { return n == 2048 ? 512 : (n == 4096 || n == 7680) ? 1024 : 0; }
@@ -37,9 +37,7 @@ int split_max_hop(int n) { return split_supported(n) ? n / 2 : 0; }
 int fused_resident_ctas(int, int) { return g_slots; }
 int back_resident_ctas(int) { return g_slots; }
 int split_resident_ctas(int, bool) { return g_slots; }
-int roformer_resident_ctas(int) { return g_slots; }
 std::vector<int> fused_radices(int) { return {}; }
-std::vector<int> roformer_radices() { return {8, 8, 8, 4}; }
 size_t mono_scratch_doubles() { return 1026; }
 cudaError_t launch_fused(int, const FusedParams&, cudaStream_t) { return cudaSuccess; }
 cudaError_t launch_front(const SplitParams&, cudaStream_t) { return cudaSuccess; }
@@ -77,8 +75,6 @@ static void replay4(const CombineParams& p) {
     const int V = 4, SC = p.S * p.C;
     const FrameGeom& G = p.g;
     const int step = (int)p.step_out, span = p.K * G.hop, ov = G.n_fft - G.hop;
-    const int64_t yo = kY - p.Y, to = kTr - p.Tr;   // 0: the stub is called with the kY/kTr bases
-    (void)yo; (void)to;
     for (int64_t il = p.i_begin; il < p.i_end; il += V) {
         const int i0 = (int)il;
         const int nv = (int)std::min<int64_t>(V, p.i_end - il);
