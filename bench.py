@@ -196,6 +196,30 @@ def profiled_traffic(kernel, workload):
 
 
 # ---- CPU baselines -------------------------------------------------------------------------
+def cpu_info():
+    """The host's CPU model and core counts (the CPU figures' context)."""
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    logical = os.cpu_count() or 1
+    try:
+        import psutil
+        physical = psutil.cpu_count(logical=False) or logical
+    except Exception:
+        physical = logical
+    return {"cpu_model": model, "logical_cores": logical, "physical_cores": physical}
+
+
+def cpu_threads():
+    """Threads of the multi-threaded CPU figure: one per physical core, as the plan says."""
+    return cpu_info()["physical_cores"]
+
+
 def cpu_repeat(fn, min_s=10.0, max_reps=30):
     """Run fn() (returns (seconds, kind)) until about min_s seconds of CPU work are timed;
     returns the mean seconds per run, the kind, and the number of runs."""
@@ -207,7 +231,7 @@ def cpu_repeat(fn, min_s=10.0, max_reps=30):
 
 
 def cpu_run(w, length, mix, mask_host, n_sample, threads):
-    """Time the CPU path on a bounded sample of chunks; returns (seconds, kind)."""
+    """Time the CPU path on the first n_sample chunks of one track; returns (seconds, kind)."""
     import oracle
     kind = "reference" if oracle.use_reference(True) else "port"
     if w["arch"] == "roformer":
@@ -231,7 +255,62 @@ def cpu_run(w, length, mix, mask_host, n_sample, threads):
     return time.perf_counter() - t0, kind
 
 
+class CpuSample:
+    """The CPU baseline's workload, shared by the reference arm and the cpu_baseline leg: the
+    chunks of one whole track (every chunk the GPU step runs for one track), their masks, and
+    the audio-seconds they stand for."""
+
+    def __init__(self, w, threads):
+        self.w = w
+        self.threads = threads
+        self.length = w["seconds"] * SR
+        self.n_chunks = _n_chunks(w, self.length)
+        self.n_sample = self.n_chunks
+        self.mix = synth_audio(w["seed"], self.length)
+        self.mask = _host_mask(w, self.n_sample)
+        self.audio_s = w["seconds"] * self.n_sample / self.n_chunks
+        self.desc = f"all {self.n_chunks} chunks of one {w['seconds']} s track"
+
+    def run(self, threads=None, n_sample=None):
+        return cpu_run(self.w, self.length, self.mix, self.mask, n_sample or self.n_sample, threads or self.threads)
+
+
+def cpu_baseline_record(w, min_s=10.0, single=True):
+    """The cpu_baseline object: the shared sample on one thread per physical core, timed for
+    about min_s seconds, and (single) the same chunks' first few on one thread."""
+    smp = CpuSample(w, cpu_threads())
+    dt, kind, reps = cpu_repeat(smp.run, min_s=min_s)
+    rec = {"value": smp.audio_s / dt, "unit": "audio-s/s", "cores": smp.threads, "kind": kind,
+           "sample": f"{smp.desc}, timed {reps} times", **cpu_info()}
+    if single:
+        n1 = max(1, min(smp.n_sample, 2))
+        dt1, _, reps1 = cpu_repeat(lambda: smp.run(threads=1, n_sample=n1), min_s=min_s / 2)
+        rec["single_thread"] = {"value": w["seconds"] * n1 / smp.n_chunks / dt1, "unit": "audio-s/s", "cores": 1,
+                                "sample": f"the first {n1} of the {smp.n_chunks} chunks, timed {reps1} times"}
+    return rec
+
+
+def workload_config(w, name, world, split=False):
+    """The config object of a RoFormer / HTDemucs / TFC-TDF workload's bench line, computed on
+    the host, so that both arms print the same one."""
+    length = w["seconds"] * SR
+    n_chunks = _n_chunks(w, length)
+    if w["arch"] == "roformer":
+        frames = w["chunk"] // w["hop"] + 1
+    elif w["arch"] == "htdemucs":
+        frames = (w["segment"] + 1023) // 1024
+    else:
+        frames = w["dim_t"]
+    tracks = 1 if split else w.get("tracks", world)
+    return {"workload": name, "desc": w["desc"], "tracks_per_step": tracks, "chunks_per_track": n_chunks,
+            "frames_per_chunk": frames, "mask_bytes_per_track": 4 * n_chunks * _mask_floats_per_chunk(w),
+            "l2": "inputs larger than L2 (no flush needed)",
+            "parallelism": f"one track split by samples x{world}" if split else f"replicas x{world}"}
+
+
 def run_reference(args, w, rank):
+    """The reference's CPU implementation of the path (its compiled stft.h under the restated
+    loops) on this box's host cores: one step = the same sample the cpu_baseline leg times."""
     if rank != 0:
         return 0
     if w["arch"] in ("io", "vr"):
@@ -250,30 +329,23 @@ def run_reference(args, w, rank):
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["desc"]},
             "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": 1, "kind": kind,
-                             "sample": f"{sample_s:.0f} s of the {w['seconds']} s request per step"},
+                             "sample": f"{sample_s:.0f} s of the {w['seconds']} s request per step", **cpu_info()},
             "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return 0
-    length = w["seconds"] * SR
-    threads = os.cpu_count() or 1
-    mix = synth_audio(w["seed"], length)
-    n_chunks = _n_chunks(w, length)
-    n_sample = max(1, min(n_chunks, threads))
-    mask = _host_mask(w, n_sample)
+    smp = CpuSample(w, cpu_threads())
     times, kind = [], "port"
     for k in range(args.warmup + args.steps):
-        dt, kind = cpu_run(w, length, mix, mask, n_sample, threads)
+        dt, kind = smp.run()
         if k >= args.warmup:
             times.append(dt)
-    per_chunk_audio = w["seconds"] / n_chunks
-    value = n_sample * per_chunk_audio / statistics.mean(times)
+    value = smp.audio_s / statistics.mean(times)
     line = {"metric": "audio_seconds_per_second", "value": value, "unit": "audio-s/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * statistics.mean(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": w["desc"], "sample_chunks": n_sample,
-                       "chunks_per_track": n_chunks},
-            "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": threads, "kind": kind,
-                             "sample": f"{n_sample} of {n_chunks} chunks of one {w['seconds']} s track per step"},
+            "config": workload_config(w, args.workload, int(os.environ.get("WORLD_SIZE", "1")), args.split_track),
+            "cpu_baseline": {"value": value, "unit": "audio-s/s", "cores": smp.threads, "kind": kind,
+                             "sample": f"{smp.desc} per step", **cpu_info()},
             "e2e": {"value": value, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -526,10 +598,17 @@ def cpu_io(w, seconds):
 
 
 # ---- our arm -----------------------------------------------------------------------------
-def run_ours(args, w, rank, world, local_rank):
+def run_ours(args, w, rank, world, local_rank, name=None, steps=None, warmup=None, split=None, e2e_steps=None):
+    """One workload through the C ABI on this rank's GPU: the device-resident step (the
+    headline value), the kernel timing behind the roofline, and end to end from pinned host
+    memory. Returns rank 0's line (None elsewhere). Every rank takes the same collective steps."""
     import torch
     import torch.distributed as dist
 
+    name = name or args.workload
+    steps = steps or args.steps
+    warmup = max(3, warmup or args.warmup)
+    split = args.split_track if split is None else split
     pkg = load_pkg()
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -555,7 +634,7 @@ def run_ours(args, w, rank, world, local_rank):
     # round-robin share of a batch (the buffers are reused; the kernels do not look at values)
     n_tracks = w.get("tracks", world)
     mine = len(pkg.sharding.tracks_for_rank(n_tracks, rank, world))
-    split = args.split_track and "tracks" not in w
+    split = split and "tracks" not in w
     if split:   # one track, its output samples split across the ranks (strong scaling)
         n_tracks = 1
         part = pkg.sharding.sample_range_for_rank(length, rank, world)
@@ -568,7 +647,7 @@ def run_ours(args, w, rank, world, local_rank):
             plan.separate(d_mix, d_mask, d_out, stream=stream)
 
     def timed_region():
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step()
         torch.cuda.synchronize(dev)
         barrier()
@@ -576,13 +655,13 @@ def run_ours(args, w, rank, world, local_rank):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local_rank) as clk:
             e0.record(stream)
-            for _ in range(args.steps):
+            for _ in range(steps):
                 step()
             e1.record(stream)
             torch.cuda.synchronize(dev)
         barrier()
         torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / args.steps, clk
+        return e0.elapsed_time(e1) / steps, clk
 
     ms, clk = timed_region()
     remeasured = False
@@ -594,7 +673,7 @@ def run_ours(args, w, rank, world, local_rank):
     # Kernel-level timing on the launching stream (events recorded inside the engine).
     eng.set_profiling(True)
     prep, fused, comb = [], [], []
-    for _ in range(max(3, min(args.steps, 20))):
+    for _ in range(max(3, min(steps, 20))):
         plan.separate(d_mix, d_mask, d_out, stream=stream)
         a, b, c, n_launch = plan.last_timing_detail()
         prep.append(a)
@@ -605,11 +684,12 @@ def run_ours(args, w, rank, world, local_rank):
     fused_ms = statistics.mean(fused)
     combine_ms = statistics.mean(comb)
 
-    # End to end through the public host-buffer entry point (pinned host memory).
+    # End to end through the public host-buffer entry point (pinned host memory): one track per
+    # e2e step on every rank.
     h_mix = torch.from_numpy(mix_h).pin_memory()
     h_mask = d_mask.cpu().pin_memory()
     h_out = torch.empty(plan.out_shape, dtype=torch.float32).pin_memory()
-    e2e_steps = max(1, min(args.steps, 10))
+    e2e_steps = e2e_steps or max(1, min(steps, 10))
     plan.separate_host_ptr(h_mix.data_ptr(), h_mask.data_ptr(), h_out.data_ptr(), stream=stream.cuda_stream)
     torch.cuda.synchronize(dev)
     barrier()
@@ -639,18 +719,19 @@ def run_ours(args, w, rank, world, local_rank):
     peak, peak_kind = measured_peak()
     kname, fbytes = kernel_algorithmic_bytes(plan, w)
     achieved = fbytes / (fused_ms / 1e3) / 1e9
-    traffic = profiled_traffic(kname, args.workload)
+    traffic = profiled_traffic(kname, name)
+    h2d = 4 * (plan.n_channels * plan.n_samples + plan.mask_floats)
+    d2h = 4 * plan.out_floats
     line = None
     if rank == 0:
+        config = workload_config(w, name, world, split)
+        assert (config["chunks_per_track"], config["frames_per_chunk"]) == (plan.n_chunks, plan.n_frames), config
         line = {
             "metric": "audio_seconds_per_second", "value": value, "unit": "audio-s/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded sines + noise; N(0, sigma) masks standing in for the network)",
-            "config": {"workload": args.workload, "desc": w["desc"], "tracks_per_step": n_tracks,
-                       "chunks_per_track": plan.n_chunks, "frames_per_chunk": plan.n_frames,
-                       "mask_bytes_per_track": 4 * plan.mask_floats,
-                       "l2": "inputs larger than L2 (no flush needed)", "parallelism": (f"one track split by samples x{world}" if split else f"replicas x{world}")},
+            "config": config,
             "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "algorithmic_bytes_per_launch": fbytes,
@@ -659,15 +740,31 @@ def run_ours(args, w, rank, world, local_rank):
                      "gbs": path_algorithmic_bytes(plan, w) / (ms / 1e3) / 1e9},
             "clocks": dict(clk.summary(), remeasured=remeasured),
             "e2e": {"value": w["seconds"] * world / e2e_s, "unit": "audio-s/s",
-                    "h2d_bytes_per_step": 4 * (plan.n_channels * plan.n_samples + plan.mask_floats),
-                    "d2h_bytes_per_step": 4 * plan.out_floats,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "per_gpu_h2d_gbs": h2d / e2e_s / 1e9, "aggregate_h2d_gbs": world * h2d / e2e_s / 1e9,
+                    "tracks_per_e2e_step": world,
                     "copies_only": w["seconds"] * world / copy_s,
                     "copies_only_note": "the same host<->device copies alone, no kernels: the PCIe bound"},
-            "gpu_launches": n_launch * args.steps * mine,
+            "gpu_launches": n_launch * steps * mine,
         }
     plan.close()
     eng.close()
     return line
+
+
+BASELINE_WORKLOADS = ("cfg0", "cfg1", "cfg2", "cfg3", "cfg4")
+
+
+def workload_summary(line):
+    """The per-workload record of the default bench line's `workloads` object."""
+    keep = {"value": line["value"], "unit": line["unit"], "ms_per_step": line["ms_per_step"], "steps": line["steps"],
+            "kernel": line["roofline"]["kernel"], "frac": line["roofline"]["frac"],
+            "fused_ms": line["roofline"]["fused_ms"], "e2e": line["e2e"]["value"],
+            "e2e_copies_only": line["e2e"]["copies_only"], "clocks_sm_mhz": line["clocks"].get("sm_mhz"),
+            "config": line["config"]}
+    if "cpu_baseline" in line:
+        keep["cpu_baseline"] = line["cpu_baseline"]
+    return keep
 
 
 def main():
@@ -678,6 +775,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="only the headline workload (no `workloads` / `strong` records)")
     ap.add_argument("--split-track", action="store_true",
                     help="one track per step, its output samples split across the ranks (strong scaling)")
     args = ap.parse_args()
@@ -700,34 +799,51 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    extra = {}
     try:
         line = {"io": run_ours_io, "vr": run_ours_vr}.get(w["arch"], run_ours)(args, w, rank, world, local_rank)
+        headline = args.workload in BASELINE_WORKLOADS and not args.split_track and not args.no_extra
+        if headline:
+            # the other BASELINE configurations in the same run (fewer steps), and one track of
+            # cfg2 split by samples over this run's GPUs (strong scaling; at one GPU, one track)
+            if world == 1:
+                for name in BASELINE_WORKLOADS:
+                    if name == args.workload:
+                        continue
+                    wx = WORKLOADS[name]
+                    r = run_ours(args, wx, rank, world, local_rank, name=name, steps=min(args.steps, 10),
+                                 warmup=3, split=False, e2e_steps=3)
+                    if rank == 0 and not args.no_cpu_baseline:
+                        r["cpu_baseline"] = cpu_baseline_record(wx, min_s=5.0, single=False)
+                    extra[name] = r
+            strong = run_ours(args, WORKLOADS["cfg2"], rank, world, local_rank, name="cfg2",
+                              steps=min(args.steps, 10), warmup=3, split=True, e2e_steps=2)
+            extra["strong"] = strong
     finally:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
             dist.destroy_process_group()
-    if rank == 0 and w["arch"] in ("io", "vr"):
+    if rank != 0:
+        return 0
+    if w["arch"] in ("io", "vr"):
         if world == 1 and not args.no_cpu_baseline:
             dt, kind, reps = cpu_repeat(lambda: (cpu_io if w["arch"] == "io" else cpu_vr)(w, 5.0))
             line["cpu_baseline"] = {"value": 5.0 / dt, "unit": "audio-s/s", "cores": 1, "kind": kind,
                                     "sample": f"5 s of the {w['seconds']} s input (one thread, as the reference "
-                                              f"runs it), timed {reps} times"}
+                                              f"runs it), timed {reps} times", **cpu_info()}
         print(json.dumps(line))
         return 0
-    if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
-            length = w["seconds"] * SR
-            threads = os.cpu_count() or 1
-            n_chunks = _n_chunks(w, length)
-            n_sample = max(1, min(n_chunks, 2 * threads))
-            mix = synth_audio(w["seed"], length)
-            mask = _host_mask(w, n_sample)
-            dt, kind, reps = cpu_repeat(lambda: cpu_run(w, length, mix, mask, n_sample, threads))
-            line["cpu_baseline"] = {"value": n_sample * (w["seconds"] / n_chunks) / dt, "unit": "audio-s/s",
-                                    "cores": threads, "kind": kind,
-                                    "sample": f"{n_sample} of {n_chunks} chunks of one {w['seconds']} s track, "
-                                              f"timed {reps} times"}
-        print(json.dumps(line))
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_record(w)
+    if extra:
+        line["workloads"] = {n: workload_summary(r) for n, r in extra.items() if n != "strong"}
+        st = extra["strong"]
+        line["strong"] = {"workload": "cfg2", "value": st["value"], "unit": st["unit"], "n_gpus": world,
+                          "ms_per_step": st["ms_per_step"], "scaling": "strong",
+                          "parallelism": st["config"]["parallelism"],
+                          "note": "one 180 s BS-RoFormer track per step, its output samples split across the GPUs "
+                                  "(the chunks at a range's edge run on both neighbours; nothing is exchanged)"}
+    print(json.dumps(line))
     return 0
 
 
