@@ -80,9 +80,14 @@ void finish_plan(HostPlan& P, int env_frames) {
     const int k_min = std::max(1, (N - hop + hop - 1) / hop);
     P.K = std::max(16, k_min);
     int64_t best = INT64_MAX;
+    // HTDemucs separations: the front kernel's items are (chunk, tile), the back kernel's
+    // (chunk, tile, stem); a frame costs about the same in both, so their rounds add up
+    const bool ht = P.arch == ARCH_HTDEMUCS && !P.primitive;
+    const int64_t front_slots = ht ? std::max(1, split_resident_ctas(N, true)) : 1;
     for (int K = std::max(16, k_min); K >= k_min; K--) {
         const int64_t items = (int64_t)P.chunks.size() * ((P.g.T + K - 1) / K);
-        const int64_t cost = (items + slots - 1) / slots * (K + 1);
+        const int64_t cost = ht ? ((items * P.S + slots - 1) / slots + (items + front_slots - 1) / front_slots) * (K + 1)
+                                : (items + slots - 1) / slots * (K + 1);
         if (cost < best) { best = cost; P.K = K; }
     }
     P.n_tiles = (P.g.T + P.K - 1) / P.K;

@@ -283,24 +283,26 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel
     if (env_on)
         for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
 
-    for (int item = blockIdx.x; item < p.n_tiles * p.n_chunks; item += gridDim.x) {
-        const int tile = item % p.n_tiles, ci = item / p.n_tiles;
+    // work items are (chunk, tile, stem), the stems of a tile adjacent: a stem's frames are a
+    // CTA's work, and the tile's other stems, on other SMs at about the same time, read the same
+    // Z rows from L2
+    const int n_items = p.n_tiles * p.n_chunks * p.S;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int s = item % p.S, ct = item / p.S;
+        const int tile = ct % p.n_tiles, ci = ct / p.n_tiles;
         const int t_begin = tile * p.K, t_end = min(G.T, t_begin + p.K);
         const bool last_tile = t_end == G.T;
-        for (int s = 0; s < p.S; s++) {
+        {
             float* Ys = p.Y + (int64_t)ci * p.y_chunk_stride + (int64_t)s * C * G.Lout;
             float* Trs = p.Tr + (int64_t)ci * p.tr_chunk_stride + ((int64_t)tile * p.S + s) * C * (N - hop);
             for (int t = t_begin; t < t_end; t++) {
                 const int q0 = G.first_pos + t * hop;
                 // BACK_ZMASK: the next frame's Z and mask rows (contiguous, 16-byte aligned) asked
                 // of L2 a frame ahead (cfg4's back kernel 1.41 -> 1.28 ms)
-                if (p.layout == BACK_ZMASK && tid == 0) {
-                    const int tn = t + 1 < t_end ? t + 1 : t_begin, sn = t + 1 < t_end ? s : s + 1;
-                    if (sn < p.S) {
-                        const unsigned bytes = (unsigned)p.n_bins * 16u;
-                        if (tn != t) prefetch_l2(p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)tn * p.n_bins, bytes);
-                        prefetch_l2(p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)sn * G.T + tn) * p.n_bins, bytes);
-                    }
+                if (p.layout == BACK_ZMASK && tid == 0 && t + 1 < t_end) {
+                    const unsigned bytes = (unsigned)p.n_bins * 16u;
+                    prefetch_l2(p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)(t + 1) * p.n_bins, bytes);
+                    prefetch_l2(p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)s * G.T + t + 1) * p.n_bins, bytes);
                 }
                 auto pack = [&](int f, float2 yl, float2 yr) {
                     if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
@@ -416,7 +418,7 @@ template <int N> cudaError_t front_t(const SplitParams& p, cudaStream_t st) {
 }
 template <int N> cudaError_t back_t(const SplitParams& p, cudaStream_t st) {
     const size_t smem = sizeof(float2) * ((size_t)padded_size(N) + N) + sizeof(float) * (size_t)(N / 2);
-    return launch_persistent(back_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks, st, p);
+    return launch_persistent(back_kernel<N>, FftCfg<N>::T, smem, (int64_t)p.n_tiles * p.n_chunks * p.S, st, p);
 }
 
 } // namespace
