@@ -7,7 +7,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libstems_gpu.so")
-SOURCES = ["kernels.cu", "split.cu", "plan.cu", "engine.cu", "noalloc.cu", "norm.cu", "convert.cu", "vr.cu", "gguf.cu"]
+SOURCES = ["kernels.cu", "pair.cu", "split.cu", "plan.cu", "engine.cu", "noalloc.cu", "norm.cu", "convert.cu", "vr.cu", "gguf.cu"]
 HEADERS = ["fft.cuh", "frame.cuh", "kernels.h", "plan.h", "engine.h"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared"]

@@ -736,6 +736,7 @@ static cudaError_t launch_fused_t(const FusedParams& p, cudaStream_t st) {
 
 cudaError_t launch_fused(int arch, const FusedParams& p, cudaStream_t st) {
     if (p.n_chunks <= 0 || p.n_tiles <= 0) return cudaSuccess;
+    if (fused_pair(arch, p.g.n_fft, p.g.hop)) return launch_fused_pair(p, st);
     switch (arch) {
         case ARCH_ROFORMER:
             if (p.g.n_fft == 2048) return launch_fused_t<ARCH_ROFORMER, 2048>(p, st);

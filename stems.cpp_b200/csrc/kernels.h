@@ -209,6 +209,13 @@ int fused_resident_ctas(int arch, int n_fft);
 // The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
 std::vector<int> fused_radices(int n_fft);
 bool fused_supported(int n_fft);
+// TFC-TDF at n_fft 7680 with an even hop runs on CTA pairs (pair.cu): whether it does, the
+// pair plan's radices (its twiddles follow the n_fft table: the 3840-point plan's, then
+// W_7680^k for k < 3840), the clusters resident at once, and the launch
+bool fused_pair(int arch, int n_fft, int hop);
+std::vector<int> fused_pair_radices(int n_fft);
+int fused_pair_slots();
+cudaError_t launch_fused_pair(const FusedParams& p, cudaStream_t st);
 bool split_supported(int n_fft);   // n_fft the front and back kernels take
 int back_resident_ctas(int n_fft); // CTAs of the back kernel resident at once (0 when unknown)
 int split_resident_ctas(int n_fft, bool front);   // the same for the front (generic) or back kernel

@@ -74,9 +74,11 @@ void finish_plan(HostPlan& P, int env_frames) {
     // sample within one tile boundary (K * hop >= n_fft - hop).
     // (HTDemucs separations run the back kernel over the chunks, the others the fused one)
     // (single-chunk primitives run the front and back kernels: the fewer resident of the two)
+    // (TFC-TDF at n_fft 7680 runs on CTA pairs: a work slot is a cluster)
     const int64_t slots = std::max(1, P.primitive ? std::min(split_resident_ctas(N, true), split_resident_ctas(N, false))
                                       : P.arch == ARCH_HTDEMUCS ? back_resident_ctas(N)
-                                                                : fused_resident_ctas(P.arch, N));
+                                      : fused_pair(P.arch, N, hop) ? fused_pair_slots()
+                                                                   : fused_resident_ctas(P.arch, N));
     const int k_min = std::max(1, (N - hop + hop - 1) / hop);
     P.K = std::max(16, k_min);
     int64_t best = INT64_MAX;
@@ -147,6 +149,17 @@ void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
     const std::vector<double> w = hann_periodic(n);
     win.assign(w.begin(), w.end());
     fft_twiddles(n, fused_radices(n), tw);
+    // the CTA-pair kernel's tables after them: its half-length plan, then W_n^k for k < n/2
+    const std::vector<int> pr = fused_pair_radices(n);
+    if (!pr.empty()) {
+        std::vector<float2> h;
+        fft_twiddles(n / 2, pr, h);
+        tw.insert(tw.end(), h.begin(), h.end());
+        for (int k = 0; k < n / 2; k++) {
+            const double th = -2.0 * M_PI * (double)k / (double)n;
+            tw.push_back(make_float2((float)std::cos(th), (float)std::sin(th)));
+        }
+    }
 }
 
 // The offsets of the random-shift passes: std::mt19937 seeded with `seed`, one draw of

@@ -29,6 +29,9 @@ namespace stg {
 // ---- stubs for the device side (values as kernels.cu and split.cu give them) ------------
 static int g_slots = 444;
 bool fused_supported(int n) { return n == 2048 || n == 4096 || n == 7680; }
+bool fused_pair(int, int, int) { return false; }
+std::vector<int> fused_pair_radices(int) { return {}; }
+int fused_pair_slots() { return g_slots; }
 int fused_max_hop(int n) { return n == 2048 ? 512 : (n == 4096 || n == 7680) ? 1024 : 0; }
 bool split_supported(int n) {
     return n == 320 || n == 512 || n == 640 || n == 960 || n == 1024 || n == 2048 || n == 4096 || n == 7680;

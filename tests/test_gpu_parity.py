@@ -141,6 +141,22 @@ def test_tfc_matches_oracle(case, pkg, engine, oracle_mod):
     check(got, want, name)
 
 
+@pytest.mark.parametrize("hop,stems", [(1023, 1), (768, 2)], ids=["odd_hop_one_cta", "even_hop_pair_two_stems"])
+def test_tfc_7680_hops(hop, stems, pkg, engine, oracle_mod):
+    """n_fft 7680 runs on CTA pairs split by sample parity when the hop is even and on one CTA
+    when it is odd; both against the oracle, the pair also with two stems."""
+    length = 61001
+    plan = engine.plan_tfc(length, n_fft=7680, hop=hop, dim_f=3072, dim_t=32, zero_bins=3, n_stems=stems,
+                           chunking="uvr_mdx", overlap=0.5, compensate=1.0, complement=True)
+    mix = synth_audio(35, length)
+    mask = synth_mask(36, plan.mask_floats, 1.0)
+    got = run_gpu(plan, mix, mask)
+    p = oracle_mod.tfc_params(n_stems=stems, n_fft=7680, hop=hop, dim_t=32, chunking=0, overlap=0.5,
+                              complement=1, threads=8)
+    assert plan.n_chunks == oracle_mod.tfc_n_chunks(p, length)
+    check(got, oracle_mod.tfc_separate(p, mix, mask), f"tfc hop {hop}")
+
+
 # ---- determinism and the host-buffer entry point ---------------------------------------
 def test_deterministic_and_host_entry(pkg, engine):
     sizes, freqs = pkg.bands.mel_bands()
