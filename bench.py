@@ -103,15 +103,17 @@ def make_plan(pkg, eng, w, length):
 def kernel_algorithmic_bytes(plan, w):
     """(the dominant kernel, the bytes it must move once per launch), 4-byte floats.
     RoFormer / TFC-TDF, the fused kernel: each chunk's audio window in, the masks in, each
-    chunk's separated output out. HTDemucs, the back kernel: each segment's spectra
-    (2048 bins x T frames x 2 channels, complex) in, the masks in, the segment outputs out."""
+    chunk's separated output out (TFC-TDF at n_fft 7680 with an even hop: the fused kernel on CTA
+    pairs). HTDemucs, the back kernel: each segment's spectra (2048 bins x T frames x 2
+    channels, complex) in, the masks in, the segment outputs out."""
     if w["arch"] == "htdemucs":
         lc = w["segment"]
         z = plan.n_chunks * plan.n_frames * 2048 * 4
         return "back_kernel", 4 * (z + plan.mask_floats + plan.n_chunks * plan.n_out_sources * plan.n_channels * lc)
     lc = w["chunk"] if w["arch"] == "roformer" else w["hop"] * (w["dim_t"] - 1)
     n_src = plan.n_out_sources
-    return "fused_kernel", 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats
+    pair = w["arch"] == "tfc" and w["n_fft"] == 7680 and w["hop"] % 2 == 0
+    return "fused_pair_kernel" if pair else "fused_kernel", 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats
                                 + plan.n_chunks * n_src * plan.n_channels * lc)
 
 
