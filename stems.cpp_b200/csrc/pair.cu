@@ -46,7 +46,8 @@ using PairFwdRest = typename Head<PairPlan>::tail;
 using PairInvInit = typename Init<PairPlan>::type;
 constexpr int kRL = Init<PairPlan>::last, kNSL = Init<PairPlan>::prod;
 constexpr int kA1 = (kH / 2 + 2) / 2;           // pairs a in [0, kA1) on CTA 0, [kA1, kH/2] on CTA 1
-constexpr int kPR = (kH / 2 + 1 - kA1 + kT - 1) / kT;   // pair rounds per thread (the larger share)
+constexpr int kPR = (kA1 + kT - 1) / kT;        // pair rounds per thread (CTA 0's share, the larger)
+static_assert(kA1 >= kH / 2 + 1 - kA1, "CTA 0 takes the larger share of the pairs");
 
 size_t pair_smem_bytes() {
     return sizeof(float2) * ((size_t)padded_size(kH) + 2 * (size_t)kH) + sizeof(float) * ((size_t)kH + kHop);

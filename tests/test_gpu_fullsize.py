@@ -65,6 +65,26 @@ def test_cfg2_bs_roformer_180s(pkg, engine, oracle_mod):
     _check(_gpu(plan, mix, mask), want, "cfg2")
 
 
+def test_cfg2_split_eight_ways_equals_whole(pkg, engine):
+    """bench.py's strong-scaling record at 8 GPUs, on one: cfg2's output samples split into 8
+    ranges (sharding.sample_range_for_rank), each written by stg_separate_part, give the same
+    bits as the whole track."""
+    import torch
+    sizes, freqs = pkg.bands.bs_bands()
+    n = 180 * SR
+    plan = engine.plan_roformer(n, sizes, freqs, chunk=352800, num_overlap=2, zero_dc=True)
+    d_mix = torch.from_numpy(synth_audio(3, n)).cuda()
+    d_mask = torch.from_numpy(synth_mask(4, plan.mask_floats, 0.5)).cuda()
+    whole = torch.empty(plan.out_shape, device="cuda")
+    plan.separate(d_mix, d_mask, whole)
+    split = torch.full(plan.out_shape, float("nan"), device="cuda")
+    for r in range(8):
+        b, e = pkg.sharding.sample_range_for_rank(n, r, 8)
+        plan.separate_part(d_mix, d_mask, split, b, e)
+    torch.cuda.synchronize()
+    assert torch.equal(split, whole)
+
+
 def test_cfg0_htdemucs_20s(engine, oracle_mod):
     n = 20 * SR
     plan = engine.plan_htdemucs(n, n_sources=4, segment=343980)
