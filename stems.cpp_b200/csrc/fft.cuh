@@ -33,6 +33,27 @@ template <bool INV> __device__ __forceinline__ float2 mul_mi(float2 a) {
     return INV ? make_float2(-a.y, a.x) : make_float2(a.y, -a.x);
 }
 
+// A complex value whose additions and subtractions run as one sm_100 f32x2 instruction
+// (add/sub.rn.f32x2: the real and imaginary parts in the two halves of a register pair, each
+// rounded as the scalar operation rounds it), which halves the issue slots the codelets spend
+// on them. Everything else (twiddle products, multiplications by -i) is the float2 code.
+struct PF2 : float2 {
+    PF2() = default;
+    __device__ __forceinline__ PF2(float2 v) : float2(v) {}
+};
+__device__ __forceinline__ PF2 cadd(PF2 a, PF2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ PF2 csub(PF2 a, PF2 b) {
+    float2 r;
+    asm("{.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\t"
+        "mov.b64 pb, {%4, %5};\n\t"
+        "sub.rn.f32x2 pd, pa, pb;\n\t"
+        "mov.b64 {%0, %1}, pd;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+template <bool INV> __device__ __forceinline__ PF2 mul_mi(PF2 a) { return mul_mi<INV>(static_cast<float2>(a)); }
+
 __host__ __device__ constexpr int pad_idx(int i) { return i + (i >> 4); }
 __host__ __device__ constexpr int padded_size(int n) { return n + (n >> 4) + 1; }
 
@@ -96,13 +117,15 @@ __device__ __forceinline__ float2 twc(float2 v) {
         return make_float2(fmaf(c, v.x, s * v.y), fmaf(c, v.y, -s * v.x));
     }
 }
+template <long M, long Nn, bool INV>
+__device__ __forceinline__ PF2 twc(PF2 v) { return twc<M, Nn, INV>(static_cast<float2>(v)); }
 
 // ---- radix-R codelets, in place on a register array ------------------------------------
 template <int R, bool INV> struct Dft;
 
 template <bool INV> struct Dft<2, INV> {
-    template <int S> __device__ __forceinline__ static void run(float2* a) {
-        const float2 t = a[0];
+    template <int S, class V> __device__ __forceinline__ static void run(V* a) {
+        const V t = a[0];
         a[0] = cadd(t, a[S]);
         a[S] = csub(t, a[S]);
     }
@@ -122,9 +145,9 @@ template <bool INV> struct Dft<3, INV> {
 };
 
 template <bool INV> struct Dft<4, INV> {
-    template <int S> __device__ __forceinline__ static void run(float2* a) {
-        const float2 t0 = cadd(a[0], a[2 * S]), t1 = csub(a[0], a[2 * S]);
-        const float2 t2 = cadd(a[S], a[3 * S]), t3 = mul_mi<INV>(csub(a[S], a[3 * S]));
+    template <int S, class V> __device__ __forceinline__ static void run(V* a) {
+        const V t0 = cadd(a[0], a[2 * S]), t1 = csub(a[0], a[2 * S]);
+        const V t2 = cadd(a[S], a[3 * S]), t3 = mul_mi<INV>(csub(a[S], a[3 * S]));
         a[0] = cadd(t0, t2);
         a[2 * S] = csub(t0, t2);
         a[S] = cadd(t1, t3);
@@ -155,7 +178,7 @@ template <bool INV> struct Dft<5, INV> {
 // output X[k*S] with k = k1 + R1*k2 (natural order).
 template <int R1, int R2, bool INV> struct DftCT {
     static constexpr int R = R1 * R2;
-    template <int S> __device__ __forceinline__ static void run(float2* a) {
+    template <int S, class V> __device__ __forceinline__ static void run(V* a) {
         // inner DFTs of length R1 over n1 (stride R2) for each n2
         inner<S, 0>(a);
         // twiddles W_R^{n2 k1}: element (n2, k1) sits at index R2*k1 + n2
@@ -163,7 +186,7 @@ template <int R1, int R2, bool INV> struct DftCT {
         // outer DFTs of length R2 over n2 (stride 1) for each k1: results land at
         // R2*k1 + k2, but natural order wants k1 + R1*k2 -> transpose the R1 x R2 block.
         outer<S, 0>(a);
-        float2 tmp[R];
+        V tmp[R];
 #pragma unroll
         for (int k1 = 0; k1 < R1; k1++)
 #pragma unroll
@@ -171,20 +194,20 @@ template <int R1, int R2, bool INV> struct DftCT {
 #pragma unroll
         for (int k = 0; k < R; k++) a[k * S] = tmp[k];
     }
-    template <int S, int N2> __device__ __forceinline__ static void inner(float2* a) {
+    template <int S, int N2, class V> __device__ __forceinline__ static void inner(V* a) {
         if constexpr (N2 < R2) {
             Dft<R1, INV>::template run<S * R2>(a + N2 * S);
             inner<S, N2 + 1>(a);
         }
     }
-    template <int S, int I> __device__ __forceinline__ static void twiddle(float2* a) {
+    template <int S, int I, class V> __device__ __forceinline__ static void twiddle(V* a) {
         if constexpr (I < R) {
             constexpr int k1 = I / R2, n2 = I % R2;
             a[I * S] = twc<(long)n2 * k1, R, INV>(a[I * S]);
             twiddle<S, I + 1>(a);
         }
     }
-    template <int S, int K1> __device__ __forceinline__ static void outer(float2* a) {
+    template <int S, int K1, class V> __device__ __forceinline__ static void outer(V* a) {
         if constexpr (K1 < R1) {
             Dft<R2, INV>::template run<S>(a + K1 * R2 * S);
             outer<S, K1 + 1>(a);
@@ -219,12 +242,14 @@ struct TwGlobal {
 // in-place pass needs; a pass that reads one buffer and writes another does not.
 // TW_EARLY: load the pass's twiddles with the points, ahead of the barrier (a kernel that has
 // the registers for them).
-template <int N, int R, int NS, int T, bool INV, bool MID_SYNC, bool TW_EARLY = false, class Tw, class Ld, class St>
+// V: the codelets' complex type (float2, or PF2 for packed additions).
+template <int N, int R, int NS, int T, bool INV, bool MID_SYNC, bool TW_EARLY = false, class V = float2, class Tw,
+          class Ld, class St>
 __device__ __forceinline__ void pass_io(const Tw& tw, int tid, Ld&& ld, St&& st) {
     constexpr int NB = N / R;
     constexpr int ROUNDS = (NB + T - 1) / T;
     constexpr bool EXACT = (NB % T) == 0;
-    float2 v[ROUNDS][R];
+    V v[ROUNDS][R];
     constexpr bool HOIST = TW_EARLY && NS > 1 && ROUNDS * (R - 1) <= 16;
     float2 wv[HOIST ? ROUNDS : 1][HOIST ? R : 1];
 #pragma unroll
@@ -280,9 +305,9 @@ template <int R, int NS> __device__ __forceinline__ int pad_store(int base, int 
 }
 
 // In-place pass on the padded shared-memory frame buf, ending with a barrier.
-template <int N, int R, int NS, int T, bool INV, bool TW_EARLY = false, class Tw>
+template <int N, int R, int NS, int T, bool INV, bool TW_EARLY = false, class V = float2, class Tw>
 __device__ __forceinline__ void stockham_pass(float2* buf, const Tw& tw, int tid) {
-    pass_io<N, R, NS, T, INV, true, TW_EARLY>(
+    pass_io<N, R, NS, T, INV, true, TW_EARLY, V>(
         tw, tid, [&](int j, int r) { return buf[pad_load<N, R>(j, r)]; },
         [&](int base, int r, float2 v) { buf[pad_store<R, NS>(base, r)] = v; });
     __syncthreads();
@@ -311,24 +336,24 @@ template <int R, int... Rest> struct Head<RadixList<R, Rest...>> {
 
 // In-place passes for the radices of a list, the first of them at stride NS; hook() runs
 // before the last of them.
-template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw, class Hook, int R, int... Rest>
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class V = float2, class Tw, class Hook, int R, int... Rest>
 __device__ __forceinline__ void passes_hook(float2* buf, const Tw& tw, int tid, Hook&& hook, RadixList<R, Rest...>) {
     if constexpr (sizeof...(Rest) == 0) {
         hook();
-        stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
+        stockham_pass<N, R, NS, T, INV, TW_EARLY, V>(buf, tw, tid);
     } else {
-        stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
-        passes_hook<N, T, INV, NS * R, TW_EARLY>(buf, tw, tid, hook, RadixList<Rest...>{});
+        stockham_pass<N, R, NS, T, INV, TW_EARLY, V>(buf, tw, tid);
+        passes_hook<N, T, INV, NS * R, TW_EARLY, V>(buf, tw, tid, hook, RadixList<Rest...>{});
     }
 }
 
 // In-place passes for the radices of a list, the first of them at stride NS.
-template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw>
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class V = float2, class Tw>
 __device__ __forceinline__ void passes(float2*, const Tw&, int, RadixList<>) {}
-template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class Tw, int R, int... Rest>
+template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class V = float2, class Tw, int R, int... Rest>
 __device__ __forceinline__ void passes(float2* buf, const Tw& tw, int tid, RadixList<R, Rest...>) {
-    stockham_pass<N, R, NS, T, INV, TW_EARLY>(buf, tw, tid);
-    passes<N, T, INV, NS * R, TW_EARLY>(buf, tw, tid, RadixList<Rest...>{});
+    stockham_pass<N, R, NS, T, INV, TW_EARLY, V>(buf, tw, tid);
+    passes<N, T, INV, NS * R, TW_EARLY, V>(buf, tw, tid, RadixList<Rest...>{});
 }
 
 // Transform the frame in buf (padded layout) in place: X[k] = sum_n x[n] W_N^{nk}, W = e^{-2 pi i/N}

@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     constexpr bool SWIN = FftCfg<N>::SMEM_WIN;
     // the RoFormer instance at n_fft 2048 has the registers to load each pass's twiddles early
     constexpr bool TW_EARLY = ARCH == ARCH_ROFORMER && N == 2048;
+    // and its codelets' complex additions in f32x2 instructions (fft.cuh: PF2)
+    using CV = std::conditional_t<ARCH == ARCH_ROFORMER && N == 2048, PF2, float2>;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
     float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             const int q0 = G.first_pos + t * hop;
             mask_row_to_l2(t + 1);
             // forward pass 1: windowed frame straight from the input ring
-            pass_io<N, R1, 1, T, false, false>(
+            pass_io<N, R1, 1, T, false, false, false, CV>(
                 tw, tid,
                 [&](int j, int r) {
                     const int n = j + r * (N / R1);
@@ -241,7 +243,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             // channels, apply the stand-in network, repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
             if constexpr (N == 2048) {
-                passes_hook<N, T, false, R1, TW_EARLY>(buf, tw, tid, [&] { mk.prefetch(p, ci, s, t, tid); }, FwdRest{});
+                passes_hook<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, [&] { mk.prefetch(p, ci, s, t, tid); }, FwdRest{});
             } else {
                 passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
                 mk.prefetch(p, ci, s, t, tid);
@@ -278,9 +280,9 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 }
             }
             __syncthreads();
-            passes<N, T, true, 1, TW_EARLY>(buf, tw, tid, InvInit{});
+            passes<N, T, true, 1, TW_EARLY, CV>(buf, tw, tid, InvInit{});
             // inverse last pass: window and overlap-add straight into the output ring
-            pass_io<N, RL, NSL, T, true, false>(
+            pass_io<N, RL, NSL, T, true, false, false, CV>(
                 tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                 [&](int base, int r, float2 v) {
                     const int n = base + r * NSL;

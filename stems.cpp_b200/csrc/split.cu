@@ -11,6 +11,8 @@
 // htdemucs_ispec), the c2r conventions (DC and Nyquist imaginary parts dropped, the HTDemucs
 // Nyquist bin zero), the inverse FFT, the window, and the overlap-add into the fused kernel's
 // Y / Tr scratch.
+#include <type_traits>
+
 #include <algorithm>
 
 #include "fft.cuh"
@@ -145,6 +147,10 @@ __device__ __forceinline__ void zmask_apply(const SplitParams& p, int ci, float4
     }
 }
 
+// The codelets' complex type: at n_fft 4096 (HTDemucs) their additions run in f32x2
+// instructions (fft.cuh: PF2)
+template <int N> using SplitCV = std::conditional_t<N == 4096, PF2, float2>;
+
 // The CTAs per SM the HTDemucs segment-spectra instance (FRONT_ZSPEC) aims its registers at
 // (two: at three, the 80-register cap spills and the separation is slower); 0 leaves the
 // other instances to the compiler's default, which an explicit 1 would raise by 30-70 registers.
@@ -192,7 +198,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (front_minb<N, L>())) front_kern
         __syncthreads();
         for (int t = t_begin; t < t_end; t++) {
             const int q0 = G.first_pos + t * hop;
-            pass_io<N, R1, 1, T, false, false>(
+            pass_io<N, R1, 1, T, false, false, false, SplitCV<N>>(
                 tw, tid,
                 [&](int j, int r) {
                     const int n = j + r * (N / R1);
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (front_minb<N, L>())) front_kern
                     }
                 }
             }
-            passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
+            passes<N, T, false, R1, false, SplitCV<N>>(buf, tw, tid, FwdRest{});
             // the thread's bins f = tid + i*T (the FRONT_ZSPEC instance unrolls over its slots)
             constexpr int BPT = L == FRONT_ZSPEC ? (N / 2 + T) / T : 1;
 #pragma unroll
@@ -345,8 +351,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel
                     }
                 }
                 __syncthreads();
-                passes<N, T, true, 1>(buf, tw, tid, InvInit{});
-                pass_io<N, RL, NSL, T, true, false>(
+                passes<N, T, true, 1, false, SplitCV<N>>(buf, tw, tid, InvInit{});
+                pass_io<N, RL, NSL, T, true, false, false, SplitCV<N>>(
                     tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                     [&](int base, int r, float2 v) {
                         const int n = base + r * NSL;
