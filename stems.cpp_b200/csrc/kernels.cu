@@ -540,6 +540,30 @@ __global__ void __launch_bounds__(256) combine_kernel4(const CombineParams p) {
             const int j0 = d.y_off + u0;
             const int q0 = j0 + G.out_offset - G.first_pos;
             const int tau0 = q0 / span, uu0 = q0 - tau0 * span;
+            // all four samples inside the chunk, none on a tile boundary's partial sums, and
+            // 16-byte aligned rows: the weights as one vector and each row's samples as two
+            // (the same sums in the same order as the per-sample loop below)
+            const bool no_tr = q0 >= 0 && (tau0 < 1 || uu0 >= ov) && uu0 + V <= span;
+            if (nv == V && u0 >= 0 && u0 + V <= olen && no_tr && ((d.w_off + u0) & 3) == 0 && (j0 & 1) == 0 &&
+                (G.Lout & 1) == 0) {
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(Wg + u0));
+                const float wv[V] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int s = 0; s < V; s++) wsum[s] += wv[s];
+#pragma unroll
+                for (int st = 0; st < SC / 2; st++) {
+                    const float4* y4 = reinterpret_cast<const float4*>(yg + 2 * ((int64_t)st * G.Lout + j0));
+                    const float4 a = __ldg(y4), b = __ldg(y4 + 1);
+                    const float2 v[V] = {make_float2(a.x, a.y), make_float2(a.z, a.w), make_float2(b.x, b.y),
+                                         make_float2(b.z, b.w)};
+#pragma unroll
+                    for (int s = 0; s < V; s++) {
+                        acc[s][2 * st] = fmaf(wv[s], v[s].x, acc[s][2 * st]);
+                        acc[s][2 * st + 1] = fmaf(wv[s], v[s].y, acc[s][2 * st + 1]);
+                    }
+                }
+                continue;
+            }
 #pragma unroll
             for (int s = 0; s < V; s++) {
                 const int u = u0 + s;
