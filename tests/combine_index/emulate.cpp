@@ -63,7 +63,7 @@ static float* const kMix = reinterpret_cast<float*>(0x300000000000ull);
 static float* const kOut = reinterpret_cast<float*>(0x400000000000ull);
 
 struct Report {
-    long violations = 0, oob_w = 0, oob_y = 0, oob_tr = 0, oob_mix = 0, launches = 0;
+    long violations = 0, oob_w = 0, oob_y = 0, oob_tr = 0, oob_mix = 0, launches = 0, vec = 0;
     std::string first;
     void bad(const std::string& what) {
         if (violations++ == 0) first = what;
@@ -108,6 +108,25 @@ static void replay4(const CombineParams& p) {
                 const int j0 = d.y_off + u0;
                 const int q0 = j0 + G.out_offset - G.first_pos;
                 const int tau0 = q0 / span, uu0 = q0 - tau0 * span;
+                // the vector path: when the kernel takes it, its four samples must be exactly the
+                // ones the per-sample loop would use (all inside the chunk, none with a Tr
+                // partial), and its 16-byte loads aligned and inside the weight table and Y
+                const bool no_tr = q0 >= 0 && (tau0 < 1 || uu0 >= ov) && uu0 + V <= span;
+                if (nv == V && u0 >= 0 && u0 + V <= olen && no_tr && ((d.w_off + u0) & 3) == 0 && (j0 & 1) == 0 &&
+                    (G.Lout & 1) == 0) {
+                    g_rep.vec++;
+                    for (int s = 0; s < V; s++) {
+                        const int tau = tau0, uu = uu0 + s;
+                        if (tau >= 1 && tau < p.n_tiles && uu < ov) g_rep.bad("vector path over a Tr partial");
+                    }
+                    const int64_t w0 = d.w_off + (int64_t)u0;
+                    if ((w0 & 3) || !in(w0, g_sz.W) || !in(w0 + 3, g_sz.W)) g_rep.bad("vector weight load outside the table");
+                    for (int st = 0; st < SC / 2; st++) {
+                        const int64_t y0 = ybase + 2 * ((int64_t)st * G.Lout + j0);
+                        if ((y0 & 3) || !in(y0, g_sz.Y) || !in(y0 + 7, g_sz.Y)) g_rep.bad("vector Y load misaligned or outside");
+                    }
+                    continue;
+                }
                 for (int s = 0; s < V; s++) {
                     const int u = u0 + s;
                     int tau, uu;
@@ -257,9 +276,9 @@ static void run(const std::string& name, const std::function<void(HostPlan&)>& b
         } catch (const std::exception& x) {
             g_rep.bad(std::string("launch_plan: ") + x.what());
         }
-        std::printf("%s slots=%d K=%d chunks=%zu launches=%ld violations=%ld oob_unguarded_W=%ld Y=%ld Tr=%ld mix=%ld first=%s\n",
+        std::printf("%s slots=%d K=%d chunks=%zu launches=%ld violations=%ld oob_unguarded_W=%ld Y=%ld Tr=%ld mix=%ld vec=%ld first=%s\n",
                     name.c_str(), slots, H.K, H.chunks.size(), g_rep.launches, g_rep.violations, g_rep.oob_w,
-                    g_rep.oob_y, g_rep.oob_tr, g_rep.oob_mix, g_rep.first.empty() ? "-" : g_rep.first.c_str());
+                    g_rep.oob_y, g_rep.oob_tr, g_rep.oob_mix, g_rep.vec, g_rep.first.empty() ? "-" : g_rep.first.c_str());
     }
 }
 

@@ -9,6 +9,9 @@ resident-CTA counts (so four tile sizes). It asserts:
   * every clamp of combine_kernel4 (uc, tc, uc2, the complement's min(s, nv - 1)) leaves its
     index unchanged wherever the loaded value is used, and every such address is inside its
     buffer (weight tables, Y, Tr, mix, out).
+Where combine_kernel4 reads a chunk's four samples as 16-byte vectors (all four inside the chunk,
+none on a tile boundary's partial sums, aligned rows), it checks that those are the samples the
+per-sample loop would use and that the vector loads are aligned and inside their buffers.
 It also reports where an unguarded load would have left its buffer: the weight table read at
 u = -3..-1 when a chunk's first output sample falls inside a thread's four samples (chunk steps
 that are not a multiple of 4), and the complement's mix read past the track's end (lengths that
@@ -82,3 +85,9 @@ def test_unguarded_candidates(replay):
                 assert (int(kv["oob_unguarded_W"]), int(kv["Y"]), int(kv["Tr"]), int(kv["mix"])) == (0, 0, 0, 0), n
         for kv in runs:   # Y and Tr reads never leave their buffers, guarded or not
             assert int(kv["Y"]) == 0 and int(kv["Tr"]) == 0, n
+
+
+def test_vector_path_taken_on_the_benchmark_plans(replay):
+    for name in ("cfg1_mel_roformer_60s", "cfg2_bs_roformer_180s", "cfg3_tfc_180s"):
+        for kv in replay[name]:
+            assert int(kv["vec"]) > 0, name
