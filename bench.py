@@ -118,7 +118,7 @@ def kernel_algorithmic_bytes(plan, w):
 
 
 def path_algorithmic_bytes(plan, w):
-    """The survey's per-track figure: audio in per chunk window + masks in + stems out once."""
+    """The path's algorithmic bytes per track: audio in per chunk window + masks in + stems out once."""
     lc = {"roformer": w.get("chunk"), "htdemucs": w.get("segment")}.get(w["arch"]) or w["hop"] * (w["dim_t"] - 1)
     return 4 * (plan.n_chunks * plan.n_channels * lc + plan.mask_floats + plan.out_floats)
 
