@@ -493,13 +493,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
 // combine_kernel (so the same floats), with the group and chunk bookkeeping (the divisions
 // by the chunk step, the chunk table loads, the tile of each sample) done once per four
 // samples; the tile of the next sample is the previous one's advanced by one. Every load
-// address is clamped into its table or buffer, so that a load the compiler issues ahead of
-// its sample's guard (the four samples are unrolled) still reads memory the plan owns: the
-// first unguarded version faulted on RoFormer plans, whose first chunk starts before sample 0.
+// address is clamped into its table or buffer; the host replay of this arithmetic
+// (tests/combine_index) shows each clamp leaves its index unchanged wherever the loaded value
+// is used. 128 threads a block (measured against 256 and 512: cfg1 45 -> 43 us).
 constexpr int kCombineV = 4;
+constexpr int kCombineThreads = 128;
 
 template <int SC>
-__global__ void __launch_bounds__(256) combine_kernel4(const CombineParams p) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel4(const CombineParams p) {
     constexpr int V = kCombineV;
     const int64_t il = p.i_begin + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * V;
     if (il >= p.i_end) return;
@@ -839,10 +840,10 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
     const int threads = 256;
     if (p.C == 2 && p.S <= 2) {   // one or two stereo stems: four samples per thread (from
         // three stems up, its registers cost more occupancy than the shared bookkeeping saves)
-        const int64_t per = (int64_t)threads * kCombineV;
+        const int64_t per = (int64_t)kCombineThreads * kCombineV;
         const unsigned b4 = (unsigned)((p.i_end - p.i_begin + per - 1) / per);
-        if (p.S == 1) combine_kernel4<2><<<b4, threads, 0, st>>>(p);
-        else combine_kernel4<4><<<b4, threads, 0, st>>>(p);
+        if (p.S == 1) combine_kernel4<2><<<b4, kCombineThreads, 0, st>>>(p);
+        else combine_kernel4<4><<<b4, kCombineThreads, 0, st>>>(p);
         return cudaGetLastError();
     }
     const unsigned blocks = (unsigned)((p.i_end - p.i_begin + threads - 1) / threads);
