@@ -39,7 +39,8 @@ template <int ARCH, int N, int T> struct MaskOp {
     static constexpr int BPT = (NBIN + T - 1) / T;
     float4 a[BPT];
     float4 b[BPT];   // RoFormer: the second band holding the bin
-    float inv[BPT];  // RoFormer: 1 / bands holding the bin (negative: more than two)
+    float inv[BPT];  // RoFormer: 1 / bands holding the bin, times scale
+    float scale = 1.0f;   // RoFormer: folded into inv (the split's factor)
 
     const int2* btab;   // RoFormer: the bin table's copy in shared memory
 
@@ -61,7 +62,7 @@ template <int ARCH, int N, int T> struct MaskOp {
                     const int2 e = btab[f];
                     const unsigned s0 = (unsigned)e.x >> 22, s1 = (unsigned)e.y >> 22;
                     const int u0 = (e.x & 0x3fffff) + t * (int)s0, u1 = (e.y & 0x3fffff) + t * (int)s1;
-                    inv[i] = s1 ? 0.5f : (s0 ? 1.0f : 0.0f);
+                    inv[i] = p.bin_multi ? __ldg(p.bin_inv + f) * scale : (s1 ? 0.5f * scale : (s0 ? scale : 0.0f));
                     if (p.n_channels == 2) {
                         a[i] = ld_stream4(ms + 4 * u0);
                         if (s1) b[i] = ld_stream4(ms + 4 * u1);
@@ -98,10 +99,8 @@ template <int ARCH, int N, int T> struct MaskOp {
             // masks of every band holding f, averaged (src/roformer.cpp:270-276), times z
             float2 al = make_float2(a[i].x + b[i].x, a[i].y + b[i].y);
             float2 ar = make_float2(a[i].z + b[i].z, a[i].w + b[i].w);
-            float w = inv[i];
             if (p.bin_multi) {   // bins in more than two bands: the rest straight from memory
                 const int e0 = __ldg(p.bin_ebeg + f), e1 = __ldg(p.bin_ebeg + f + 1);
-                w = __ldg(p.bin_inv + f);
                 const float* ms = p.mask + (int64_t)ci * p.mask_chunk_stride + (int64_t)s * p.stem_stride;
                 for (int k = e0 + 2; k < e1; k++) {
                     const int2 en = __ldg(p.bin_ent + k);
@@ -110,8 +109,8 @@ template <int ARCH, int N, int T> struct MaskOp {
                     if (p.n_channels == 2) { ar.x += ld_stream(q + 2); ar.y += ld_stream(q + 3); }
                 }
             }
-            yl = cmul(zl, cscale(al, w));
-            yr = cmul(zr, cscale(ar, w));
+            yl = cmul(zl, al);   // the band average's weight came with zl, zr
+            yr = cmul(zr, ar);
             if (p.zero_dc && f == 0) { yl = make_float2(0.f, 0.f); yr = yl; }      // :278
         } else {
             // y = in * mask per CaC plane; zero below zero_bins and from dim_f up (the loads
@@ -163,6 +162,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
         for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
 
     MaskOp<ARCH, N, T> mk;
+    mk.scale = half_fwd;
     InPrefetch<T, FftCfg<N>::HOPMAX> nx;
     if constexpr (ARCH == ARCH_ROFORMER) {
         for (int i = tid; i < N / 2 + 1; i += T) btab_s[i] = __ldg(p.bin_tab + i);
@@ -270,8 +270,9 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     const int fm = f == 0 ? 0 : N - f;
                     const float2 X = BATCH ? Xa[BATCH ? i : 0] : buf[pad_idx(f)];
                     const float2 Xm = BATCH ? Xb[BATCH ? i : 0] : buf[pad_idx(fm)];
-                    const float2 zl = make_float2(half_fwd * (X.x + Xm.x), half_fwd * (X.y - Xm.y));
-                    const float2 zr = make_float2(half_fwd * (X.y + Xm.y), -half_fwd * (X.x - Xm.x));
+                    const float sc = ARCH == ARCH_ROFORMER ? mk.inv[i] : half_fwd;   // RoFormer: with the band weight
+                    const float2 zl = make_float2(sc * (X.x + Xm.x), sc * (X.y - Xm.y));
+                    const float2 zr = make_float2(sc * (X.y + Xm.y), -sc * (X.x - Xm.x));
                     float2 yl, yr;
                     mk.apply(p, ci, s, t, f, i, zl, zr, yl, yr);
                     if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
