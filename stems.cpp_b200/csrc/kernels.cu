@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
         for (int i = tid; i < hop; i += T) env_s[i] = __ldg(p.env_period + i);
 
     MaskOp<ARCH, N, T> mk;
-    mk.scale = half_fwd;
+    // RoFormer: the inverse transform's scale goes in with the mask too (the transform is
+    // linear), so the overlap-add multiplies by the window alone
+    mk.scale = ARCH == ARCH_ROFORMER ? half_fwd * p.inv_scale : half_fwd;
     InPrefetch<T, FftCfg<N>::HOPMAX> nx;
     if constexpr (ARCH == ARCH_ROFORMER) {
         for (int i = tid; i < N / 2 + 1; i += T) btab_s[i] = __ldg(p.bin_tab + i);
@@ -287,7 +289,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                 [&](int base, int r, float2 v) {
                     const int n = base + r * NSL;
-                    const float w = (SWIN ? win[n] : __ldg(win + n)) * p.inv_scale;
+                    const float w = ARCH == ARCH_ROFORMER ? (SWIN ? win[n] : __ldg(win + n))
+                                                          : (SWIN ? win[n] : __ldg(win + n)) * p.inv_scale;
                     float2& o = out_ring[ring_slot<N>(q0 + n)];
                     o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
                 });
