@@ -334,19 +334,6 @@ template <int R, int... Rest> struct Head<RadixList<R, Rest...>> {
     using tail = RadixList<Rest...>;
 };
 
-// In-place passes for the radices of a list, the first of them at stride NS; hook() runs
-// before the last of them.
-template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class V = float2, class Tw, class Hook, int R, int... Rest>
-__device__ __forceinline__ void passes_hook(float2* buf, const Tw& tw, int tid, Hook&& hook, RadixList<R, Rest...>) {
-    if constexpr (sizeof...(Rest) == 0) {
-        hook();
-        stockham_pass<N, R, NS, T, INV, TW_EARLY, V>(buf, tw, tid);
-    } else {
-        stockham_pass<N, R, NS, T, INV, TW_EARLY, V>(buf, tw, tid);
-        passes_hook<N, T, INV, NS * R, TW_EARLY, V>(buf, tw, tid, hook, RadixList<Rest...>{});
-    }
-}
-
 // In-place passes for the radices of a list, the first of them at stride NS.
 template <int N, int T, bool INV, int NS, bool TW_EARLY = false, class V = float2, class Tw>
 __device__ __forceinline__ void passes(float2*, const Tw&, int, RadixList<>) {}

@@ -240,12 +240,13 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     }
                 }
             }
-            // all of this frame's mask loads in flight at once (at n_fft 2048 before the last
-            // forward pass, whose work hides their latency), then the spectral op: split the
-            // channels, apply the stand-in network, repack as one Hermitian pair
+            // all of this frame's mask loads in flight at once (at n_fft 2048 before the second
+            // and third forward passes, whose work hides their latency), then the spectral op:
+            // split the channels, apply the stand-in network, repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
             if constexpr (N == 2048) {
-                passes_hook<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, [&] { mk.prefetch(p, ci, s, t, tid); }, FwdRest{});
+                mk.prefetch(p, ci, s, t, tid);
+                passes<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, FwdRest{});
             } else {
                 passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
                 mk.prefetch(p, ci, s, t, tid);
