@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     constexpr bool TW_EARLY = ARCH == ARCH_ROFORMER && N == 2048;
     // and its codelets' complex additions in f32x2 instructions (fft.cuh: PF2)
     using CV = std::conditional_t<ARCH == ARCH_ROFORMER && N == 2048, PF2, float2>;
+    // and its loads of the next frame's new samples issued after the frame's mask loads
+    constexpr bool LATE_NX = ARCH == ARCH_ROFORMER && N == 2048;
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
     float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     const int u = tid + k * T;
                     if (u < hop) in_ring[ring_slot<N>(q0 + N + u)] = nx.v[k];
                 }
-                if (t + 2 < t_end) {
+                if (!LATE_NX && t + 2 < t_end) {   // (RoFormer at n_fft 2048: after the mask loads, below)
 #pragma unroll
                     for (int k = 0; k < nx.K; k++) {
                         const int u = tid + k * T;
@@ -241,11 +243,19 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 }
             }
             // all of this frame's mask loads in flight at once (at n_fft 2048 before the second
-            // and third forward passes, whose work hides their latency), then the spectral op:
-            // split the channels, apply the stand-in network, repack as one Hermitian pair
+            // and third forward passes, whose work hides their latency, and before the next
+            // frame's new samples), then the spectral op: split the channels, apply the
+            // stand-in network, repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
             if constexpr (N == 2048) {
                 mk.prefetch(p, ci, s, t, tid);
+                if (LATE_NX && t + 2 < t_end) {
+#pragma unroll
+                    for (int k = 0; k < nx.K; k++) {
+                        const int u = tid + k * T;
+                        if (u < hop) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + hop + N + u);
+                    }
+                }
                 passes<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, FwdRest{});
             } else {
                 passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
