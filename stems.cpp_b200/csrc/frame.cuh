@@ -18,6 +18,10 @@ template <> struct FftCfg<2048> {
     static constexpr bool MASK_L2 = false;  // TFC-TDF: the next frame's mask row prefetched into L2
     static constexpr bool SMEM_WIN = false;   // the window copied into shared memory
     using Plan = RadixList<8, 16, 16>;
+    // The RoFormer kernel's forward transform runs the radices in the opposite order, so its
+    // last pass and the inverse's first are both radix 8 on the same butterflies (kernels.cu:
+    // the mirror step); its twiddles follow Plan's in the table.
+    using FwdPlan = RadixList<16, 16, 8>;
 };
 template <> struct FftCfg<4096> {
     static constexpr int T = 256, MINB = 2, HOPMAX = 1024;

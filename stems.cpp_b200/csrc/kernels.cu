@@ -32,11 +32,26 @@
 namespace stg {
 
 // ---- the stand-in network ---------------------------------------------------------------
-// Each thread owns bins f = tid + i*T (i < BPT); prefetch() issues every mask load of its bins
-// for one (stem, frame) before apply() consumes them, so the loads overlap one another.
+// Each thread owns the bins bin(tid, i) (i < BPT); prefetch() issues every mask load of its
+// bins for one (stem, frame) before apply() consumes them, so the loads overlap one another.
 template <int ARCH, int N, int T> struct MaskOp {
     static constexpr int NBIN = N / 2 + 1;
     static constexpr int BPT = (NBIN + T - 1) / T;
+    // RoFormer at n_fft 2048 (the mirror step of fused_kernel): thread tid holds the radix-8
+    // butterflies g0 = tid and g1 = 256 - tid (128 for thread 0), i.e. the points g + 256r, so its
+    // bins are g0 + 256i (i < 4), g1 + 256(i - 4) (i < 8) and, for thread 0, the Nyquist bin.
+    // Elsewhere bins are dealt round-robin: tid + i*T.
+    static constexpr bool MIR = ARCH == ARCH_ROFORMER && N == 2048;
+    static_assert(!MIR || (T == 128 && BPT == 9), "the mirror step deals 2048 points to 128 threads");
+    __device__ __forceinline__ static int bin(int tid, int i) {
+        if constexpr (MIR) {
+            if (i < 4) return tid + 256 * i;
+            if (i < 8) return (tid ? 256 - tid : 128) + 256 * (i - 4);
+            return tid ? NBIN : N / 2;
+        } else {
+            return tid + i * T;
+        }
+    }
     float4 a[BPT];
     float4 b[BPT];   // RoFormer: the second band holding the bin
     float inv[BPT];  // RoFormer: 1 / bands holding the bin, times scale
@@ -53,7 +68,7 @@ template <int ARCH, int N, int T> struct MaskOp {
             const float* ms = m + (int64_t)s * p.stem_stride;
 #pragma unroll
             for (int i = 0; i < BPT; i++) {
-                const int f = tid + i * T;
+                const int f = bin(tid, i);
                 a[i] = b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 inv[i] = 0.0f;
                 if (f < NBIN) {
@@ -92,7 +107,7 @@ template <int ARCH, int N, int T> struct MaskOp {
         }
     }
 
-    // Bin f = tid + i*T of the two channels' spectra zl, zr -> the spectra the iSTFT consumes.
+    // Bin f = bin(tid, i) of the two channels' spectra zl, zr -> the spectra the iSTFT consumes.
     __device__ __forceinline__ void apply(const FusedParams& p, int ci, int s, int t, int f, int i,
                                           float2 zl, float2 zr, float2& yl, float2& yr) const {
         if constexpr (ARCH == ARCH_ROFORMER) {
@@ -121,6 +136,10 @@ template <int ARCH, int N, int T> struct MaskOp {
     }
 };
 
+// The forward transform's radix plan: FftCfg::FwdPlan for the mirror step, else the common one.
+template <class Cfg, bool OWN> struct FwdPlanOf { using type = typename Cfg::Plan; };
+template <class Cfg> struct FwdPlanOf<Cfg, true> { using type = typename Cfg::FwdPlan; };
+
 template <int ARCH, int N>
 __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(const FusedParams p) {
     constexpr int T = FftCfg<N>::T;
@@ -136,6 +155,17 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     using CV = std::conditional_t<ARCH == ARCH_ROFORMER && N == 2048, PF2, float2>;
     // and its loads of the next frame's new samples issued after the frame's mask loads
     constexpr bool LATE_NX = ARCH == ARCH_ROFORMER && N == 2048;
+    // and the mirror step: the forward plan ends in radix 8 (FftCfg::FwdPlan), and each thread's
+    // two last butterflies g and 256 - g hold the bins k and N - k that the split pairs, which are
+    // also the points of the inverse's first radix-8 butterflies. So the forward's last pass, the
+    // spectral op and the inverse's first pass run in registers between one load and one store
+    // of the frame.
+    constexpr bool MIR = MaskOp<ARCH, N, T>::MIR;
+    using FwdPlan = typename FwdPlanOf<FftCfg<N>, MIR>::type;
+    constexpr int R1F = Head<FwdPlan>::first;
+    using FwdMid = typename Init<typename Head<FwdPlan>::tail>::type;   // [MIR] passes before the step
+    using InvMid = typename Head<InvInit>::tail;                         // [MIR] passes after it
+    static_assert(!MIR || (Init<FwdPlan>::last == 8 && Head<Plan>::first == 8), "mirror step: radix 8 both sides");
     extern __shared__ float4 smem_raw[];
     float2* buf = reinterpret_cast<float2*>(smem_raw);    // padded frame
     float2* in_ring = buf + padded_size(N);               // input samples (L, R) by position mod N
@@ -144,6 +174,7 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
     int2* btab_s = reinterpret_cast<int2*>(win_s + (SWIN ? N : 0));   // [RoFormer] bin table copy
     float* env_s = reinterpret_cast<float*>(btab_s + (ARCH == ARCH_ROFORMER ? N / 2 + 2 : 0));   // envelope period
     const TwGlobal tw{p.tw};
+    const TwGlobal twf{p.tw + (MIR ? N : 0)};   // the forward plan's table (plan.cu: fft_tables)
     const float* win = SWIN ? win_s : p.win;
 
     const int tid = threadIdx.x;
@@ -217,15 +248,15 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
             const int q0 = G.first_pos + t * hop;
             mask_row_to_l2(t + 1);
             // forward pass 1: windowed frame straight from the input ring
-            pass_io<N, R1, 1, T, false, false, false, CV>(
-                tw, tid,
+            pass_io<N, R1F, 1, T, false, false, false, CV>(
+                twf, tid,
                 [&](int j, int r) {
-                    const int n = j + r * (N / R1);
+                    const int n = j + r * (N / R1F);
                     const float2 x = in_ring[ring_slot<N>(q0 + n)];
                     const float w = SWIN ? win[n] : __ldg(win + n);
                     return make_float2(x.x * w, x.y * w);
                 },
-                [&](int base, int r, float2 v) { buf[pad_store<R1, 1>(base, r)] = v; });
+                [&](int base, int r, float2 v) { buf[pad_store<R1F, 1>(base, r)] = v; });
             __syncthreads();
             // the next frame's new samples replace the ones this frame was the last to use
             if (t + 1 < t_end) {
@@ -256,45 +287,118 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                         if (u < hop) nx.v[k] = tile_sample(p, cd, chL, chR, lxf, lin, q0 + hop + N + u);
                     }
                 }
-                passes<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, FwdRest{});
+                if constexpr (MIR) passes<N, T, false, R1F, TW_EARLY, CV>(buf, twf, tid, FwdMid{});
+                else passes<N, T, false, R1, TW_EARLY, CV>(buf, tw, tid, FwdRest{});
             } else {
                 passes<N, T, false, R1>(buf, tw, tid, FwdRest{});
                 mk.prefetch(p, ci, s, t, tid);
             }
-            // at n_fft 2048 and 7680 every bin's two spectrum points are loaded before the
-            // arithmetic and the stores (the stores could alias later loads as far as the compiler
-            // knows); at 4096 the 128-register cap leaves no room for it
+            // (n_fft 2048: the frame's loads batched ahead of its stores here and in the flush)
             constexpr bool BATCH = N == 2048;
-            float2 Xa[BATCH ? BPT : 1], Xb[BATCH ? BPT : 1];
-            if constexpr (BATCH) {
+            if constexpr (MIR) {
+                // the mirror step. Thread tid takes the forward's last radix-8 butterflies g0 = tid
+                // and g1 = 256 - tid (thread 0: 0 and 128), whose outputs are the bins g + 256r
+                // (fft.cuh: a last pass writes j + r*N/R). Bin k's mirror N - k is then
+                // g1 + 256(7 - r) for k = g0 + 256r and the other way round, except on thread 0,
+                // whose two butterflies each hold their own mirrors (and bins 0 and N/2).
+                constexpr int NB = N / 8;
+                const int g0 = tid, g1 = tid ? NB - tid : NB / 2;
+                const bool t0 = tid == 0;
+                CV z[16];
+                float2 w[16];
 #pragma unroll
+                for (int r = 1; r < 8; r++) {
+                    w[r] = twf(twiddle_index<NB>(r, g0));
+                    w[8 + r] = twf(twiddle_index<NB>(r, g1));
+                }
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    z[r] = buf[pad_load<N, 8>(g0, r)];
+                    z[8 + r] = buf[pad_load<N, 8>(g1, r)];
+                }
+                __syncthreads();   // every point read before the inverse's first pass writes
+#pragma unroll
+                for (int r = 1; r < 8; r++) {
+                    z[r] = cmul(z[r], w[r]);
+                    z[8 + r] = cmul(z[8 + r], w[8 + r]);
+                }
+                Dft<8, false>::template run<1>(z);
+                Dft<8, false>::template run<1>(z + 8);
+                // slot i: bin bin(tid, i) at z[i] (i < 4), z[i + 4] (i < 8) or z[4] (thread 0's
+                // Nyquist bin); gx the inverse's input at the bin, gm at its mirror
+                float2 gx[BPT], gm[BPT];
+                gx[8] = make_float2(0.f, 0.f);   // (read, and not used, by the other threads)
+#pragma unroll
+                for (int i = 0; i < BPT; i++) {
+                    const int f = MaskOp<ARCH, N, T>::bin(tid, i);
+                    if (i < 8 || t0) {
+                        const float2 X = i < 4 ? z[i] : (i < 8 ? z[i + 4] : z[4]);
+                        const float2 Xm = i < 4 ? (t0 ? z[(8 - i) & 7] : z[15 - i])
+                                                : (i < 8 ? (t0 ? z[19 - i] : z[11 - i]) : z[4]);
+                        const float sc = mk.inv[i];   // with the band weight
+                        const float2 zl = make_float2(sc * (X.x + Xm.x), sc * (X.y - Xm.y));
+                        const float2 zr = make_float2(sc * (X.y + Xm.y), -sc * (X.x - Xm.x));
+                        float2 yl, yr;
+                        mk.apply(p, ci, s, t, f, i, zl, zr, yl, yr);
+                        if ((i == 0 && t0) || i == 8) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
+                        gx[i] = make_float2(yl.x - yr.y, yl.y + yr.x);
+                        gm[i] = make_float2(yl.x + yr.y, yr.x - yl.y);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    z[i] = gx[i];
+                    z[i + 8] = gx[i + 4];
+                    z[12 + i] = t0 ? gm[7 - i] : gm[3 - i];
+                }
+                z[4] = t0 ? gx[8] : gm[7];
+#pragma unroll
+                for (int m = 1; m < 4; m++) z[4 + m] = t0 ? gm[4 - m] : gm[7 - m];
+                // the inverse's first pass (radix 8 at stride 1): butterfly g writes 8g + r
+                Dft<8, true>::template run<1>(z);
+                Dft<8, true>::template run<1>(z + 8);
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    buf[pad_store<8, 1>(8 * g0, r)] = z[r];
+                    buf[pad_store<8, 1>(8 * g1, r)] = z[8 + r];
+                }
+                __syncthreads();
+                passes<N, T, true, 8, TW_EARLY, CV>(buf, tw, tid, InvMid{});
+            } else {
+                // at n_fft 2048 every bin's two spectrum points are loaded before the arithmetic
+                // and the stores (the stores could alias later loads as far as the compiler
+                // knows); at 4096 the 128-register cap leaves no room for it
+                float2 Xa[BATCH ? BPT : 1], Xb[BATCH ? BPT : 1];
+                if constexpr (BATCH) {
+    #pragma unroll
+                    for (int i = 0; i < BPT; i++) {
+                        const int f = tid + i * T;
+                        if (f <= N / 2) {
+                            Xa[i] = buf[pad_idx(f)];
+                            Xb[i] = buf[pad_idx(f == 0 ? 0 : N - f)];
+                        }
+                    }
+                }
+    #pragma unroll
                 for (int i = 0; i < BPT; i++) {
                     const int f = tid + i * T;
                     if (f <= N / 2) {
-                        Xa[i] = buf[pad_idx(f)];
-                        Xb[i] = buf[pad_idx(f == 0 ? 0 : N - f)];
+                        const int fm = f == 0 ? 0 : N - f;
+                        const float2 X = BATCH ? Xa[BATCH ? i : 0] : buf[pad_idx(f)];
+                        const float2 Xm = BATCH ? Xb[BATCH ? i : 0] : buf[pad_idx(fm)];
+                        const float sc = ARCH == ARCH_ROFORMER ? mk.inv[i] : half_fwd;   // RoFormer: with the band weight
+                        const float2 zl = make_float2(sc * (X.x + Xm.x), sc * (X.y - Xm.y));
+                        const float2 zr = make_float2(sc * (X.y + Xm.y), -sc * (X.x - Xm.x));
+                        float2 yl, yr;
+                        mk.apply(p, ci, s, t, f, i, zl, zr, yl, yr);
+                        if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
+                        buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
+                        if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
                     }
                 }
+                __syncthreads();
+                passes<N, T, true, 1, TW_EARLY, CV>(buf, tw, tid, InvInit{});
             }
-#pragma unroll
-            for (int i = 0; i < BPT; i++) {
-                const int f = tid + i * T;
-                if (f <= N / 2) {
-                    const int fm = f == 0 ? 0 : N - f;
-                    const float2 X = BATCH ? Xa[BATCH ? i : 0] : buf[pad_idx(f)];
-                    const float2 Xm = BATCH ? Xb[BATCH ? i : 0] : buf[pad_idx(fm)];
-                    const float sc = ARCH == ARCH_ROFORMER ? mk.inv[i] : half_fwd;   // RoFormer: with the band weight
-                    const float2 zl = make_float2(sc * (X.x + Xm.x), sc * (X.y - Xm.y));
-                    const float2 zr = make_float2(sc * (X.y + Xm.y), -sc * (X.x - Xm.x));
-                    float2 yl, yr;
-                    mk.apply(p, ci, s, t, f, i, zl, zr, yl, yr);
-                    if (f == 0 || f == N / 2) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
-                    buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
-                    if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
-                }
-            }
-            __syncthreads();
-            passes<N, T, true, 1, TW_EARLY, CV>(buf, tw, tid, InvInit{});
             // inverse last pass: window and overlap-add straight into the output ring
             pass_io<N, RL, NSL, T, true, false, false, CV>(
                 tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
@@ -715,6 +819,11 @@ std::vector<int> fused_radices(int n) {
         case 7680: return radix_vec(FftCfg<7680>::Plan{});
         default: return {};
     }
+}
+
+std::vector<int> fused_fwd_radices(int n) {
+    if (n == 2048) return radix_vec(FftCfg<2048>::FwdPlan{});
+    return {};
 }
 
 template <int ARCH, int N> static int resident_t() {

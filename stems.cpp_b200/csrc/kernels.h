@@ -208,6 +208,9 @@ int fused_max_hop(int n_fft);      // the largest hop the fused kernel takes at 
 int fused_resident_ctas(int arch, int n_fft);
 // The radices of the FFT plan at this n_fft, in pass order (fft.cuh: twiddle_index).
 std::vector<int> fused_radices(int n_fft);
+// The radices of the forward transform's own plan where it differs from fused_radices (empty
+// otherwise); its twiddles follow that plan's n_fft entries in the table.
+std::vector<int> fused_fwd_radices(int n_fft);
 bool fused_supported(int n_fft);
 // TFC-TDF at n_fft 7680 with an even hop runs on CTA pairs (pair.cu): whether it does, the
 // pair plan's radices (its twiddles follow the n_fft table: the 3840-point plan's, then

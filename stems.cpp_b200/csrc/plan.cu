@@ -149,6 +149,13 @@ void fft_tables(int n, std::vector<float>& win, std::vector<float2>& tw) {
     const std::vector<double> w = hann_periodic(n);
     win.assign(w.begin(), w.end());
     fft_twiddles(n, fused_radices(n), tw);
+    // a forward plan of its own (n_fft 2048): its table right after
+    const std::vector<int> fr = fused_fwd_radices(n);
+    if (!fr.empty()) {
+        std::vector<float2> f;
+        fft_twiddles(n, fr, f);
+        tw.insert(tw.end(), f.begin(), f.end());
+    }
     // the CTA-pair kernel's tables after them: its half-length plan, then W_n^k for k < n/2
     const std::vector<int> pr = fused_pair_radices(n);
     if (!pr.empty()) {

@@ -41,6 +41,7 @@ int fused_resident_ctas(int, int) { return g_slots; }
 int back_resident_ctas(int) { return g_slots; }
 int split_resident_ctas(int, bool) { return g_slots; }
 std::vector<int> fused_radices(int) { return {}; }
+std::vector<int> fused_fwd_radices(int) { return {}; }
 size_t mono_scratch_doubles() { return 1026; }
 cudaError_t launch_fused(int, const FusedParams&, cudaStream_t) { return cudaSuccess; }
 cudaError_t launch_front(const SplitParams&, cudaStream_t) { return cudaSuccess; }
