@@ -399,8 +399,13 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                 __syncthreads();
                 passes<N, T, true, 1, TW_EARLY, CV>(buf, tw, tid, InvInit{});
             }
-            // inverse last pass: window and overlap-add straight into the output ring
-            pass_io<N, RL, NSL, T, true, false, false, CV>(
+            // inverse last pass: window and overlap-add straight into the output ring. Butterfly
+            // j < NSL writes the positions j + r*NSL, so a thread adds into the ring positions
+            // q0 + n with n = tid mod T, the very ones it flushes below: the pass's barrier goes
+            // between its loads and its stores (the next frame's first pass rewrites buf), and the
+            // flush needs none before it.
+            static_assert(NSL % T == 0, "the overlap-add and the flush give a thread the same positions");
+            pass_io<N, RL, NSL, T, true, true, false, CV>(
                 tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                 [&](int base, int r, float2 v) {
                     const int n = base + r * NSL;
@@ -409,7 +414,6 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     float2& o = out_ring[ring_slot<N>(q0 + n)];
                     o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
                 });
-            __syncthreads();
             // flush what no later frame of this tile touches
             const bool last = t == t_end - 1;
             const int ny = (last && last_tile) ? N : hop;
