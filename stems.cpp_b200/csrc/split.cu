@@ -352,7 +352,11 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel
                 }
                 __syncthreads();
                 passes<N, T, true, 1, false, SplitCV<N>>(buf, tw, tid, InvInit{});
-                pass_io<N, RL, NSL, T, true, false, false, SplitCV<N>>(
+                // the overlap-add: a thread adds into the ring positions q0 + n, n = tid mod T, the
+                // ones it flushes below, so the barrier goes between the pass's loads and stores
+                // (the next frame's packing rewrites buf) and the flush needs none
+                static_assert(NSL % T == 0, "the overlap-add and the flush give a thread the same positions");
+                pass_io<N, RL, NSL, T, true, true, false, SplitCV<N>>(
                     tw, tid, [&](int j, int r) { return buf[pad_load<N, RL>(j, r)]; },
                     [&](int base, int r, float2 v) {
                         const int n = base + r * NSL;
@@ -360,7 +364,6 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel
                         float2& o = out_ring[ring_slot<N>(q0 + n)];
                         o = make_float2(fmaf(v.x, w, o.x), fmaf(v.y, w, o.y));
                     });
-                __syncthreads();
                 const bool last = t == t_end - 1;
                 const int ny = (last && last_tile) ? N : hop;
                 const int nflush = last ? N : hop;
