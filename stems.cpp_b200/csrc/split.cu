@@ -316,42 +316,110 @@ __global__ void __launch_bounds__(FftCfg<N>::T, (N == 4096 ? 3 : 0)) back_kernel
                     buf[pad_idx(f)] = make_float2(yl.x - yr.y, yl.y + yr.x);
                     if (f != 0 && f != N / 2) buf[pad_idx(fm)] = make_float2(yl.x + yr.y, yr.x - yl.y);
                 };
-                if (p.layout == BACK_ZMASK) {
-                    // the bins' Z and mask vectors in groups of GRP slots, every load of a group in
-                    // flight before the first is used
-                    constexpr int BPT = (N / 2 + T) / T, GRP = 5;
-                    const float4* zs = p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins;
-                    const float* ms = p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)s * G.T + t) * p.n_bins;
+                bool paired = false;
+                if constexpr (N == 4096) {
+                    if (p.layout == BACK_ZMASK) {
+                        // lane pairs: threads 2m and 2m + 1 take the inverse's first butterflies
+                        // j = m and 256 - m (thread 1: 128). Butterfly j reads the points j + 256r,
+                        // and bin k's mirror point N - k lies in the partner's butterfly, so each
+                        // thread repacks its own bins j + 256r (r < 8; thread 0 also N/2) into both
+                        // points, keeps the one at its own position and hands the partner the other
+                        // (one shuffle per point); the first pass then runs in registers.
+                        // (groups of three bins' loads in flight: five spilled 48 bytes at the
+                        // 128-register cap and ran 11 % slower)
+                        paired = true;
+                        constexpr int NB = N / 16, GRP = 3;
+                        static_assert(NB == T && Head<InvInit>::first == 16, "one first-pass butterfly per thread");
+                        const int m2 = tid >> 1;
+                        const int j = (tid & 1) ? (m2 ? NB - m2 : NB / 2) : m2;
+                        const float4* zs = p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins;
+                        const float* ms = p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)s * G.T + t) * p.n_bins;
+                        SplitCV<N> v[16];
+                        float2 gm[9];
+                        float2 g8 = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int g0 = 0; g0 < BPT; g0 += GRP) {
-                        float4 z[GRP], m[GRP];
+                        for (int g0 = 0; g0 < 9; g0 += GRP) {
+                            float4 z[GRP], m[GRP];
 #pragma unroll
-                        for (int k = 0; k < GRP; k++) {
-                            const int f = tid + (g0 + k) * T;
-                            z[k] = m[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (g0 + k < BPT && f < p.n_bins) {
-                                z[k] = zs[f];
-                                m[k] = ld_stream4(ms + 4 * f);
+                            for (int k = 0; k < GRP; k++) {
+                                const int r = g0 + k, f = j + NB * r;
+                                z[k] = m[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (r < 9 && (r < 8 || tid == 0) && f < p.n_bins) {
+                                    z[k] = zs[f];
+                                    m[k] = ld_stream4(ms + 4 * f);
+                                }
+                            }
+#pragma unroll
+                            for (int k = 0; k < GRP; k++) {
+                                const int r = g0 + k;
+                                if (r >= 9) continue;
+                                float2 yl, yr;
+                                zmask_apply(p, ci, z[k], m[k], yl, yr);
+                                if (r == 8 || (r == 0 && tid == 0)) { yl.y = 0.0f; yr.y = 0.0f; }   // c2r ignores these
+                                const float2 gx = make_float2(yl.x - yr.y, yl.y + yr.x);
+                                if (r < 8) {
+                                    v[r] = gx;
+                                    gm[r] = make_float2(yl.x + yr.y, yr.x - yl.y);
+                                } else {
+                                    g8 = gx;
+                                }
                             }
                         }
 #pragma unroll
-                        for (int k = 0; k < GRP; k++) {
-                            const int f = tid + (g0 + k) * T;
-                            if (g0 + k >= BPT || f > N / 2) continue;
+                        for (int r = 8; r < 16; r++) {
+                            const float2 q = gm[15 - r];
+                            const float2 t2 = make_float2(__shfl_xor_sync(0xffffffffu, q.x, 1),
+                                                          __shfl_xor_sync(0xffffffffu, q.y, 1));
+                            // the butterflies 0 and 128 hold their own mirrors
+                            const float2 own = tid == 1 ? gm[15 - r] : (r == 8 ? g8 : gm[(16 - r) & 7]);
+                            v[r] = tid > 1 ? t2 : own;
+                        }
+                        Dft<16, true>::template run<1>(v);
+                        // (the previous frame's overlap-add barrier ordered its reads of buf first)
+#pragma unroll
+                        for (int r = 0; r < 16; r++) buf[pad_store<16, 1>(16 * j, r)] = v[r];
+                        __syncthreads();
+                        passes<N, T, true, 16, false, SplitCV<N>>(buf, tw, tid, typename Head<InvInit>::tail{});
+                    }
+                }
+                if (!paired) {
+                    if (p.layout == BACK_ZMASK) {
+                        // the bins' Z and mask vectors in groups of GRP slots, every load of a group in
+                        // flight before the first is used
+                        constexpr int BPT = (N / 2 + T) / T, GRP = 5;
+                        const float4* zs = p.zspec + (int64_t)ci * p.z_chunk_stride + (int64_t)t * p.n_bins;
+                        const float* ms = p.net + (int64_t)ci * p.net_chunk_stride + 4 * ((int64_t)s * G.T + t) * p.n_bins;
+#pragma unroll
+                        for (int g0 = 0; g0 < BPT; g0 += GRP) {
+                            float4 z[GRP], m[GRP];
+#pragma unroll
+                            for (int k = 0; k < GRP; k++) {
+                                const int f = tid + (g0 + k) * T;
+                                z[k] = m[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (g0 + k < BPT && f < p.n_bins) {
+                                    z[k] = zs[f];
+                                    m[k] = ld_stream4(ms + 4 * f);
+                                }
+                            }
+#pragma unroll
+                            for (int k = 0; k < GRP; k++) {
+                                const int f = tid + (g0 + k) * T;
+                                if (g0 + k >= BPT || f > N / 2) continue;
+                                float2 yl, yr;
+                                zmask_apply(p, ci, z[k], m[k], yl, yr);
+                                pack(f, yl, yr);
+                            }
+                        }
+                    } else {
+                        for (int f = tid; f <= N / 2; f += T) {
                             float2 yl, yr;
-                            zmask_apply(p, ci, z[k], m[k], yl, yr);
+                            back_load(p, ci, s, t, f, yl, yr);
                             pack(f, yl, yr);
                         }
                     }
-                } else {
-                    for (int f = tid; f <= N / 2; f += T) {
-                        float2 yl, yr;
-                        back_load(p, ci, s, t, f, yl, yr);
-                        pack(f, yl, yr);
-                    }
+                    __syncthreads();
+                    passes<N, T, true, 1, false, SplitCV<N>>(buf, tw, tid, InvInit{});
                 }
-                __syncthreads();
-                passes<N, T, true, 1, false, SplitCV<N>>(buf, tw, tid, InvInit{});
                 // the overlap-add: a thread adds into the ring positions q0 + n, n = tid mod T, the
                 // ones it flushes below, so the barrier goes between the pass's loads and stores
                 // (the next frame's packing rewrites buf) and the flush needs none
