@@ -457,8 +457,8 @@ STG_API stg_status stg_htdemucs_ispec(stg_engine* engine, const float* d_spec, i
  * (device buffers, same layouts as stg_separate with a RoFormer plan); everything else the
  * separation needs, its tables and the fused kernel's scratch, lives in one static device
  * array of 64 MiB that every GPU loading this library reserves until the process exits.
- * With 352800-sample chunks of a stereo one-stem model that is 16 chunks: a 20 s track at
- * num_overlap 4, 56 s at num_overlap 2. Longer inputs are rejected with
+ * With 352800-sample chunks of a stereo one-stem model that is 17 chunks (61.8 MiB): a track of
+ * up to 22 s at num_overlap 4, 60 s at num_overlap 2. Longer inputs are rejected with
  * STG_INVALID_ARGUMENT and a message saying how much they need.
  *
  * Contexts: the call runs in `device`'s primary context, the one the CUDA runtime (and an
