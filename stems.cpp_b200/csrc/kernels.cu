@@ -285,10 +285,10 @@ __global__ void __launch_bounds__(FftCfg<N>::T, FftCfg<N>::MINB) fused_kernel(co
                     }
                 }
             }
-            // all of this frame's mask loads in flight at once (at n_fft 2048 before the second
-            // and third forward passes, whose work hides their latency, and before the next
-            // frame's new samples), then the spectral op: split the channels, apply the
-            // stand-in network, repack as one Hermitian pair
+            // all of this frame's mask loads in flight at once (at n_fft 2048 before the rest of
+            // the forward transform, whose work hides their latency, and before the next frame's
+            // new samples), then the spectral op: split the channels, apply the stand-in network,
+            // repack as one Hermitian pair
             constexpr int BPT = MaskOp<ARCH, N, T>::BPT;
             if constexpr (N == 2048) {
                 mk.prefetch(p, ci, s, t, tid);
